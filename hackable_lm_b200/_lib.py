@@ -1,0 +1,110 @@
+"""ctypes binding of libhlm_b200.so (the C ABI declared in include/hlm_b200.h).
+
+The shared library is built in-tree by ``python -m hackable_lm_b200.build``.
+There is no fallback: if the library is missing or fails to load, every
+operator raises, so a GPU run can never silently take a different path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libhlm_b200.so"
+
+HLM_OK = 0
+HLM_F32, HLM_BF16, HLM_F16 = 0, 1, 2
+
+_P = c_void_p
+_I64 = c_int64
+_I64P = POINTER(c_int64)
+
+# name -> (argtypes, restype); mirrors include/hlm_b200.h one to one.
+SIGNATURES: dict[str, tuple[list, object]] = {
+    "hlm_version": ([], c_int),
+    "hlm_strerror": ([c_int], c_char_p),
+    "hlm_device_error_get": ([POINTER(c_int), _P], c_int),
+    "hlm_device_error_clear": ([_P], c_int),
+    "hlm_swiglu_fwd": ([_P, _P, _I64, _I64, c_int, _P], c_int),
+    "hlm_swiglu_bwd": ([_P, _P, _P, _I64, _I64, c_int, _P], c_int),
+    "hlm_residual_rms_norm_fwd": ([_P, _P, _P, _P, _P, _I64, _I64, c_float, c_int, _P], c_int),
+    "hlm_residual_rms_norm_bwd": (
+        [_P, _P, _P, _P, _P, _P, _P, c_size_t, _I64, _I64, c_float, c_int, _P], c_int),
+    "hlm_rms_norm_bwd_workspace_bytes": ([_I64, _I64], c_size_t),
+    "hlm_qk_norm_rope_fwd": (
+        [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64, c_int,
+         c_float, c_int, _P], c_int),
+    "hlm_qk_norm_rope_bwd": (
+        [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64,
+         c_int, c_float, c_int, _P], c_int),
+    "hlm_qkv_rope_fwd": (
+        [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, c_int,
+         c_float, _P], c_int),
+    "hlm_qkv_rope_bwd": (
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _I64, _I64, _I64, _I64,
+         _I64, _I64, _I64, _I64, c_int, c_float, _P], c_int),
+    "hlm_qkv_rope_bwd_workspace_bytes": ([_I64, _I64, _I64, _I64, _I64, _I64], c_size_t),
+    "hlm_lm_head_ce": (
+        [_P, _P, _P, _P, _P, _P, _P, c_size_t, _I64, _I64, _I64, _I64, _I64, _P], c_int),
+    "hlm_lm_head_ce_workspace_bytes": ([_I64, _I64, _I64, _I64], c_size_t),
+    "hlm_scale_by_device_scalar": ([_P, _P, _I64, c_int, _P], c_int),
+    "hlm_gemm_bf16": (
+        [_P, _P, _P, _I64, _I64, _I64, c_int, c_int, _I64, _I64, _I64, c_int, c_int, _P], c_int),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class HlmError(RuntimeError):
+    """A libhlm_b200 entry point returned a non-zero status."""
+
+
+def load() -> ctypes.CDLL:
+    """Load libhlm_b200.so once and attach the C signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = Path(os.environ.get("HLM_B200_LIB", str(LIB_PATH)))
+        if not path.exists():
+            raise HlmError(
+                f"hackable_lm_b200 CUDA library not found at {path}; "
+                "build it with `python -m hackable_lm_b200.build`"
+            )
+        # Load after torch so the library binds to the process's CUDA runtime.
+        import torch  # noqa: F401
+
+        lib = ctypes.CDLL(str(path), mode=ctypes.RTLD_LOCAL)
+        for name, (argtypes, restype) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+        _lib = lib
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != HLM_OK:
+        msg = load().hlm_strerror(rc)
+        raise HlmError(f"{what} failed: {msg.decode() if msg else rc} (code {rc})")
+
+
+def device_error(stream: int = 0) -> int:
+    """Synchronously read the device error word (0 = no kernel reported a problem)."""
+    out = c_int(0)
+    check(load().hlm_device_error_get(ctypes.byref(out), c_void_p(stream)), "hlm_device_error_get")
+    return out.value
+
+
+def clear_device_error(stream: int = 0) -> None:
+    check(load().hlm_device_error_clear(c_void_p(stream)), "hlm_device_error_clear")
+
+
+def int64_array(values) -> ctypes.Array:
+    arr = (c_int64 * len(values))(*[int(v) for v in values])
+    return arr

@@ -1,0 +1,655 @@
+// Memory-bound operators of the hackable-lm hot path: SwiGLU forward/backward,
+// residual-add + RMSNorm forward/backward (optional weight), and the scalar
+// rescale used by the fused LM-head backward.
+//
+// Design: 128-bit vectorised coalesced loads (ld.global.nc for streamed
+// inputs), fp32 math in registers, one warp per row for the row reductions
+// (shuffle-xor trees, no shared memory), grids sized to the SM count.  A
+// scalar path covers shapes whose rows are not 16-byte multiples (the
+// reference accepts any even width, e.g. the [17,130] fp32 GPU test).
+#include "hlm_common.cuh"
+
+namespace hlm {
+
+template <typename T>
+struct DTypeOf;
+template <>
+struct DTypeOf<float> {
+  static constexpr int value = HLM_F32;
+};
+template <>
+struct DTypeOf<__nv_bfloat16> {
+  static constexpr int value = HLM_BF16;
+};
+template <>
+struct DTypeOf<__half> {
+  static constexpr int value = HLM_F16;
+};
+
+#define HLM_DISPATCH_DTYPE(dtype, T, ...)          \
+  switch (dtype) {                                 \
+    case HLM_F32: {                                \
+      using T = float;                             \
+      __VA_ARGS__;                                 \
+      break;                                       \
+    }                                              \
+    case HLM_BF16: {                               \
+      using T = __nv_bfloat16;                     \
+      __VA_ARGS__;                                 \
+      break;                                       \
+    }                                              \
+    case HLM_F16: {                                \
+      using T = __half;                            \
+      __VA_ARGS__;                                 \
+      break;                                       \
+    }                                              \
+    default:                                       \
+      return HLM_ERR_UNSUPPORTED;                  \
+  }
+
+static inline int elementwise_grid(int64_t work_items, int threads) {
+  const int64_t max_blocks = static_cast<int64_t>(num_sms_of_current_device()) * (2048 / threads);
+  int64_t blocks = (work_items + threads - 1) / threads;
+  if (blocks > max_blocks) blocks = max_blocks;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU (kernels.py:343-386)
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_fwd_vec_kernel(const T* __restrict__ gate_up,
+                                                            T* __restrict__ out, int64_t rows,
+                                                            int64_t hidden) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int64_t hv = hidden / VEC;
+  const int64_t total = rows * hv;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += 2 * stride) {
+    uint4 g_raw[2], u_raw[2];
+    int64_t off_in[2], off_out[2];
+    bool ok[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t vv = v + u * stride;
+      ok[u] = vv < total;
+      const int64_t row = ok[u] ? vv / hv : 0;
+      const int64_t cv = ok[u] ? vv - row * hv : 0;
+      off_in[u] = row * 2 * hidden + cv * VEC;
+      off_out[u] = row * hidden + cv * VEC;
+      if (ok[u]) {
+        g_raw[u] = ld_global_nc_v4(gate_up + off_in[u]);
+        u_raw[u] = ld_global_nc_v4(gate_up + off_in[u] + hidden);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (!ok[u]) continue;
+      Vec16<T> gv, uv, ov;
+      gv.raw = g_raw[u];
+      uv.raw = u_raw[u];
+      float g[VEC], up[VEC], o[VEC];
+      gv.to_float(g);
+      uv.to_float(up);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) o[i] = g[i] * sigmoidf_(g[i]) * up[i];
+      ov.from_float(o);
+      st_global_v4(out + off_out[u], ov.raw);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_fwd_scalar_kernel(const T* __restrict__ gate_up,
+                                                               T* __restrict__ out, int64_t rows,
+                                                               int64_t hidden) {
+  const int64_t total = rows * hidden;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / hidden, col = i - row * hidden;
+    const float g = to_f32(gate_up[row * 2 * hidden + col]);
+    const float u = to_f32(gate_up[row * 2 * hidden + hidden + col]);
+    out[i] = from_f32<T>(g * sigmoidf_(g) * u);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_bwd_vec_kernel(const T* __restrict__ gate_up,
+                                                            const T* __restrict__ grad_out,
+                                                            T* __restrict__ grad_gate_up,
+                                                            int64_t rows, int64_t hidden) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int64_t hv = hidden / VEC;
+  const int64_t total = rows * hv;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += stride) {
+    const int64_t row = v / hv;
+    const int64_t cv = v - row * hv;
+    const int64_t off_in = row * 2 * hidden + cv * VEC;
+    const int64_t off_g = row * hidden + cv * VEC;
+    Vec16<T> gv, uv, dv, og, ou;
+    gv.raw = ld_global_nc_v4(gate_up + off_in);
+    uv.raw = ld_global_nc_v4(gate_up + off_in + hidden);
+    dv.raw = ld_global_nc_v4(grad_out + off_g);
+    float g[VEC], up[VEC], d[VEC], rg[VEC], ru[VEC];
+    gv.to_float(g);
+    uv.to_float(up);
+    dv.to_float(d);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const float s = sigmoidf_(g[i]);
+      const float silu = g[i] * s;
+      const float dsilu = s * (1.0f + g[i] * (1.0f - s));
+      rg[i] = d[i] * up[i] * dsilu;
+      ru[i] = d[i] * silu;
+    }
+    og.from_float(rg);
+    ou.from_float(ru);
+    st_global_v4(grad_gate_up + off_in, og.raw);
+    st_global_v4(grad_gate_up + off_in + hidden, ou.raw);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_bwd_scalar_kernel(const T* __restrict__ gate_up,
+                                                               const T* __restrict__ grad_out,
+                                                               T* __restrict__ grad_gate_up,
+                                                               int64_t rows, int64_t hidden) {
+  const int64_t total = rows * hidden;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / hidden, col = i - row * hidden;
+    const int64_t gi = row * 2 * hidden + col;
+    const float g = to_f32(gate_up[gi]);
+    const float u = to_f32(gate_up[gi + hidden]);
+    const float d = to_f32(grad_out[i]);
+    const float s = sigmoidf_(g);
+    grad_gate_up[gi] = from_f32<T>(d * u * s * (1.0f + g * (1.0f - s)));
+    grad_gate_up[gi + hidden] = from_f32<T>(d * g * s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Residual add + RMSNorm (model.py:14-16, 73-75)
+// One warp per row; lane l owns 16-byte vectors l, l+32, ... of the row.
+// ---------------------------------------------------------------------------
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_vec_kernel(
+    const T* __restrict__ residual, const T* __restrict__ branch, const T* __restrict__ weight,
+    T* __restrict__ out, T* __restrict__ norm, int64_t rows, int cols, float eps) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const float inv_cols = 1.0f / static_cast<float>(cols);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); row < rows;
+       row += static_cast<int64_t>(gridDim.x) * wpb) {
+    const int64_t base = row * cols;
+    float x[NV][VEC];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * VEC;
+      if (c < cols) {
+        Vec16<T> bv;
+        bv.raw = ld_global_nc_v4(branch + base + c);
+        bv.to_float(x[j]);
+        if (residual != nullptr) {
+          Vec16<T> rv, ov;
+          rv.raw = ld_global_nc_v4(residual + base + c);
+          float r[VEC];
+          rv.to_float(r);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) x[j][i] += r[i];
+          ov.from_float(x[j]);
+          st_global_v4(out + base + c, ov.raw);
+          ov.to_float(x[j]);  // the norm sees the value stored in `out` (dtype-rounded)
+        }
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) ss += x[j][i] * x[j][i];
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss * inv_cols + eps);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * VEC;
+      if (c < cols) {
+        float y[VEC];
+        if (weight != nullptr) {
+          Vec16<T> wv;
+          wv.raw = ld_global_v4(weight + c);
+          float w[VEC];
+          wv.to_float(w);
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) y[i] = x[j][i] * r * w[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) y[i] = x[j][i] * r;
+        }
+        Vec16<T> yv;
+        yv.from_float(y);
+        st_global_v4(norm + base + c, yv.raw);
+      }
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_scalar_kernel(
+    const T* __restrict__ residual, const T* __restrict__ branch, const T* __restrict__ weight,
+    T* __restrict__ out, T* __restrict__ norm, int64_t rows, int cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); row < rows;
+       row += static_cast<int64_t>(gridDim.x) * wpb) {
+    const int64_t base = row * cols;
+    float ss = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+      float x = to_f32(branch[base + c]);
+      if (residual != nullptr) {
+        const T o = from_f32<T>(x + to_f32(residual[base + c]));
+        out[base + c] = o;
+        x = to_f32(o);
+      }
+      ss += x * x;
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / static_cast<float>(cols) + eps);
+    __syncwarp();
+    for (int c = lane; c < cols; c += 32) {
+      const float x = residual != nullptr ? to_f32(out[base + c]) : to_f32(branch[base + c]);
+      float y = x * r;
+      if (weight != nullptr) y *= to_f32(weight[c]);
+      norm[base + c] = from_f32<T>(y);
+    }
+  }
+}
+
+// Backward.  partial (optional) receives per-warp sums of g*x*r for dweight:
+// partial[(blockIdx.x * wpb + warp) * cols + c].
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(
+    const T* __restrict__ xin, const T* __restrict__ weight, const T* __restrict__ grad_out,
+    const T* __restrict__ grad_norm, T* __restrict__ grad_in, float* __restrict__ partial,
+    int64_t rows, int cols, float eps) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const float inv_cols = 1.0f / static_cast<float>(cols);
+  float wacc[NV][VEC];
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) wacc[j][i] = 0.0f;
+  float w[NV][VEC];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (lane + 32 * j) * VEC;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) w[j][i] = 1.0f;
+    if (weight != nullptr && c < cols) {
+      Vec16<T> wv;
+      wv.raw = ld_global_v4(weight + c);
+      wv.to_float(w[j]);
+    }
+  }
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); row < rows;
+       row += static_cast<int64_t>(gridDim.x) * wpb) {
+    const int64_t base = row * cols;
+    float x[NV][VEC], g[NV][VEC];
+    float ss = 0.0f, dot = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * VEC;
+      if (c < cols) {
+        Vec16<T> xv, gv;
+        xv.raw = ld_global_nc_v4(xin + base + c);
+        gv.raw = ld_global_nc_v4(grad_norm + base + c);
+        xv.to_float(x[j]);
+        gv.to_float(g[j]);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          ss += x[j][i] * x[j][i];
+          dot += g[j][i] * w[j][i] * x[j][i];
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    dot = warp_sum(dot);
+    const float r = rsqrtf(ss * inv_cols + eps);
+    const float k3 = r * r * r * dot * inv_cols;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * VEC;
+      if (c < cols) {
+        float go[VEC];
+        if (grad_out != nullptr) {
+          Vec16<T> ov;
+          ov.raw = ld_global_nc_v4(grad_out + base + c);
+          ov.to_float(go);
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) go[i] = 0.0f;
+        }
+        float d[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          d[i] = go[i] + r * g[j][i] * w[j][i] - x[j][i] * k3;
+          wacc[j][i] += g[j][i] * x[j][i] * r;
+        }
+        Vec16<T> dv;
+        dv.from_float(d);
+        st_global_v4(grad_in + base + c, dv.raw);
+      }
+    }
+  }
+  if (partial != nullptr) {
+    float* dst = partial + (static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5)) * cols;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * VEC;
+      if (c < cols) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) dst[c + i] = wacc[j][i];
+      }
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_scalar_kernel(
+    const T* __restrict__ xin, const T* __restrict__ weight, const T* __restrict__ grad_out,
+    const T* __restrict__ grad_norm, T* __restrict__ grad_in, float* __restrict__ partial,
+    int64_t rows, int cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  float* dst = partial != nullptr
+                   ? partial + (static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5)) * cols
+                   : nullptr;
+  if (dst != nullptr)
+    for (int c = lane; c < cols; c += 32) dst[c] = 0.0f;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); row < rows;
+       row += static_cast<int64_t>(gridDim.x) * wpb) {
+    const int64_t base = row * cols;
+    float ss = 0.0f, dot = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+      const float x = to_f32(xin[base + c]);
+      const float w = weight != nullptr ? to_f32(weight[c]) : 1.0f;
+      ss += x * x;
+      dot += to_f32(grad_norm[base + c]) * w * x;
+    }
+    ss = warp_sum(ss);
+    dot = warp_sum(dot);
+    const float r = rsqrtf(ss / static_cast<float>(cols) + eps);
+    const float k3 = r * r * r * dot / static_cast<float>(cols);
+    for (int c = lane; c < cols; c += 32) {
+      const float x = to_f32(xin[base + c]);
+      const float g = to_f32(grad_norm[base + c]);
+      const float w = weight != nullptr ? to_f32(weight[c]) : 1.0f;
+      const float go = grad_out != nullptr ? to_f32(grad_out[base + c]) : 0.0f;
+      grad_in[base + c] = from_f32<T>(go + r * g * w - x * k3);
+      if (dst != nullptr) dst[c] += g * x * r;
+    }
+  }
+}
+
+// grad_weight[c] = sum_p partial[p][c]  (fixed summation order: deterministic)
+template <typename T>
+__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ partial,
+                                                             T* __restrict__ grad_weight,
+                                                             int num_partials, int cols) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float acc = 0.0f;
+  for (int p = 0; p < num_partials; ++p) acc += partial[static_cast<int64_t>(p) * cols + c];
+  grad_weight[c] = from_f32<T>(acc);
+}
+
+// data *= *scale
+template <typename T>
+__global__ void __launch_bounds__(256) scale_kernel(T* __restrict__ data,
+                                                   const float* __restrict__ scale, int64_t n) {
+  constexpr int VEC = 16 / sizeof(T);
+  const float s = *scale;
+  const int64_t nv = n / VEC;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int64_t v = tid; v < nv; v += stride) {
+    Vec16<T> x;
+    x.raw = ld_global_v4(data + v * VEC);
+    float f[VEC];
+    x.to_float(f);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) f[i] *= s;
+    x.from_float(f);
+    st_global_v4(data + v * VEC, x.raw);
+  }
+  for (int64_t i = nv * VEC + tid; i < n; i += stride) data[i] = from_f32<T>(to_f32(data[i]) * s);
+}
+
+// Number of per-warp dweight partials used by the RMSNorm backward.
+static constexpr int kRmsBwdThreads = 256;
+static constexpr int kRmsBwdWarps = kRmsBwdThreads / 32;
+static constexpr int kRmsBwdMaxBlocks = 128;
+
+static inline int rms_bwd_weight_blocks(int64_t rows) {
+  int64_t b = (rows + kRmsBwdWarps - 1) / kRmsBwdWarps;
+  if (b > kRmsBwdMaxBlocks) b = kRmsBwdMaxBlocks;
+  if (b < 1) b = 1;
+  return static_cast<int>(b);
+}
+
+template <typename T>
+static int pick_nv(int cols) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int nv = (cols + 32 * VEC - 1) / (32 * VEC);
+  if (nv <= 1) return 1;
+  if (nv <= 2) return 2;
+  if (nv <= 3) return 3;
+  if (nv <= 4) return 4;
+  if (nv <= 6) return 6;
+  if (nv <= 8) return 8;
+  return 0;  // too wide for the register-resident path
+}
+
+#define HLM_DISPATCH_NV(nv, NVC, ...) \
+  switch (nv) {                       \
+    case 1: {                         \
+      constexpr int NVC = 1;          \
+      __VA_ARGS__;                    \
+      break;                          \
+    }                                 \
+    case 2: {                         \
+      constexpr int NVC = 2;          \
+      __VA_ARGS__;                    \
+      break;                          \
+    }                                 \
+    case 3: {                         \
+      constexpr int NVC = 3;          \
+      __VA_ARGS__;                    \
+      break;                          \
+    }                                 \
+    case 4: {                         \
+      constexpr int NVC = 4;          \
+      __VA_ARGS__;                    \
+      break;                          \
+    }                                 \
+    case 6: {                         \
+      constexpr int NVC = 6;          \
+      __VA_ARGS__;                    \
+      break;                          \
+    }                                 \
+    default: {                        \
+      constexpr int NVC = 8;          \
+      __VA_ARGS__;                    \
+      break;                          \
+    }                                 \
+  }
+
+}  // namespace hlm
+
+using namespace hlm;
+
+extern "C" int hlm_swiglu_fwd(const void* gate_up, void* out, int64_t rows, int64_t hidden,
+                              int dtype, void* stream) {
+  if (rows < 0 || hidden < 0) return HLM_ERR_INVALID_ARG;
+  if (rows == 0 || hidden == 0) return HLM_OK;
+  if (gate_up == nullptr || out == nullptr) return HLM_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  HLM_DISPATCH_DTYPE(dtype, T, {
+    constexpr int VEC = 16 / sizeof(T);
+    const bool vec = (hidden % VEC == 0) && host_aligned16(gate_up) && host_aligned16(out);
+    if (vec) {
+      const int grid = elementwise_grid(rows * (hidden / VEC) / 2 + 1, 256);
+      swiglu_fwd_vec_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(gate_up),
+                                                    static_cast<T*>(out), rows, hidden);
+    } else {
+      const int grid = elementwise_grid(rows * hidden, 256);
+      swiglu_fwd_scalar_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(gate_up),
+                                                       static_cast<T*>(out), rows, hidden);
+    }
+  });
+  return launch_status();
+}
+
+extern "C" int hlm_swiglu_bwd(const void* gate_up, const void* grad_out, void* grad_gate_up,
+                              int64_t rows, int64_t hidden, int dtype, void* stream) {
+  if (rows < 0 || hidden < 0) return HLM_ERR_INVALID_ARG;
+  if (rows == 0 || hidden == 0) return HLM_OK;
+  if (gate_up == nullptr || grad_out == nullptr || grad_gate_up == nullptr)
+    return HLM_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  HLM_DISPATCH_DTYPE(dtype, T, {
+    constexpr int VEC = 16 / sizeof(T);
+    const bool vec = (hidden % VEC == 0) && host_aligned16(gate_up) && host_aligned16(grad_out) &&
+                     host_aligned16(grad_gate_up);
+    if (vec) {
+      const int grid = elementwise_grid(rows * (hidden / VEC), 256);
+      swiglu_bwd_vec_kernel<T><<<grid, 256, 0, s>>>(
+          static_cast<const T*>(gate_up), static_cast<const T*>(grad_out),
+          static_cast<T*>(grad_gate_up), rows, hidden);
+    } else {
+      const int grid = elementwise_grid(rows * hidden, 256);
+      swiglu_bwd_scalar_kernel<T><<<grid, 256, 0, s>>>(
+          static_cast<const T*>(gate_up), static_cast<const T*>(grad_out),
+          static_cast<T*>(grad_gate_up), rows, hidden);
+    }
+  });
+  return launch_status();
+}
+
+extern "C" int hlm_residual_rms_norm_fwd(const void* residual, const void* branch,
+                                         const void* weight, void* out, void* norm, int64_t rows,
+                                         int64_t cols, float eps, int dtype, void* stream) {
+  if (rows < 0 || cols < 0 || cols > (1ll << 30)) return HLM_ERR_INVALID_ARG;
+  if (rows == 0 || cols == 0) return HLM_OK;
+  if (branch == nullptr || norm == nullptr) return HLM_ERR_INVALID_ARG;
+  if (residual != nullptr && out == nullptr) return HLM_ERR_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int threads = 256, wpb = threads / 32;
+  HLM_DISPATCH_DTYPE(dtype, T, {
+    constexpr int VEC = 16 / sizeof(T);
+    const int nv = pick_nv<T>(static_cast<int>(cols));
+    const bool vec = nv > 0 && cols % VEC == 0 && host_aligned16(branch) && host_aligned16(norm) &&
+                     (residual == nullptr || (host_aligned16(residual) && host_aligned16(out))) &&
+                     (weight == nullptr || host_aligned16(weight));
+    const int grid = elementwise_grid(rows * 32, threads);
+    (void)wpb;
+    if (vec) {
+      HLM_DISPATCH_NV(nv, NVC, {
+        rmsnorm_fwd_vec_kernel<T, NVC><<<grid, threads, 0, s>>>(
+            static_cast<const T*>(residual), static_cast<const T*>(branch),
+            static_cast<const T*>(weight), static_cast<T*>(out), static_cast<T*>(norm), rows,
+            static_cast<int>(cols), eps);
+      });
+    } else {
+      rmsnorm_fwd_scalar_kernel<T><<<grid, threads, 0, s>>>(
+          static_cast<const T*>(residual), static_cast<const T*>(branch),
+          static_cast<const T*>(weight), static_cast<T*>(out), static_cast<T*>(norm), rows,
+          static_cast<int>(cols), eps);
+    }
+  });
+  return launch_status();
+}
+
+extern "C" size_t hlm_rms_norm_bwd_workspace_bytes(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return static_cast<size_t>(rms_bwd_weight_blocks(rows)) * kRmsBwdWarps *
+         static_cast<size_t>(cols) * sizeof(float);
+}
+
+extern "C" int hlm_residual_rms_norm_bwd(const void* x, const void* weight, const void* grad_out,
+                                         const void* grad_norm, void* grad_in, void* grad_weight,
+                                         void* workspace, size_t workspace_bytes, int64_t rows,
+                                         int64_t cols, float eps, int dtype, void* stream) {
+  if (rows < 0 || cols < 0 || cols > (1ll << 30)) return HLM_ERR_INVALID_ARG;
+  if (cols == 0) return HLM_OK;
+  if (x == nullptr || grad_norm == nullptr || grad_in == nullptr) {
+    if (rows != 0) return HLM_ERR_INVALID_ARG;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool want_w = weight != nullptr && grad_weight != nullptr;
+  float* partial = nullptr;
+  int grid = 1;
+  const int threads = kRmsBwdThreads;
+  if (want_w) {
+    if (workspace == nullptr || workspace_bytes < hlm_rms_norm_bwd_workspace_bytes(rows, cols))
+      return HLM_ERR_WORKSPACE;
+    partial = static_cast<float*>(workspace);
+    grid = rms_bwd_weight_blocks(rows);
+  } else {
+    grid = elementwise_grid(rows * 32, threads);
+  }
+  HLM_DISPATCH_DTYPE(dtype, T, {
+    if (rows > 0) {
+      constexpr int VEC = 16 / sizeof(T);
+      const int nv = pick_nv<T>(static_cast<int>(cols));
+      const bool vec = nv > 0 && cols % VEC == 0 && host_aligned16(x) &&
+                       host_aligned16(grad_norm) && host_aligned16(grad_in) &&
+                       (grad_out == nullptr || host_aligned16(grad_out)) &&
+                       (weight == nullptr || host_aligned16(weight));
+      if (vec) {
+        HLM_DISPATCH_NV(nv, NVC, {
+          rmsnorm_bwd_vec_kernel<T, NVC><<<grid, threads, 0, s>>>(
+              static_cast<const T*>(x), static_cast<const T*>(weight),
+              static_cast<const T*>(grad_out), static_cast<const T*>(grad_norm),
+              static_cast<T*>(grad_in), partial, rows, static_cast<int>(cols), eps);
+        });
+      } else {
+        rmsnorm_bwd_scalar_kernel<T><<<grid, threads, 0, s>>>(
+            static_cast<const T*>(x), static_cast<const T*>(weight),
+            static_cast<const T*>(grad_out), static_cast<const T*>(grad_norm),
+            static_cast<T*>(grad_in), partial, rows, static_cast<int>(cols), eps);
+      }
+    } else if (want_w) {
+      // No rows: dweight is zero.
+      if (cudaMemsetAsync(partial, 0, static_cast<size_t>(cols) * sizeof(float), s) !=
+          cudaSuccess)
+        return HLM_ERR_LAUNCH;
+    }
+    if (want_w) {
+      const int nparts = rows > 0 ? grid * kRmsBwdWarps : 1;
+      reduce_partials_kernel<T><<<static_cast<int>((cols + 255) / 256), 256, 0, s>>>(
+          partial, static_cast<T*>(grad_weight), nparts, static_cast<int>(cols));
+    }
+  });
+  return launch_status();
+}
+
+extern "C" int hlm_scale_by_device_scalar(void* data, const float* scale, int64_t n, int dtype,
+                                          void* stream) {
+  if (n < 0) return HLM_ERR_INVALID_ARG;
+  if (n == 0) return HLM_OK;
+  if (data == nullptr || scale == nullptr) return HLM_ERR_INVALID_ARG;
+  if (!host_aligned16(data)) return HLM_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  HLM_DISPATCH_DTYPE(dtype, T, {
+    constexpr int VEC = 16 / sizeof(T);
+    const int grid = elementwise_grid(n / VEC + 1, 256);
+    scale_kernel<T><<<grid, 256, 0, s>>>(static_cast<T*>(data), scale, n);
+  });
+  return launch_status();
+}

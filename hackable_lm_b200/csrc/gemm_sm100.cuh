@@ -1,0 +1,428 @@
+// Persistent warp-specialised tcgen05 GEMM core for sm_100a.
+//
+//   D[M, N] (+)= A[M, K] * B[N, K]^T      bf16 operands, fp32 accumulation in TMEM
+//
+// Roles (192 threads, one CTA per SM, grid = min(#tiles, #SMs)):
+//   warp 0      : one thread issues TMA loads (cp.async.bulk.tensor, 128-byte
+//                 swizzle) into a STAGES-deep shared-memory ring
+//   warp 1      : allocates TMEM; one thread issues tcgen05.mma (M=128, N=BN,
+//                 K=16) and tcgen05.commit to release stages / publish tiles
+//   warps 2..5  : epilogue; warp w reads TMEM lanes 32*(w%4)..+31 (one
+//                 accumulator row per thread) and runs the Epi functor
+// Two accumulators of BN columns each live in TMEM, so the epilogue of tile i
+// overlaps the MMAs of tile i+1.
+//
+// Operand layouts: each operand is either K-major (stored [rows][ld], K
+// contiguous; one TMA box {64, rows} per stage) or MN-major (stored [K][ld],
+// M or N contiguous; rows/64 boxes {64, 64} per stage).  The contiguous
+// dimension of A may be the concatenation of up to three tensors
+// ("segments", boundaries a_seg1 / a_seg2), which lets the QKV backward read
+// dq/dk/dv in place as one concatenated operand.
+//
+// Every mbarrier wait is bounded (see mbar_wait); on a timeout the kernel
+// records an error code, drains its own in-flight TMA copies, frees TMEM and
+// returns.
+#pragma once
+
+#include "hlm_common.cuh"
+
+namespace hlm {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
+constexpr int kUmmaK = 16;
+constexpr int kGemmThreads = 192;
+constexpr int kEpiWarp0 = 2;
+
+struct GemmParams {
+  int M, N, K;
+  int m_tiles, n_tiles, k_blocks;
+  int splits, kb_per_split;
+  // A's contiguous dimension may be the concatenation of three tensors:
+  // [0, a_seg1) -> map 0, [a_seg1, a_seg2) -> map 1, [a_seg2, ...) -> map 2.
+  // a_seg1 == 0 means a single tensor.  Boundaries are multiples of 64.
+  int a_seg1, a_seg2;
+  int* err;
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kNumBars = 2 * STAGES + 4;
+  static constexpr int kTmemSlotOffset = kBarOffset + kNumBars * 8;
+  static constexpr int kEpiOffset = ((kTmemSlotOffset + 16 + 1023) / 1024) * 1024;
+  static constexpr int kTmemCols = 2 * BN;
+  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
+};
+
+HLM_DEVICE void decode_work(int w, const GemmParams& p, int& m_tile, int& n_tile, int& split) {
+  const int per_split = p.m_tiles * p.n_tiles;
+  split = w / per_split;
+  const int r = w - split * per_split;
+  m_tile = r / p.n_tiles;
+  n_tile = r - m_tile * p.n_tiles;
+}
+
+HLM_DEVICE void select_segment(const GemmParams& p, int& c, const CUtensorMap*& mp,
+                               const CUtensorMap* m0, const CUtensorMap* m1,
+                               const CUtensorMap* m2) {
+  if (c < p.a_seg1) {
+    mp = m0;
+  } else if (c < p.a_seg2) {
+    c -= p.a_seg1;
+    mp = m1;
+  } else {
+    c -= p.a_seg2;
+    mp = m2;
+  }
+}
+
+// Wait by lane 0, result broadcast to the warp (keeps .sync.aligned tcgen05
+// instructions that follow convergent even when a wait times out).
+HLM_DEVICE bool warp_wait(uint32_t bar, uint32_t parity, int* err, int code, int lane) {
+  int ok = 1;
+  if (lane == 0) ok = mbar_wait(bar, parity, err, code) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  return ok != 0;
+}
+
+// Wait that ignores the error word (used only to drain in-flight TMA copies
+// before the CTA exits); bounded by the same timeout.
+HLM_DEVICE bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      record_error(err, kDevErrTimeoutDrain);
+      return false;
+    }
+  }
+  return true;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA0,
+                      const __grid_constant__ CUtensorMap tmA1,
+                      const __grid_constant__ CUtensorMap tmA2,
+                      const __grid_constant__ CUtensorMap tmB, const GemmParams p,
+                      const typename Epi::Params ep) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t bar0 = base + L::kBarOffset;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + L::kTmemSlotOffset);
+  int* err = p.err;
+
+#define FULL_BAR(s) (bar0 + 8u * (s))
+#define EMPTY_BAR(s) (bar0 + 8u * (STAGES + (s)))
+#define TFULL_BAR(a) (bar0 + 8u * (2 * STAGES + (a)))
+#define TEMPTY_BAR(a) (bar0 + 8u * (2 * STAGES + 2 + (a)))
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(FULL_BAR(s), 1);
+      mbar_init(EMPTY_BAR(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(TFULL_BAR(a), 1);
+      mbar_init(TEMPTY_BAR(a), 4);  // one arrival per epilogue warp
+    }
+    fence_mbar_init();
+    prefetch_tensormap(&tmA0);
+    if (p.a_seg1 > 0) {
+      prefetch_tensormap(&tmA1);
+      prefetch_tensormap(&tmA2);
+    }
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  const int total = p.m_tiles * p.n_tiles * p.splits;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_mask = 0, armed_par = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+        int m_tile, n_tile, split;
+        decode_work(w, p, m_tile, n_tile, split);
+        const int m0 = m_tile * kBM;
+        const int n0 = n_tile * BN;
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(EMPTY_BAR(stage), phase ^ 1u, err, kDevErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(FULL_BAR(stage), L::kStageBytes);
+          armed_mask |= 1u << stage;
+          armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+          const uint32_t sa = base + stage * L::kStageBytes;
+          const uint32_t sb = sa + L::kABytes;
+          const int k0 = kb * kBK;
+          // ---- A
+          if constexpr (!A_MN) {
+            const CUtensorMap* mp = &tmA0;
+            int kc = k0;
+            if (p.a_seg1 > 0) select_segment(p, kc, mp, &tmA0, &tmA1, &tmA2);
+            tma_load_2d(sa, mp, kc, m0, FULL_BAR(stage));
+          } else {
+#pragma unroll
+            for (int i = 0; i < kBM / 64; ++i) {
+              const CUtensorMap* mp = &tmA0;
+              int mc = m0 + 64 * i;
+              if (p.a_seg1 > 0) select_segment(p, mc, mp, &tmA0, &tmA1, &tmA2);
+              tma_load_2d(sa + i * 8192u, mp, mc, k0, FULL_BAR(stage));
+            }
+          }
+          // ---- B
+          if constexpr (!B_MN) {
+            tma_load_2d(sb, &tmB, k0, n0, FULL_BAR(stage));
+          } else {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i) tma_load_2d(sb + i * 8192u, &tmB, n0 + 64 * i, k0, FULL_BAR(stage));
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: every stage we armed must have landed before shared memory is
+      // released (immediate in normal runs: the MMA warp consumed them).
+      for (int s = 0; s < STAGES; ++s)
+        if (armed_mask & (1u << s)) mbar_wait_drain(FULL_BAR(s), (armed_par >> s) & 1u, err);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
+        int m_tile, n_tile, split;
+        decode_work(w, p, m_tile, n_tile, split);
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        const int acc = it & 1;
+        const uint32_t acc_par = static_cast<uint32_t>((it >> 1) & 1);
+        if (!mbar_wait(TEMPTY_BAR(acc), acc_par ^ 1u, err, kDevErrTimeoutTmemEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(FULL_BAR(stage), phase, err, kDevErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + stage * L::kStageBytes;
+          const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+            const uint64_t adesc = A_MN ? make_sw128_desc(sa + kk * 2048u, 8192u, 1024u)
+                                        : make_sw128_desc(sa + kk * 32u, 16u, 1024u);
+            const uint64_t bdesc = B_MN ? make_sw128_desc(sb + kk * 2048u, 8192u, 1024u)
+                                        : make_sw128_desc(sb + kk * 32u, 16u, 1024u);
+            tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(EMPTY_BAR(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(TFULL_BAR(acc));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    int it = 0;
+    for (int w = blockIdx.x; w < total; w += gridDim.x, ++it) {
+      int m_tile, n_tile, split;
+      decode_work(w, p, m_tile, n_tile, split);
+      const int acc = it & 1;
+      const uint32_t acc_par = static_cast<uint32_t>((it >> 1) & 1);
+      if (!warp_wait(TFULL_BAR(acc), acc_par, err, kDevErrTimeoutTmemFull, lane)) break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      Epi::template run<BN>(ep, p, base_ptr + L::kEpiOffset, taddr, m_tile, n_tile, split, quad,
+                            lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(TEMPTY_BAR(acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+#undef FULL_BAR
+#undef EMPTY_BAR
+#undef TFULL_BAR
+#undef TEMPTY_BAR
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+// Encode a 2-D bf16 tensor map with 128-byte swizzle.
+//   inner: elements along the contiguous dimension, outer: number of rows,
+//   ld: row stride in elements, box = {64, box_outer}.
+bool encode_bf16_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t ld, uint32_t box_outer);
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+int launch_gemm_sm100(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& a2,
+                      const CUtensorMap& b, const GemmParams& p, const typename Epi::Params& ep,
+                      cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES>;
+  auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, Epi>;
+  const int smem = L::kEpiOffset + Epi::kSmemBytes + 1024;
+  static_assert(L::kEpiOffset + Epi::kSmemBytes + 1024 <= 232448, "shared memory budget exceeded");
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return HLM_ERR_LAUNCH;
+  const int total = p.m_tiles * p.n_tiles * p.splits;
+  if (total <= 0) return HLM_OK;
+  int grid = num_sms_of_current_device();
+  if (grid > total) grid = total;
+  kern<<<grid, kGemmThreads, smem, stream>>>(a0, a1, a2, b, p, ep);
+  return launch_status();
+}
+
+// Fill the tiling fields of GemmParams.
+inline void gemm_tiling(GemmParams& p, int M, int N, int K, int BN, int splits) {
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.m_tiles = (M + kBM - 1) / kBM;
+  p.n_tiles = (N + BN - 1) / BN;
+  p.k_blocks = (K + kBK - 1) / kBK;
+  if (splits < 1) splits = 1;
+  if (splits > p.k_blocks) splits = p.k_blocks;
+  p.kb_per_split = (p.k_blocks + splits - 1) / splits;
+  p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+  p.a_seg1 = 0;
+  p.a_seg2 = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue: store D (bf16 or fp32), optional accumulate, optional split-K slab
+// ---------------------------------------------------------------------------
+struct EpiStore {
+  struct Params {
+    void* d;
+    int64_t ldd;
+    int64_t split_stride;  // elements between split-K slabs (fp32 partials)
+    int dtype;             // HLM_BF16 or HLM_F32
+    int accumulate;        // D += acc (read-modify-write)
+    int vec_ok;            // ldd % 8 == 0 and d 16-byte aligned
+  };
+  static constexpr int kSmemBytes = 0;
+
+  template <int BN>
+  static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t* /*smem*/,
+                             uint32_t taddr, int m_tile, int n_tile, int split, int quad,
+                             int lane) {
+    const int row = m_tile * kBM + quad * 32 + lane;
+    const bool row_ok = row < p.M;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), r);
+      tmem_ld_wait();
+      const int col0 = n_tile * BN + c * 32;
+      if (!row_ok || col0 >= p.N) continue;
+      const bool full = ep.vec_ok && (col0 + 32 <= p.N);
+      if (ep.dtype == HLM_F32) {
+        float* d = static_cast<float*>(ep.d) + static_cast<int64_t>(split) * ep.split_stride +
+                   static_cast<int64_t>(row) * ep.ldd + col0;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                   __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            if (ep.accumulate) {
+              const float4 o = *reinterpret_cast<const float4*>(d + j);
+              v.x += o.x;
+              v.y += o.y;
+              v.z += o.z;
+              v.w += o.w;
+            }
+            *reinterpret_cast<float4*>(d + j) = v;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j < p.N) {
+              float v = __uint_as_float(r[j]);
+              if (ep.accumulate) v += d[j];
+              d[j] = v;
+            }
+          }
+        }
+      } else {
+        __nv_bfloat16* d = static_cast<__nv_bfloat16*>(ep.d) + static_cast<int64_t>(row) * ep.ldd + col0;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            float f[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(r[j + i]);
+            if (ep.accumulate) {
+              Vec16<__nv_bfloat16> o;
+              o.raw = *reinterpret_cast<const uint4*>(d + j);
+              float of[8];
+              o.to_float(of);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) f[i] += of[i];
+            }
+            Vec16<__nv_bfloat16> v;
+            v.from_float(f);
+            *reinterpret_cast<uint4*>(d + j) = v.raw;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j < p.N) {
+              float v = __uint_as_float(r[j]);
+              if (ep.accumulate) v += __bfloat162float(d[j]);
+              d[j] = __float2bfloat16_rn(v);
+            }
+          }
+        }
+      }
+    }
+  }
+};
+
+}  // namespace hlm

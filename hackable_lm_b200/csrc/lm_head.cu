@@ -1,0 +1,441 @@
+// Fused LM head + cross-entropy (forward and backward in one call), the B200
+// restatement of _TritonFusedLinearCrossEntropy (kernels.py:878-942) and
+// _linear_ce_kernel (kernels.py:291-318), with F.cross_entropy ignore_index
+// semantics (ignored rows: no loss, no gradient; mean over the other rows).
+//
+// Per token chunk (the whole batch when it fits the logits budget):
+//   1. logits GEMM   S = H_chunk @ W^T on tcgen05 (BN = 256 vocab columns per
+//      tile); the epilogue rounds each logit to bf16 (the reference's logits
+//      dtype), stores it, and folds it into a per-(row, tile) running
+//      (max, sum exp) pair; the target logit is picked up in the tile that
+//      holds it.  Full fp32 logits never exist in memory.
+//   2. finalize      lse[row] = combine of the per-tile pairs; per-row loss;
+//      deterministic per-block loss sums.
+//   3. dlogits       in place: P = (exp(S - lse) - onehot(target)) / n_valid,
+//      zero for ignored rows (the reference's in-place gradient overwrite,
+//      kernels.py:315-318).
+//   4. dX GEMM       grad_hidden[chunk] = P @ W        (W read N-major)
+//   5. dW GEMM       grad_weight (+)= P^T @ H_chunk    (both operands MN-major)
+// A pre-pass counts the valid targets of the whole batch so the 1/n_valid
+// scale is known to every chunk on the device, with no host round trip.
+#include "gemm_sm100.cuh"
+
+namespace hlm {
+
+constexpr int kLmBN = 256;
+constexpr int kLmStages = 4;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct LmStats {
+  int n_valid;
+  float inv_n;    // 1 / n_valid (0 when no row is valid)
+  float loss_sum; // running sum of per-row losses over chunks
+  int bad_target; // count of targets outside [0, V) that are not ignore_index
+};
+
+struct EpiLogitsLSE {
+  struct Params {
+    __nv_bfloat16* logits;   // [rows][ld]
+    int64_t ld;              // = V
+    float2* partial;         // [n_tiles][rows] (max, sum exp(x - max))
+    float* tgt_logit;        // [rows]
+    const int64_t* targets;  // [rows]
+    int V;
+    int rows;
+  };
+  static constexpr int kSmemBytes = 0;
+
+  template <int BN>
+  static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t*, uint32_t taddr,
+                             int m_tile, int n_tile, int, int quad, int lane) {
+    const int row = m_tile * kBM + quad * 32 + lane;
+    const bool row_ok = row < p.M;
+    const int64_t tgt = row_ok ? ep.targets[row] : -1;
+    const int n0 = n_tile * BN;
+    float m_run = -INFINITY, s_run = 0.0f;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), r);
+      tmem_ld_wait();
+      const int col0 = n0 + c * 32;
+      float v[32];
+      float cmax = -INFINITY;
+      uint32_t packed[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const __nv_bfloat162 h2 =
+            __floats2bfloat162_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+        packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+        const float2 f2 = __bfloat1622float2(h2);
+        v[j] = (col0 + j < ep.V) ? f2.x : -INFINITY;
+        v[j + 1] = (col0 + j + 1 < ep.V) ? f2.y : -INFINITY;
+        cmax = fmaxf(cmax, fmaxf(v[j], v[j + 1]));
+      }
+      if (tgt >= col0 && tgt < col0 + 32) {
+        float tl = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j == tgt) tl = v[j];
+        ep.tgt_logit[row] = tl;
+      }
+      if (cmax > -INFINITY) {
+        const float new_m = fmaxf(m_run, cmax);
+        const float nm2 = new_m * kLog2e;
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s += exp2f(fmaf(v[j], kLog2e, -nm2));
+        s_run = s_run * exp2f((m_run - new_m) * kLog2e) + s;
+        m_run = new_m;
+      }
+      if (row_ok && col0 < ep.V) {
+        __nv_bfloat16* dst = ep.logits + static_cast<int64_t>(row) * ep.ld + col0;
+        if (col0 + 32 <= ep.V) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            st_global_v4(dst + 2 * j, make_uint4(packed[j], packed[j + 1], packed[j + 2], packed[j + 3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < ep.V) dst[j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+    if (row_ok) ep.partial[static_cast<int64_t>(n_tile) * ep.rows + row] = make_float2(m_run, s_run);
+  }
+};
+
+__global__ void __launch_bounds__(1024) lm_count_valid_kernel(const int64_t* __restrict__ targets,
+                                                             int64_t n, int64_t V,
+                                                             int64_t ignore_index,
+                                                             LmStats* __restrict__ stats) {
+  __shared__ int s_valid[32], s_bad[32];
+  int valid = 0, bad = 0;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const int64_t t = targets[i];
+    if (t == ignore_index) continue;
+    if (t >= 0 && t < V)
+      ++valid;
+    else
+      ++bad;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    valid += __shfl_xor_sync(0xffffffffu, valid, o);
+    bad += __shfl_xor_sync(0xffffffffu, bad, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_valid[threadIdx.x >> 5] = valid;
+    s_bad[threadIdx.x >> 5] = bad;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int tv = 0, tb = 0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {
+      tv += s_valid[w];
+      tb += s_bad[w];
+    }
+    stats->n_valid = tv;
+    stats->inv_n = tv > 0 ? 1.0f / static_cast<float>(tv) : 0.0f;
+    stats->loss_sum = 0.0f;
+    stats->bad_target = tb;
+  }
+}
+
+// One thread per row: lse, per-row loss, per-block loss sums.
+__global__ void __launch_bounds__(256) lm_finalize_kernel(
+    const float2* __restrict__ partial, int n_parts, const float* __restrict__ tgt_logit,
+    const int64_t* __restrict__ targets, int rows, int64_t V, int64_t ignore_index,
+    float* __restrict__ lse_out, float* __restrict__ block_sums) {
+  __shared__ float s_sum[8];
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  float loss = 0.0f;
+  if (row < rows) {
+    float m = -INFINITY;
+    for (int t = 0; t < n_parts; ++t) m = fmaxf(m, partial[static_cast<int64_t>(t) * rows + row].x);
+    float s = 0.0f;
+    for (int t = 0; t < n_parts; ++t) {
+      const float2 pr = partial[static_cast<int64_t>(t) * rows + row];
+      if (pr.y > 0.0f) s += pr.y * exp2f((pr.x - m) * kLog2e);
+    }
+    const float lse = m + log2f(s) * kLn2;
+    lse_out[row] = lse;
+    const int64_t t = targets[row];
+    if (t != ignore_index && t >= 0 && t < V) loss = lse - tgt_logit[row];
+  }
+  loss = warp_sum(loss);
+  if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = loss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = 0.0f;
+    for (int w = 0; w < 8; ++w) b += s_sum[w];
+    block_sums[blockIdx.x] = b;
+  }
+}
+
+// Single block: add this chunk's block sums (fixed order) to the running sum;
+// on the last chunk write loss = sum / n_valid.
+__global__ void __launch_bounds__(256) lm_loss_reduce_kernel(const float* __restrict__ block_sums,
+                                                            int n_blocks, LmStats* __restrict__ stats,
+                                                            float* __restrict__ loss, int last) {
+  __shared__ float s_sum[8];
+  float v = 0.0f;
+  for (int i = threadIdx.x; i < n_blocks; i += blockDim.x) v += block_sums[i];
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = 0.0f;
+    for (int w = 0; w < 8; ++w) b += s_sum[w];
+    const float total = stats->loss_sum + b;
+    stats->loss_sum = total;
+    if (last) *loss = stats->n_valid > 0 ? total / static_cast<float>(stats->n_valid) : NAN;
+  }
+}
+
+// In place: logits -> (softmax - onehot) / n_valid, zero rows for ignored targets.
+__global__ void __launch_bounds__(256) lm_dlogits_kernel(__nv_bfloat16* __restrict__ logits,
+                                                        const float* __restrict__ lse,
+                                                        const int64_t* __restrict__ targets,
+                                                        int rows, int64_t V, int64_t ignore_index,
+                                                        const LmStats* __restrict__ stats) {
+  const float inv_n = stats->inv_n;
+  const int64_t vpr = V / 8;
+  const int64_t total = static_cast<int64_t>(rows) * vpr;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = v / vpr;
+    const int64_t col0 = (v - row * vpr) * 8;
+    const int64_t t = targets[row];
+    const bool valid = t != ignore_index && t >= 0 && t < V;
+    __nv_bfloat16* p = logits + row * V + col0;
+    uint4 out = make_uint4(0, 0, 0, 0);
+    if (valid) {
+      const float l2 = lse[row] * kLog2e;
+      Vec16<__nv_bfloat16> in;
+      in.raw = ld_global_v4(p);
+      float f[8];
+      in.to_float(f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float q = exp2f(fmaf(f[i], kLog2e, -l2));
+        if (col0 + i == t) q -= 1.0f;
+        f[i] = q * inv_n;
+      }
+      Vec16<__nv_bfloat16> o;
+      o.from_float(f);
+      out = o.raw;
+    }
+    st_global_v4(p, out);
+  }
+}
+
+__global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restrict__ src,
+                                                         __nv_bfloat16* __restrict__ dst,
+                                                         int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+// ---------------------------------------------------------------------------
+// Workspace plan
+// ---------------------------------------------------------------------------
+static constexpr int64_t kLogitsBudgetBytes = 4ll << 30;  // per-chunk bf16 logits
+
+struct LmPlan {
+  int64_t chunk;
+  int n_chunks;
+  int n_parts;
+  size_t off_logits, off_partial, off_tgt, off_lse, off_bsum, off_stats, off_dw, total;
+};
+
+static inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+static LmPlan lm_plan(int64_t n_tokens, int64_t C, int64_t V, int64_t chunk_tokens, bool want_dw) {
+  LmPlan pl;
+  int64_t chunk;
+  if (chunk_tokens > 0) {
+    chunk = ((chunk_tokens + kBM - 1) / kBM) * kBM;
+  } else {
+    chunk = kLogitsBudgetBytes / (V * 2);
+    chunk = (chunk / kBM) * kBM;
+    if (chunk < kBM) chunk = kBM;
+  }
+  if (chunk > n_tokens) chunk = n_tokens;
+  if (chunk < 1) chunk = 1;
+  pl.chunk = chunk;
+  pl.n_chunks = static_cast<int>((n_tokens + chunk - 1) / chunk);
+  pl.n_parts = static_cast<int>((V + kLmBN - 1) / kLmBN);
+  size_t off = 0;
+  pl.off_logits = off;
+  off = align256(off + static_cast<size_t>(chunk) * V * 2);
+  pl.off_partial = off;
+  off = align256(off + static_cast<size_t>(pl.n_parts) * chunk * sizeof(float2));
+  pl.off_tgt = off;
+  off = align256(off + static_cast<size_t>(chunk) * 4);
+  pl.off_lse = off;
+  off = align256(off + static_cast<size_t>(chunk) * 4);
+  pl.off_bsum = off;
+  off = align256(off + static_cast<size_t>((chunk + 255) / 256) * 4);
+  pl.off_stats = off;
+  off = align256(off + sizeof(LmStats));
+  pl.off_dw = off;
+  if (want_dw && pl.n_chunks > 1) off = align256(off + static_cast<size_t>(V) * C * 4);
+  pl.total = off;
+  return pl;
+}
+
+}  // namespace hlm
+
+using namespace hlm;
+
+extern "C" size_t hlm_lm_head_ce_workspace_bytes(int64_t n_tokens, int64_t C, int64_t V,
+                                                 int64_t chunk_tokens) {
+  if (n_tokens <= 0 || C <= 0 || V <= 0) return 256;
+  return lm_plan(n_tokens, C, V, chunk_tokens, true).total;
+}
+
+extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int64_t* targets,
+                              float* loss, void* grad_hidden, void* grad_weight, void* workspace,
+                              size_t workspace_bytes, int64_t n_tokens, int64_t C, int64_t V,
+                              int64_t ignore_index, int64_t chunk_tokens, void* stream) {
+  if (n_tokens <= 0 || C <= 0 || V <= 0) return HLM_ERR_INVALID_ARG;
+  if (hidden == nullptr || weight == nullptr || targets == nullptr || loss == nullptr ||
+      workspace == nullptr)
+    return HLM_ERR_INVALID_ARG;
+  if (C % 64 != 0 || V % 8 != 0) return HLM_ERR_UNSUPPORTED;
+  if (n_tokens > (1ll << 30) || V > (1ll << 30) || C > 65536) return HLM_ERR_UNSUPPORTED;
+  if (!host_aligned16(hidden) || !host_aligned16(weight) ||
+      (grad_hidden != nullptr && !host_aligned16(grad_hidden)) ||
+      (grad_weight != nullptr && !host_aligned16(grad_weight)))
+    return HLM_ERR_UNSUPPORTED;
+  const bool want_dx = grad_hidden != nullptr;
+  const bool want_dw = grad_weight != nullptr;
+  const LmPlan pl = lm_plan(n_tokens, C, V, chunk_tokens, want_dw);
+  if (workspace_bytes < pl.total) return HLM_ERR_WORKSPACE;
+  if (!host_aligned16(workspace)) return HLM_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  __nv_bfloat16* logits = reinterpret_cast<__nv_bfloat16*>(ws + pl.off_logits);
+  float2* partial = reinterpret_cast<float2*>(ws + pl.off_partial);
+  float* tgt_logit = reinterpret_cast<float*>(ws + pl.off_tgt);
+  float* lse = reinterpret_cast<float*>(ws + pl.off_lse);
+  float* bsum = reinterpret_cast<float*>(ws + pl.off_bsum);
+  LmStats* stats = reinterpret_cast<LmStats*>(ws + pl.off_stats);
+  float* dw_acc = reinterpret_cast<float*>(ws + pl.off_dw);
+  int* err = device_error_ptr();
+  if (err == nullptr) return HLM_ERR_LAUNCH;
+
+  const __nv_bfloat16* H = static_cast<const __nv_bfloat16*>(hidden);
+  const __nv_bfloat16* W = static_cast<const __nv_bfloat16*>(weight);
+
+  lm_count_valid_kernel<<<1, 1024, 0, s>>>(targets, n_tokens, V, ignore_index, stats);
+  if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
+
+  // Tensor maps that do not depend on the chunk.
+  CUtensorMap map_w_k, map_w_n;
+  if (!encode_bf16_map(&map_w_k, W, C, V, C, kLmBN)) return HLM_ERR_DRIVER;  // B of logits GEMM
+  if (!encode_bf16_map(&map_w_n, W, C, V, C, 64)) return HLM_ERR_DRIVER;     // B of dX GEMM
+
+  for (int ci = 0; ci < pl.n_chunks; ++ci) {
+    const int64_t r0 = static_cast<int64_t>(ci) * pl.chunk;
+    const int rows = static_cast<int>(n_tokens - r0 < pl.chunk ? n_tokens - r0 : pl.chunk);
+    const __nv_bfloat16* Hc = H + r0 * C;
+    const int64_t* tc = targets + r0;
+    const bool last = ci == pl.n_chunks - 1;
+
+    // 1. logits + per-tile softmax statistics
+    {
+      CUtensorMap map_h;
+      if (!encode_bf16_map(&map_h, Hc, C, rows, C, kBM)) return HLM_ERR_DRIVER;
+      GemmParams p;
+      gemm_tiling(p, rows, static_cast<int>(V), static_cast<int>(C), kLmBN, 1);
+      p.err = err;
+      EpiLogitsLSE::Params ep;
+      ep.logits = logits;
+      ep.ld = V;
+      ep.partial = partial;
+      ep.tgt_logit = tgt_logit;
+      ep.targets = tc;
+      ep.V = static_cast<int>(V);
+      ep.rows = rows;
+      const int rc = launch_gemm_sm100<kLmBN, kLmStages, false, false, EpiLogitsLSE>(
+          map_h, map_h, map_h, map_w_k, p, ep, s);
+      if (rc != HLM_OK) return rc;
+    }
+    // 2. lse + loss
+    {
+      const int nb = (rows + 255) / 256;
+      lm_finalize_kernel<<<nb, 256, 0, s>>>(partial, pl.n_parts, tgt_logit, tc, rows, V,
+                                            ignore_index, lse, bsum);
+      lm_loss_reduce_kernel<<<1, 256, 0, s>>>(bsum, nb, stats, loss, last ? 1 : 0);
+      if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
+    }
+    if (!want_dx && !want_dw) continue;
+    // 3. dlogits in place
+    {
+      const int64_t vecs = static_cast<int64_t>(rows) * (V / 8);
+      int64_t blocks = (vecs + 255) / 256;
+      const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
+      if (blocks > cap) blocks = cap;
+      lm_dlogits_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(logits, lse, tc, rows, V,
+                                                                 ignore_index, stats);
+      if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
+    }
+    // 4. grad_hidden[chunk] = P @ W
+    if (want_dx) {
+      CUtensorMap map_p;
+      if (!encode_bf16_map(&map_p, logits, V, rows, V, kBM)) return HLM_ERR_DRIVER;
+      GemmParams p;
+      gemm_tiling(p, rows, static_cast<int>(C), static_cast<int>(V), kLmBN, 1);
+      p.err = err;
+      EpiStore::Params ep;
+      ep.d = static_cast<__nv_bfloat16*>(grad_hidden) + r0 * C;
+      ep.ldd = C;
+      ep.split_stride = 0;
+      ep.dtype = HLM_BF16;
+      ep.accumulate = 0;
+      ep.vec_ok = 1;
+      const int rc = launch_gemm_sm100<kLmBN, kLmStages, false, true, EpiStore>(
+          map_p, map_p, map_p, map_w_n, p, ep, s);
+      if (rc != HLM_OK) return rc;
+    }
+    // 5. grad_weight (+)= P^T @ H_chunk
+    if (want_dw) {
+      CUtensorMap map_pt, map_hn;
+      if (!encode_bf16_map(&map_pt, logits, V, rows, V, 64)) return HLM_ERR_DRIVER;
+      if (!encode_bf16_map(&map_hn, Hc, C, rows, C, 64)) return HLM_ERR_DRIVER;
+      GemmParams p;
+      gemm_tiling(p, static_cast<int>(V), static_cast<int>(C), rows, kLmBN, 1);
+      p.err = err;
+      EpiStore::Params ep;
+      ep.ldd = C;
+      ep.split_stride = 0;
+      ep.vec_ok = 1;
+      if (pl.n_chunks == 1) {
+        ep.d = grad_weight;
+        ep.dtype = HLM_BF16;
+        ep.accumulate = 0;
+      } else {
+        ep.d = dw_acc;
+        ep.dtype = HLM_F32;
+        ep.accumulate = ci > 0 ? 1 : 0;
+      }
+      const int rc = launch_gemm_sm100<kLmBN, kLmStages, true, true, EpiStore>(
+          map_pt, map_pt, map_pt, map_hn, p, ep, s);
+      if (rc != HLM_OK) return rc;
+    }
+  }
+  if (want_dw && pl.n_chunks > 1) {
+    const int64_t n = V * C;
+    int64_t blocks = (n + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
+    if (blocks > cap) blocks = cap;
+    f32_to_bf16_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
+        dw_acc, static_cast<__nv_bfloat16*>(grad_weight), n);
+    if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
+  }
+  return HLM_OK;
+}

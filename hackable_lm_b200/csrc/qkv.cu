@@ -1,0 +1,429 @@
+// Fused QKV projection + QK-norm + RoPE (forward) and its backward.
+//
+// Forward = one tcgen05 GEMM  qkv = X @ W_qkv^T  with BN = 128 = head_dim, so
+// each output tile is exactly one head of 128 token rows.  The epilogue owns
+// whole head rows (one row per thread): for q/k heads it computes the RMS
+// over the 128 fp32 accumulators, normalises, rotates the first rotary_dim
+// dims (rotate-half, cos/sin[t, d mod half]) and writes [B,T,H,D]; v heads are
+// written as they are.  This replaces the reference's GEMM -> bf16 qkv ->
+// strided split -> qk_norm_rope chain (model.py:92-99, 117-126;
+// kernels.py:446-503) with one pass over the output.
+//
+// Backward: a memory-bound kernel recovers the normalised vectors from the
+// saved outputs (inverse rotation) and the saved 1/rms, applies the
+// norm/RoPE backward (kernels.py:546-612) to produce dq_pre/dk_pre, then two
+// tcgen05 GEMMs read [dq_pre | dk_pre | dv] as one segmented operand:
+//   grad_x = [dq|dk|dv] @ W_qkv          (W read N-major)
+//   grad_w = [dq|dk|dv]^T @ X            (split-K, fp32 slabs, fixed-order sum)
+#include "gemm_sm100.cuh"
+
+namespace hlm {
+
+constexpr int kQkvD = 128;
+constexpr int kQkvStages = 6;
+constexpr int kDwBN = 256;
+constexpr int kDwStages = 4;
+constexpr int kDwTargetUnits = 2 * 148;
+
+template <int RD>
+struct EpiQKV {
+  struct Params {
+    __nv_bfloat16* q_out;
+    __nv_bfloat16* k_out;
+    __nv_bfloat16* v_out;
+    float* rstd;
+    const void* cosp;
+    const void* sinp;
+    int64_t cs_stride;
+    int cs_dtype;
+    int T, Hq, Hk;
+    float eps;
+  };
+  static constexpr int kSmemBytes = 0;
+
+  template <int BN>
+  static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t*, uint32_t taddr,
+                             int m_tile, int n_tile, int, int quad, int lane) {
+    static_assert(BN == kQkvD, "one head per tile");
+    const int row = m_tile * kBM + quad * 32 + lane;
+    const bool row_ok = row < p.M;
+    uint32_t r0[32], r1[32], r2[32], r3[32];
+    tmem_ld_32x32b_x32(taddr + 0u, r0);
+    tmem_ld_32x32b_x32(taddr + 32u, r1);
+    tmem_ld_32x32b_x32(taddr + 64u, r2);
+    tmem_ld_32x32b_x32(taddr + 96u, r3);
+    tmem_ld_wait();
+    float v[kQkvD];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      v[i] = __uint_as_float(r0[i]);
+      v[32 + i] = __uint_as_float(r1[i]);
+      v[64 + i] = __uint_as_float(r2[i]);
+      v[96 + i] = __uint_as_float(r3[i]);
+    }
+    const int head = n_tile;
+    const int nqk = ep.Hq + ep.Hk;
+    __nv_bfloat16* dst;
+    if (head < nqk) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kQkvD; ++i) ss = fmaf(v[i], v[i], ss);
+      const float inv = rsqrtf(ss * (1.0f / kQkvD) + ep.eps);
+#pragma unroll
+      for (int i = 0; i < kQkvD; ++i) v[i] *= inv;
+      if constexpr (RD > 0) {
+        if (row_ok) {
+          const int64_t t = row % ep.T;
+#pragma unroll
+          for (int i = 0; i < RD / 2; ++i) {
+            const float c = load_cs(ep.cosp, t * ep.cs_stride + i, ep.cs_dtype);
+            const float s = load_cs(ep.sinp, t * ep.cs_stride + i, ep.cs_dtype);
+            const float a = v[i], b = v[i + RD / 2];
+            v[i] = a * c - b * s;
+            v[i + RD / 2] = b * c + a * s;
+          }
+        }
+      }
+      if (row_ok) ep.rstd[static_cast<int64_t>(row) * nqk + head] = inv;
+      dst = head < ep.Hq
+                ? ep.q_out + (static_cast<int64_t>(row) * ep.Hq + head) * kQkvD
+                : ep.k_out + (static_cast<int64_t>(row) * ep.Hk + (head - ep.Hq)) * kQkvD;
+    } else {
+      dst = ep.v_out + (static_cast<int64_t>(row) * ep.Hk + (head - nqk)) * kQkvD;
+    }
+    if (row_ok) {
+#pragma unroll
+      for (int j = 0; j < kQkvD; j += 8) {
+        Vec16<__nv_bfloat16> o;
+        float f[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = v[j + i];
+        o.from_float(f);
+        st_global_v4(dst + j, o.raw);
+      }
+    }
+  }
+};
+
+// Backward of the norm + RoPE part, from saved outputs y and 1/rms.
+// 16 lanes per head vector (8 bf16 each), two head vectors per warp.
+__global__ void __launch_bounds__(256) qkv_norm_rope_bwd_kernel(
+    const __nv_bfloat16* __restrict__ q_out, const __nv_bfloat16* __restrict__ k_out,
+    const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ gq,
+    const __nv_bfloat16* __restrict__ gk, const void* __restrict__ cosp,
+    const void* __restrict__ sinp, int64_t cs_stride, int cs_dtype, __nv_bfloat16* __restrict__ dq,
+    __nv_bfloat16* __restrict__ dk, int64_t M, int T, int Hq, int Hk, int rd) {
+  constexpr int VEC = 8, LPH = kQkvD / VEC, HPW = 32 / LPH;
+  const int lane = threadIdx.x & 31;
+  const int slot = lane / LPH, li = lane % LPH;
+  const int H = Hq + Hk;
+  const int64_t total = M * H;
+  const int half = rd / 2;
+  const int d0 = li * VEC;
+  const int pdelta = half / VEC;
+  const int role = d0 < half ? 0 : (d0 < rd ? 1 : 2);
+  const int src_lane = role == 0 ? lane + pdelta : (role == 1 ? lane - pdelta : lane);
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (int64_t base_item = warp_id * HPW; base_item < total; base_item += warps_total * HPW) {
+    const int64_t item = base_item + slot;
+    const bool valid = item < total;
+    const int64_t m = valid ? item / H : 0;
+    const int h = valid ? static_cast<int>(item - m * H) : 0;
+    const bool is_q = h < Hq;
+    const int hh = is_q ? h : h - Hq;
+    const int64_t off = (m * (is_q ? Hq : Hk) + hh) * kQkvD + d0;
+    float y[VEC], g[VEC];
+    float inv = 0.0f;
+    if (valid) {
+      Vec16<__nv_bfloat16> yv, gv;
+      yv.raw = ld_global_nc_v4((is_q ? q_out : k_out) + off);
+      gv.raw = ld_global_nc_v4((is_q ? gq : gk) + off);
+      yv.to_float(y);
+      gv.to_float(g);
+      inv = rstd[m * H + h];
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) y[i] = g[i] = 0.0f;
+    }
+    float c[VEC], s[VEC];
+    if (role != 2 && valid) {
+      const int64_t t = m % T;
+      const int cb = role == 0 ? d0 : d0 - half;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        c[i] = load_cs(cosp, t * cs_stride + cb + i, cs_dtype);
+        s[i] = load_cs(sinp, t * cs_stride + cb + i, cs_dtype);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        c[i] = 1.0f;
+        s[i] = 0.0f;
+      }
+    }
+    float py[VEC], pg[VEC], z[VEC], gn[VEC];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      py[i] = __shfl_sync(0xffffffffu, y[i], src_lane);
+      pg[i] = __shfl_sync(0xffffffffu, g[i], src_lane);
+    }
+    float dot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      // inverse rotation (rotation by -theta) of the output and of its gradient
+      z[i] = role == 0 ? y[i] * c[i] + py[i] * s[i] : (role == 1 ? y[i] * c[i] - py[i] * s[i] : y[i]);
+      gn[i] = role == 0 ? g[i] * c[i] + pg[i] * s[i] : (role == 1 ? g[i] * c[i] - pg[i] * s[i] : g[i]);
+      dot += gn[i] * z[i];
+    }
+#pragma unroll
+    for (int o = LPH / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    dot *= 1.0f / kQkvD;
+    if (valid) {
+      float res[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) res[i] = inv * (gn[i] - z[i] * dot);
+      Vec16<__nv_bfloat16> o;
+      o.from_float(res);
+      st_global_v4((is_q ? dq : dk) + off, o.raw);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) splitk_reduce_bf16_kernel(const float* __restrict__ slabs,
+                                                                int splits, int64_t n,
+                                                                __nv_bfloat16* __restrict__ out) {
+  const int64_t nv = n / 4;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nv;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 acc = reinterpret_cast<const float4*>(slabs)[v];
+    for (int sidx = 1; sidx < splits; ++sidx) {
+      const float4 x = reinterpret_cast<const float4*>(slabs + static_cast<int64_t>(sidx) * n)[v];
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
+    }
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(out + v * 4);
+    o[0] = __floats2bfloat162_rn(acc.x, acc.y);
+    o[1] = __floats2bfloat162_rn(acc.z, acc.w);
+  }
+}
+
+static inline int qkv_dw_splits(int64_t tokens, int64_t nqkv, int64_t C) {
+  const int64_t tiles = ((nqkv + kBM - 1) / kBM) * ((C + kDwBN - 1) / kDwBN);
+  const int64_t kblocks = (tokens + kBK - 1) / kBK;
+  int64_t s = (kDwTargetUnits + tiles - 1) / tiles;
+  if (s > kblocks / 4) s = kblocks / 4;
+  if (s < 1) s = 1;
+  // gemm_tiling may merge splits; compute the effective count the same way
+  const int64_t kb_per = (kblocks + s - 1) / s;
+  return static_cast<int>((kblocks + kb_per - 1) / kb_per);
+}
+
+static inline size_t a256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+struct QkvBwdPlan {
+  int splits;
+  size_t off_dq, off_dk, off_slab, total;
+};
+
+static QkvBwdPlan qkv_bwd_plan(int64_t M, int64_t C, int64_t Hq, int64_t Hk) {
+  QkvBwdPlan pl;
+  const int64_t nqkv = (Hq + 2 * Hk) * kQkvD;
+  pl.splits = qkv_dw_splits(M, nqkv, C);
+  size_t off = 0;
+  pl.off_dq = off;
+  off = a256(off + static_cast<size_t>(M) * Hq * kQkvD * 2);
+  pl.off_dk = off;
+  off = a256(off + static_cast<size_t>(M) * Hk * kQkvD * 2);
+  pl.off_slab = off;
+  off = a256(off + static_cast<size_t>(pl.splits) * nqkv * C * 4);
+  pl.total = off;
+  return pl;
+}
+
+template <int RD>
+static int qkv_fwd_launch(const CUtensorMap& mx, const CUtensorMap& mw, const GemmParams& p,
+                          const typename EpiQKV<RD>::Params& ep, cudaStream_t s) {
+  return launch_gemm_sm100<kQkvD, kQkvStages, false, false, EpiQKV<RD>>(mx, mx, mx, mw, p, ep, s);
+}
+
+}  // namespace hlm
+
+using namespace hlm;
+
+extern "C" int hlm_qkv_rope_fwd(const void* x, const void* w_qkv, const void* cos, const void* sin,
+                                void* q_out, void* k_out, void* v_out, float* rstd, int64_t B,
+                                int64_t T, int64_t C, int64_t Hq, int64_t Hk, int64_t D,
+                                int64_t rotary_dim, int64_t cs_stride_t, int cs_dtype, float eps,
+                                void* stream) {
+  if (B < 0 || T <= 0 || C <= 0 || Hq <= 0 || Hk <= 0 || D <= 0) return HLM_ERR_INVALID_ARG;
+  if (D != kQkvD) return HLM_ERR_UNSUPPORTED;
+  const int64_t M = B * T;
+  if (M == 0) return HLM_OK;
+  if (x == nullptr || w_qkv == nullptr || q_out == nullptr || k_out == nullptr ||
+      v_out == nullptr || rstd == nullptr)
+    return HLM_ERR_INVALID_ARG;
+  if (rotary_dim > 0 && (cos == nullptr || sin == nullptr)) return HLM_ERR_INVALID_ARG;
+  if (C % 64 != 0 || M > (1ll << 31) - 256) return HLM_ERR_UNSUPPORTED;
+  if (cs_dtype != HLM_F32 && cs_dtype != HLM_BF16 && cs_dtype != HLM_F16) return HLM_ERR_UNSUPPORTED;
+  if (!host_aligned16(x) || !host_aligned16(w_qkv) || !host_aligned16(q_out) ||
+      !host_aligned16(k_out) || !host_aligned16(v_out))
+    return HLM_ERR_UNSUPPORTED;
+  const int64_t nqkv = (Hq + 2 * Hk) * kQkvD;
+  CUtensorMap mx, mw;
+  if (!encode_bf16_map(&mx, x, C, M, C, kBM)) return HLM_ERR_DRIVER;
+  if (!encode_bf16_map(&mw, w_qkv, C, nqkv, C, kQkvD)) return HLM_ERR_DRIVER;
+  GemmParams p;
+  gemm_tiling(p, static_cast<int>(M), static_cast<int>(nqkv), static_cast<int>(C), kQkvD, 1);
+  p.err = device_error_ptr();
+  if (p.err == nullptr) return HLM_ERR_LAUNCH;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define HLM_QKV_CASE(RDV)                                  \
+  case RDV: {                                              \
+    EpiQKV<RDV>::Params ep;                                \
+    ep.q_out = static_cast<__nv_bfloat16*>(q_out);         \
+    ep.k_out = static_cast<__nv_bfloat16*>(k_out);         \
+    ep.v_out = static_cast<__nv_bfloat16*>(v_out);         \
+    ep.rstd = rstd;                                        \
+    ep.cosp = cos;                                         \
+    ep.sinp = sin;                                         \
+    ep.cs_stride = cs_stride_t;                            \
+    ep.cs_dtype = cs_dtype;                                \
+    ep.T = static_cast<int>(T);                            \
+    ep.Hq = static_cast<int>(Hq);                          \
+    ep.Hk = static_cast<int>(Hk);                          \
+    ep.eps = eps;                                          \
+    return qkv_fwd_launch<RDV>(mx, mw, p, ep, s);          \
+  }
+  switch (rotary_dim) {
+    HLM_QKV_CASE(0)
+    HLM_QKV_CASE(16)
+    HLM_QKV_CASE(32)
+    HLM_QKV_CASE(64)
+    HLM_QKV_CASE(128)
+    default:
+      return HLM_ERR_UNSUPPORTED;
+  }
+#undef HLM_QKV_CASE
+}
+
+extern "C" size_t hlm_qkv_rope_bwd_workspace_bytes(int64_t B, int64_t T, int64_t C, int64_t Hq,
+                                                   int64_t Hk, int64_t D) {
+  (void)D;
+  if (B <= 0 || T <= 0 || C <= 0 || Hq <= 0 || Hk <= 0) return 256;
+  return qkv_bwd_plan(B * T, C, Hq, Hk).total;
+}
+
+extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_out,
+                                const void* k_out, const float* rstd, const void* cos,
+                                const void* sin, const void* grad_q, const void* grad_k,
+                                const void* grad_v, void* grad_x, void* grad_w, void* workspace,
+                                size_t workspace_bytes, int64_t B, int64_t T, int64_t C,
+                                int64_t Hq, int64_t Hk, int64_t D, int64_t rotary_dim,
+                                int64_t cs_stride_t, int cs_dtype, float eps, void* stream) {
+  (void)eps;
+  if (B < 0 || T <= 0 || C <= 0 || Hq <= 0 || Hk <= 0 || D <= 0) return HLM_ERR_INVALID_ARG;
+  if (D != kQkvD) return HLM_ERR_UNSUPPORTED;
+  if (rotary_dim < 0 || rotary_dim > D || (rotary_dim / 2) % 8 != 0 || (rotary_dim & 1))
+    return HLM_ERR_UNSUPPORTED;
+  const int64_t M = B * T;
+  if (M == 0) return HLM_OK;
+  if (x == nullptr || w_qkv == nullptr || q_out == nullptr || k_out == nullptr ||
+      rstd == nullptr || grad_q == nullptr || grad_k == nullptr || grad_v == nullptr ||
+      workspace == nullptr)
+    return HLM_ERR_INVALID_ARG;
+  if (rotary_dim > 0 && (cos == nullptr || sin == nullptr)) return HLM_ERR_INVALID_ARG;
+  if (C % 64 != 0 || M > (1ll << 31) - 256) return HLM_ERR_UNSUPPORTED;
+  if (cs_dtype != HLM_F32 && cs_dtype != HLM_BF16 && cs_dtype != HLM_F16) return HLM_ERR_UNSUPPORTED;
+  const void* ptrs[] = {x, w_qkv, q_out, k_out, grad_q, grad_k, grad_v, workspace};
+  for (const void* ptr : ptrs)
+    if (!host_aligned16(ptr)) return HLM_ERR_UNSUPPORTED;
+  if ((grad_x != nullptr && !host_aligned16(grad_x)) || (grad_w != nullptr && !host_aligned16(grad_w)))
+    return HLM_ERR_UNSUPPORTED;
+  const QkvBwdPlan pl = qkv_bwd_plan(M, C, Hq, Hk);
+  if (workspace_bytes < pl.total) return HLM_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(ws + pl.off_dq);
+  __nv_bfloat16* dk = reinterpret_cast<__nv_bfloat16*>(ws + pl.off_dk);
+  float* slabs = reinterpret_cast<float*>(ws + pl.off_slab);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* err = device_error_ptr();
+  if (err == nullptr) return HLM_ERR_LAUNCH;
+  const int64_t nqkv = (Hq + 2 * Hk) * kQkvD;
+
+  // 1. norm + RoPE backward -> dq_pre, dk_pre
+  {
+    const int64_t items = M * (Hq + Hk);
+    int64_t blocks = (items * 16 + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    qkv_norm_rope_bwd_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(q_out), static_cast<const __nv_bfloat16*>(k_out), rstd,
+        static_cast<const __nv_bfloat16*>(grad_q), static_cast<const __nv_bfloat16*>(grad_k), cos,
+        sin, cs_stride_t, cs_dtype, dq, dk, M, static_cast<int>(T), static_cast<int>(Hq),
+        static_cast<int>(Hk), static_cast<int>(rotary_dim));
+    if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
+  }
+  const int seg1 = static_cast<int>(Hq * kQkvD);
+  const int seg2 = static_cast<int>((Hq + Hk) * kQkvD);
+  // 2. grad_x = [dq|dk|dv] @ W_qkv
+  if (grad_x != nullptr) {
+    CUtensorMap a0, a1, a2, mb;
+    if (!encode_bf16_map(&a0, dq, Hq * kQkvD, M, Hq * kQkvD, kBM) ||
+        !encode_bf16_map(&a1, dk, Hk * kQkvD, M, Hk * kQkvD, kBM) ||
+        !encode_bf16_map(&a2, grad_v, Hk * kQkvD, M, Hk * kQkvD, kBM) ||
+        !encode_bf16_map(&mb, w_qkv, C, nqkv, C, 64))
+      return HLM_ERR_DRIVER;
+    GemmParams p;
+    gemm_tiling(p, static_cast<int>(M), static_cast<int>(C), static_cast<int>(nqkv), kDwBN, 1);
+    p.a_seg1 = seg1;
+    p.a_seg2 = seg2;
+    p.err = err;
+    EpiStore::Params ep;
+    ep.d = grad_x;
+    ep.ldd = C;
+    ep.split_stride = 0;
+    ep.dtype = HLM_BF16;
+    ep.accumulate = 0;
+    ep.vec_ok = 1;
+    const int rc = launch_gemm_sm100<kDwBN, kDwStages, false, true, EpiStore>(a0, a1, a2, mb, p, ep, s);
+    if (rc != HLM_OK) return rc;
+  }
+  // 3. grad_w = [dq|dk|dv]^T @ X   (split-K over tokens)
+  if (grad_w != nullptr) {
+    CUtensorMap a0, a1, a2, mb;
+    if (!encode_bf16_map(&a0, dq, Hq * kQkvD, M, Hq * kQkvD, 64) ||
+        !encode_bf16_map(&a1, dk, Hk * kQkvD, M, Hk * kQkvD, 64) ||
+        !encode_bf16_map(&a2, grad_v, Hk * kQkvD, M, Hk * kQkvD, 64) ||
+        !encode_bf16_map(&mb, x, C, M, C, 64))
+      return HLM_ERR_DRIVER;
+    GemmParams p;
+    gemm_tiling(p, static_cast<int>(nqkv), static_cast<int>(C), static_cast<int>(M), kDwBN,
+                pl.splits);
+    if (p.splits != pl.splits) return HLM_ERR_LAUNCH;
+    p.a_seg1 = seg1;
+    p.a_seg2 = seg2;
+    p.err = err;
+    EpiStore::Params ep;
+    ep.d = slabs;
+    ep.ldd = C;
+    ep.split_stride = nqkv * C;
+    ep.dtype = HLM_F32;
+    ep.accumulate = 0;
+    ep.vec_ok = 1;
+    const int rc = launch_gemm_sm100<kDwBN, kDwStages, true, true, EpiStore>(a0, a1, a2, mb, p, ep, s);
+    if (rc != HLM_OK) return rc;
+    const int64_t n = nqkv * C;
+    int64_t blocks = (n / 4 + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    splitk_reduce_bf16_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
+        slabs, pl.splits, n, static_cast<__nv_bfloat16*>(grad_w));
+    if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
+  }
+  return HLM_OK;
+}

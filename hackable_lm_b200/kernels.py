@@ -1,0 +1,298 @@
+"""Drop-in operator layer: the reference ``kernels.py`` entry points on sm_100a.
+
+The functions that hackable-lm's ``model.py`` and ``train.py`` call keep their
+names and signatures (kernels.py:126-972 in the reference), and route to the
+hand-written CUDA kernels of ``libhlm_b200.so`` through the custom operators in
+:mod:`hackable_lm_b200.ops`:
+
+=====================================  =========================================
+reference entry point                  B200 implementation
+=====================================  =========================================
+``swiglu_triton(gate_up)``             ``hackable_lm_b200::swiglu`` (+ backward)
+``qk_norm_rope_triton(q,k,cos,sin,e)`` ``hackable_lm_b200::qk_norm_rope``
+``fused_linear_cross_entropy_with_``   ``hackable_lm_b200::lm_head_ce`` (tcgen05
+``weight(h, W, bias, t, backend, c)``  logits GEMM + online LSE + dX/dW GEMMs)
+``rms_norm(x, weight, eps)``           ``hackable_lm_b200::rms_norm``
+``model.residual_rms_norm(r, b, eps)`` ``hackable_lm_b200::residual_rms_norm``
+=====================================  =========================================
+
+The module backend value ``"triton"`` is accepted as an alias of ``"b200"`` so
+that reference configs and command lines select the new path unchanged.  The
+new path has no CPU fallback: CPU tensors raise.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import asdict, dataclass
+from typing import Any
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+from .config import MODULE_BACKEND_FIELDS, MODULE_BACKENDS, normalize_attention_backend
+
+B200_MODULE_BACKENDS = frozenset(MODULE_BACKEND_FIELDS)
+# Reference name kept for callers that import it (kernels.py:49-53); on this
+# path every module backend field has a B200 implementation.
+TRITON_MODULE_BACKENDS = B200_MODULE_BACKENDS
+
+
+@dataclass
+class KernelInfo:
+    requested_backend: str
+    attention_backend: str
+    qkv_backend: str
+    output_backend: str
+    gate_up_backend: str
+    down_backend: str
+    lm_head_backend: str
+    torch_compile: bool
+    torch_compile_mode: str
+    torch_compile_capture_scalar_outputs: bool
+    precision: str
+    b200_library: str
+    b200_library_version: int
+
+    def to_dict(self) -> dict[str, Any]:
+        return asdict(self)
+
+
+def _cuda_only(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(
+            f"{what}: the hackable_lm_b200 path runs only on CUDA (sm_100a) tensors; "
+            "use the 'torch' module backend for CPU runs"
+        )
+
+
+def resolve_kernel_backends(
+    requested: str,
+    precision: str,
+    compile_model: bool,
+    compile_mode: str = "default",
+    compile_capture_scalar_outputs: bool = True,
+    attention_backend: str = "sdpa",
+    allow_torch_backend: bool = False,
+    **module_backends: str,
+) -> KernelInfo:
+    """Validate backend names the way the reference does (kernels.py:146-242).
+
+    Module backends resolve to ``"torch"`` or ``"b200"`` (``"triton"`` is an
+    alias of ``"b200"``).  Requesting ``"b200"`` loads the CUDA library and
+    fails loudly if it is missing.
+    """
+    from . import _lib
+
+    requested = requested.lower()
+    if requested != "torch":
+        raise ValueError(f"unknown kernel backend {requested!r}")
+    unknown = set(module_backends) - set(MODULE_BACKEND_FIELDS)
+    if unknown:
+        raise ValueError(f"unknown module backend fields {sorted(unknown)!r}")
+    resolved = {}
+    for name in MODULE_BACKEND_FIELDS:
+        value = module_backends.get(name, "torch")
+        if not isinstance(value, str):
+            raise ValueError(f"unknown {name} {value!r}")
+        backend = value.lower()
+        if backend not in MODULE_BACKENDS:
+            raise ValueError(f"unknown {name} {backend!r}")
+        resolved[name] = "b200" if backend == "triton" else backend
+    attention = normalize_attention_backend(attention_backend)
+    if precision != "bf16" and not allow_torch_backend:
+        raise RuntimeError(f"unsupported precision mode {precision!r}; the training fast path uses bf16")
+    lib_version = 0
+    lib_path = str(_lib.LIB_PATH)
+    if any(v == "b200" for v in resolved.values()):
+        lib_version = int(_lib.load().hlm_version())
+    return KernelInfo(
+        requested_backend=requested,
+        attention_backend=attention,
+        **resolved,
+        torch_compile=compile_model,
+        torch_compile_mode=compile_mode,
+        torch_compile_capture_scalar_outputs=compile_capture_scalar_outputs,
+        precision=precision,
+        b200_library=lib_path,
+        b200_library_version=lib_version,
+    )
+
+
+def compile_training_model(model: torch.nn.Module, enabled: bool, mode: str = "default",
+                           capture_scalar_outputs: bool = True) -> torch.nn.Module:
+    """torch.compile wrapper with the reference's settings (kernels.py:126-137)."""
+    if not enabled:
+        return model
+    import torch._dynamo
+
+    torch._dynamo.config.capture_scalar_outputs = capture_scalar_outputs
+    return torch.compile(model, mode=None if mode == "default" else mode, dynamic=False, fullgraph=True)
+
+
+def mark_compiled_step_begin(enabled: bool) -> None:
+    if enabled:
+        torch.compiler.cudagraph_mark_step_begin()
+
+
+# ---------------------------------------------------------------------------
+# Hot-path entry points
+# ---------------------------------------------------------------------------
+def rms_norm(x: torch.Tensor, weight: torch.Tensor | None, eps: float) -> torch.Tensor:
+    """x * rsqrt(mean(x^2) + eps) [* weight]  (kernels.py:245-247)."""
+    _cuda_only(x, "rms_norm")
+    return ops.rms_norm(x, weight, eps)
+
+
+def residual_rms_norm(residual: torch.Tensor, branch: torch.Tensor, eps: float,
+                      weight: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(residual + branch, rms_norm(residual + branch))  (model.py:73-75)."""
+    _cuda_only(branch, "residual_rms_norm")
+    return ops.residual_rms_norm(residual, branch, weight, eps)
+
+
+def swiglu_triton(gate_up: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up on the packed [..., 2H] projection (kernels.py:743-753)."""
+    if gate_up.shape[-1] % 2:
+        raise RuntimeError(f"SwiGLU input last dimension must be even, got {gate_up.shape[-1]}")
+    _cuda_only(gate_up, "swiglu")
+    return ops.swiglu(gate_up)
+
+
+def qk_norm_rope_triton(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                        eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """Weightless RMSNorm over head_dim, then partial rotate-half RoPE (kernels.py:756-771)."""
+    _cuda_only(q, "qk_norm_rope")
+    if cos.shape[-1] % 2:
+        raise RuntimeError(f"rotary dim must be even, got {cos.shape[-1]}")
+    return ops.qk_norm_rope(q, k, cos, sin, eps)
+
+
+def qkv_projection_rope(x: torch.Tensor, w_qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                        n_head: int, n_kv_head: int, eps: float
+                        ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Fused x @ w_qkv^T + head split + QK-norm + RoPE (QKVProjection, model.py:92-126).
+
+    Runs as one tcgen05 GEMM with the norm/RoPE in its epilogue when
+    head_dim == 128 and rotary_dim is 0/16/32/64/128; otherwise as the tcgen05
+    GEMM followed by the standalone qk_norm_rope kernel.
+    """
+    _cuda_only(x, "qkv_projection_rope")
+    B, T, C = x.shape
+    head_dim = w_qkv.shape[0] // (n_head + 2 * n_kv_head)
+    rd = cos.shape[-1]
+    if ops.fused_qkv_supported(head_dim, rd, C) and x.dtype == torch.bfloat16:
+        q, k, v, _ = ops.qkv_rope(x, w_qkv, cos, sin, n_head, n_kv_head, eps)
+        return q, k, v
+    qkv = F.linear(x, w_qkv)
+    q_dim, kv_dim = n_head * head_dim, n_kv_head * head_dim
+    q, k, v = qkv.split((q_dim, kv_dim, kv_dim), dim=-1)
+    q = q.view(B, T, n_head, head_dim)
+    k = k.view(B, T, n_kv_head, head_dim)
+    v = v.view(B, T, n_kv_head, head_dim)
+    q, k = ops.qk_norm_rope(q, k, cos.reshape(1, T, 1, rd), sin.reshape(1, T, 1, rd), eps)
+    return q, k, v
+
+
+class _B200FusedLinearCrossEntropy(torch.autograd.Function):
+    """Forward computes loss, dX and dW in one library call; backward only
+    rescales the saved gradients by grad_output (kernels.py:878-942)."""
+
+    @staticmethod
+    def forward(ctx, hidden, weight, targets, ignore_index, requested_chunk_size):
+        if requested_chunk_size is not None and requested_chunk_size < 0:
+            raise RuntimeError(f"loss_chunk_size must be nonnegative, got {requested_chunk_size}")
+        need_dx = hidden.requires_grad
+        need_dw = weight.requires_grad
+        loss, gx, gw = ops.lm_head_ce(hidden, weight, targets, int(ignore_index), 0, need_dx, need_dw)
+        ctx.save_for_backward(gx if need_dx else None, gw if need_dw else None)
+        ctx.need = (need_dx, need_dw)
+        return loss
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        gx, gw = ctx.saved_tensors
+        need_dx, need_dw = ctx.need
+        if need_dx and ctx.needs_input_grad[0]:
+            ops.scale_(gx, grad_output)
+        else:
+            gx = None
+        if need_dw and ctx.needs_input_grad[1]:
+            ops.scale_(gw, grad_output)
+        else:
+            gw = None
+        return gx, gw, None, None, None
+
+
+def fused_linear_cross_entropy_with_weight(hidden: torch.Tensor, weight: torch.Tensor,
+                                           bias: torch.Tensor | None, targets: torch.Tensor,
+                                           backend: str, chunk_size: int | None = None,
+                                           ignore_index: int = -100) -> torch.Tensor:
+    """Mean cross-entropy of hidden @ weight^T against targets (kernels.py:945-959).
+
+    Rows whose target equals ``ignore_index`` contribute neither loss nor
+    gradient, and the mean runs over the remaining rows (F.cross_entropy
+    semantics).  ``chunk_size`` is validated as in the reference; the library
+    sizes its own token chunks from a memory budget, which changes only the
+    order of floating-point accumulation, not the result.
+    """
+    if backend not in {"triton", "b200"}:
+        raise RuntimeError(f"unsupported fused linear cross entropy backend {backend!r}")
+    if bias is not None:
+        raise RuntimeError("the B200 fused LM head has no bias term (the model uses bias=False)")
+    hidden_flat = hidden.reshape(-1, hidden.size(-1))
+    targets_flat = targets.reshape(-1).contiguous()
+    _cuda_only(hidden_flat, "fused_linear_cross_entropy")
+    return _B200FusedLinearCrossEntropy.apply(hidden_flat, weight, targets_flat, ignore_index, chunk_size)
+
+
+def scaled_dot_product_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dropout_p: float,
+                                 is_causal: bool = True, attn_mask: torch.Tensor | None = None,
+                                 window_size: int | None = None, backend: str = "sdpa") -> torch.Tensor:
+    """Attention core on [B, H, T, D] tensors.
+
+    ``"sdpa"`` uses torch.nn.functional.scaled_dot_product_attention (the
+    attention core named by the benchmark configuration); ``"torch"`` is the
+    reference's explicit softmax formulation (kernels.py:785-800).
+    """
+    if backend == "sdpa":
+        if window_size is not None and attn_mask is None:
+            T = q.shape[-2]
+            pos = torch.arange(T, device=q.device)
+            dist = pos[:, None] - pos[None, :]
+            attn_mask = (dist >= 0) & (dist < window_size)
+            is_causal = False
+        return F.scaled_dot_product_attention(q, k, v, attn_mask=attn_mask, dropout_p=dropout_p,
+                                              is_causal=is_causal and attn_mask is None)
+    if backend == "torch":
+        scale = 1.0 / math.sqrt(q.shape[-1])
+        attn = torch.matmul(q, k.transpose(-2, -1)) * scale
+        if is_causal:
+            q_len, kv_len = q.shape[-2], k.shape[-2]
+            causal = torch.ones((q_len, kv_len), device=q.device, dtype=torch.bool).tril()
+            attn = attn.masked_fill(~causal, float("-inf"))
+        if attn_mask is not None:
+            if attn_mask.dtype == torch.bool:
+                attn = attn.masked_fill(~attn_mask, float("-inf"))
+            else:
+                attn = attn + attn_mask
+        attn = torch.softmax(attn.float(), dim=-1).to(dtype=q.dtype)
+        if dropout_p:
+            attn = F.dropout(attn, p=dropout_p, training=True)
+        return torch.matmul(attn, v)
+    raise RuntimeError(f"unsupported attention backend {backend!r}")
+
+
+def apply_precision_policy(model: torch.nn.Module, precision: str,
+                           allow_torch_backend: bool = False) -> torch.nn.Module:
+    """Cast floating parameters (and grads) to bf16 (kernels.py:962-972)."""
+    if precision == "bf16":
+        for param in model.parameters():
+            if param.is_floating_point():
+                param.data = param.data.to(dtype=torch.bfloat16)
+                if param.grad is not None:
+                    param.grad.data = param.grad.data.to(dtype=torch.bfloat16)
+        return model
+    if precision in {"fp32_test", "bf16_test"} and allow_torch_backend:
+        return model
+    raise RuntimeError(f"unsupported precision mode {precision!r}; the training fast path uses bf16")

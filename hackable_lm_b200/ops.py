@@ -1,0 +1,504 @@
+"""PyTorch custom operators over the libhlm_b200 C ABI.
+
+Every operator here is a ``torch.library.custom_op`` in the
+``hackable_lm_b200`` namespace with a fake (meta) implementation, so it stays
+opaque and shape-correct under ``torch.compile(fullgraph=True)`` and CUDA
+graph capture.  Outputs and workspaces are allocated by PyTorch's caching
+allocator; the CUDA library itself never allocates, never synchronises, and
+launches on the current stream of the tensor's device.
+
+There is no CPU path: a CPU tensor raises.  The reference's CPU behaviour is
+restated separately (test-only) for parity checking.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import HLM_BF16, HLM_F16, HLM_F32, check
+
+_DTYPE_CODE = {torch.float32: HLM_F32, torch.bfloat16: HLM_BF16, torch.float16: HLM_F16}
+
+
+def _code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dtype]
+    except KeyError:
+        raise RuntimeError(f"hackable_lm_b200: unsupported dtype {dtype}") from None
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    for t in tensors:
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                "hackable_lm_b200 operators run only on CUDA tensors (sm_100a); got a tensor on "
+                f"{t.device}"
+            )
+        if t.device != dev:
+            raise RuntimeError("hackable_lm_b200: all tensors must be on the same device")
+    return dev
+
+
+def _stream(dev: torch.device) -> int:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if torch.cuda.current_device() != idx:
+        torch.cuda.set_device(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _lib_():
+    return _lib.load()
+
+
+# ---------------------------------------------------------------------------
+# SwiGLU  (reference: kernels.py:343-419, 685-700, 743-753)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("hackable_lm_b200::swiglu", mutates_args=())
+def swiglu(gate_up: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(gate_up)
+    gate_up = gate_up.contiguous()
+    hidden = gate_up.shape[-1] // 2
+    rows = gate_up.numel() // max(1, 2 * hidden)
+    out = torch.empty((*gate_up.shape[:-1], hidden), dtype=gate_up.dtype, device=dev)
+    check(_lib_().hlm_swiglu_fwd(_ptr(gate_up), _ptr(out), rows, hidden, _code(gate_up.dtype),
+                                  _stream(dev)), "hlm_swiglu_fwd")
+    return out
+
+
+@swiglu.register_fake
+def _swiglu_fake(gate_up):
+    return gate_up.new_empty((*gate_up.shape[:-1], gate_up.shape[-1] // 2))
+
+
+@torch.library.custom_op("hackable_lm_b200::swiglu_backward", mutates_args=())
+def swiglu_backward(gate_up: torch.Tensor, grad_out: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(gate_up, grad_out)
+    gate_up = gate_up.contiguous()
+    grad_out = grad_out.contiguous()
+    hidden = grad_out.shape[-1]
+    rows = grad_out.numel() // max(1, hidden)
+    grad = torch.empty_like(gate_up)
+    check(_lib_().hlm_swiglu_bwd(_ptr(gate_up), _ptr(grad_out), _ptr(grad), rows, hidden,
+                                  _code(gate_up.dtype), _stream(dev)), "hlm_swiglu_bwd")
+    return grad
+
+
+@swiglu_backward.register_fake
+def _swiglu_backward_fake(gate_up, grad_out):
+    return torch.empty_like(gate_up)
+
+
+def _swiglu_setup(ctx, inputs, output):
+    (gate_up,) = inputs
+    ctx.save_for_backward(gate_up)
+
+
+def _swiglu_bwd(ctx, grad_out):
+    if grad_out is None:
+        return None
+    (gate_up,) = ctx.saved_tensors
+    return swiglu_backward(gate_up, grad_out)
+
+
+swiglu.register_autograd(_swiglu_bwd, setup_context=_swiglu_setup)
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm / residual-add + RMSNorm  (reference: model.py:14-16, 73-75; kernels.py:245-247)
+# ---------------------------------------------------------------------------
+def _rows_cols(x: torch.Tensor) -> tuple[int, int]:
+    cols = x.shape[-1]
+    return (x.numel() // cols if cols else 0), cols
+
+
+@torch.library.custom_op("hackable_lm_b200::rms_norm", mutates_args=())
+def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float) -> torch.Tensor:
+    dev = _require_cuda(x) if weight is None else _require_cuda(x, weight)
+    x = x.contiguous()
+    w = None if weight is None else weight.to(x.dtype).contiguous()
+    rows, cols = _rows_cols(x)
+    norm = torch.empty_like(x)
+    check(_lib_().hlm_residual_rms_norm_fwd(None, _ptr(x), _ptr(w), None, _ptr(norm), rows, cols,
+                                             float(eps), _code(x.dtype), _stream(dev)),
+          "hlm_residual_rms_norm_fwd")
+    return norm
+
+
+@rms_norm.register_fake
+def _rms_norm_fake(x, weight, eps):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("hackable_lm_b200::residual_rms_norm", mutates_args=())
+def residual_rms_norm(residual: torch.Tensor, branch: torch.Tensor, weight: Optional[torch.Tensor],
+                      eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    tensors = [residual, branch] + ([] if weight is None else [weight])
+    dev = _require_cuda(*tensors)
+    if residual.shape != branch.shape or residual.dtype != branch.dtype:
+        raise RuntimeError("residual_rms_norm: residual and branch must match in shape and dtype")
+    residual = residual.contiguous()
+    branch = branch.contiguous()
+    w = None if weight is None else weight.to(branch.dtype).contiguous()
+    rows, cols = _rows_cols(branch)
+    out = torch.empty_like(branch)
+    norm = torch.empty_like(branch)
+    check(_lib_().hlm_residual_rms_norm_fwd(_ptr(residual), _ptr(branch), _ptr(w), _ptr(out),
+                                             _ptr(norm), rows, cols, float(eps),
+                                             _code(branch.dtype), _stream(dev)),
+          "hlm_residual_rms_norm_fwd")
+    return out, norm
+
+
+@residual_rms_norm.register_fake
+def _residual_rms_norm_fake(residual, branch, weight, eps):
+    return torch.empty_like(branch), torch.empty_like(branch)
+
+
+@torch.library.custom_op("hackable_lm_b200::rms_norm_backward", mutates_args=())
+def rms_norm_backward(x: torch.Tensor, weight: Optional[torch.Tensor],
+                      grad_out: Optional[torch.Tensor], grad_norm: torch.Tensor,
+                      eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(x, grad_norm)
+    x = x.contiguous()
+    grad_norm = grad_norm.contiguous()
+    go = None if grad_out is None else grad_out.contiguous()
+    w = None if weight is None else weight.to(x.dtype).contiguous()
+    rows, cols = _rows_cols(x)
+    grad = torch.empty_like(x)
+    if w is not None:
+        gw = torch.empty(cols, dtype=x.dtype, device=dev)
+        nbytes = _lib_().hlm_rms_norm_bwd_workspace_bytes(rows, cols)
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+    else:
+        gw = torch.empty(0, dtype=x.dtype, device=dev)
+        nbytes = 0
+        ws = None
+    check(_lib_().hlm_residual_rms_norm_bwd(_ptr(x), _ptr(w), _ptr(go), _ptr(grad_norm),
+                                             _ptr(grad), _ptr(gw) if w is not None else None,
+                                             _ptr(ws), nbytes, rows, cols, float(eps),
+                                             _code(x.dtype), _stream(dev)),
+          "hlm_residual_rms_norm_bwd")
+    return grad, gw
+
+
+@rms_norm_backward.register_fake
+def _rms_norm_backward_fake(x, weight, grad_out, grad_norm, eps):
+    cols = x.shape[-1]
+    return torch.empty_like(x), x.new_empty(cols if weight is not None else 0)
+
+
+def _rms_norm_setup(ctx, inputs, output):
+    x, weight, eps = inputs
+    ctx.save_for_backward(x, weight)
+    ctx.eps = eps
+
+
+def _rms_norm_bwd(ctx, grad_norm):
+    x, weight = ctx.saved_tensors
+    if grad_norm is None:
+        return None, None, None
+    gx, gw = rms_norm_backward(x, weight, None, grad_norm, ctx.eps)
+    return gx, (gw.to(weight.dtype) if weight is not None else None), None
+
+
+rms_norm.register_autograd(_rms_norm_bwd, setup_context=_rms_norm_setup)
+
+
+def _residual_rms_norm_setup(ctx, inputs, output):
+    residual, branch, weight, eps = inputs
+    out, _ = output
+    ctx.save_for_backward(out, weight)
+    ctx.eps = eps
+
+
+def _residual_rms_norm_bwd(ctx, grad_out, grad_norm):
+    out, weight = ctx.saved_tensors
+    if grad_norm is None:
+        if grad_out is None:
+            return None, None, None, None
+        return grad_out, grad_out, (torch.zeros_like(weight) if weight is not None else None), None
+    g, gw = rms_norm_backward(out, weight, grad_out, grad_norm, ctx.eps)
+    return g, g, (gw.to(weight.dtype) if weight is not None else None), None
+
+
+residual_rms_norm.register_autograd(_residual_rms_norm_bwd, setup_context=_residual_rms_norm_setup)
+
+
+# ---------------------------------------------------------------------------
+# QK-norm + RoPE  (reference: kernels.py:446-658, 679-682, 711-735, 756-771)
+# ---------------------------------------------------------------------------
+def _cos_sin_2d(cos: torch.Tensor, sin: torch.Tensor, seq_len: int) -> tuple[torch.Tensor, torch.Tensor, int]:
+    rd = cos.shape[-1]
+    c = cos.reshape(seq_len, rd)
+    s = sin.reshape(seq_len, rd)
+    if c.stride(1) != 1 or s.stride(1) != 1 or c.stride(0) != s.stride(0):
+        c = c.contiguous()
+        s = s.contiguous()
+    return c, s, c.stride(0)
+
+
+def _orient_cos(cos: torch.Tensor, sin: torch.Tensor, q: torch.Tensor):
+    # Accept [1,1,T,rd] as well as [1,T,1,rd] (kernels.py:766-768).
+    if cos.ndim == 4 and cos.shape[1] != q.shape[1] and cos.shape[2] == q.shape[1]:
+        cos = cos.transpose(1, 2)
+        sin = sin.transpose(1, 2)
+    return cos, sin
+
+
+@torch.library.custom_op("hackable_lm_b200::qk_norm_rope", mutates_args=())
+def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                 eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(q, k, cos, sin)
+    B, T, Hq, D = q.shape
+    Hk = k.shape[2]
+    cos, sin = _orient_cos(cos, sin, q)
+    rd = cos.shape[-1]
+    c2, s2, cstride = _cos_sin_2d(cos, sin, T)
+    q_out = torch.empty((B, T, Hq, D), dtype=q.dtype, device=dev)
+    k_out = torch.empty((B, T, Hk, D), dtype=k.dtype, device=dev)
+    check(_lib_().hlm_qk_norm_rope_fwd(
+        _ptr(q), _ptr(k), _ptr(c2), _ptr(s2), _ptr(q_out), _ptr(k_out), B, T, Hq, Hk, D, rd,
+        _lib.int64_array(q.stride()), _lib.int64_array(k.stride()), cstride, _code(c2.dtype),
+        float(eps), _code(q.dtype), _stream(dev)), "hlm_qk_norm_rope_fwd")
+    return q_out, k_out
+
+
+@qk_norm_rope.register_fake
+def _qk_norm_rope_fake(q, k, cos, sin, eps):
+    return q.new_empty(q.shape), k.new_empty(k.shape)
+
+
+@torch.library.custom_op("hackable_lm_b200::qk_norm_rope_backward", mutates_args=())
+def qk_norm_rope_backward(q: torch.Tensor, k: torch.Tensor, grad_q: torch.Tensor,
+                          grad_k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                          eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(q, k, grad_q, grad_k, cos, sin)
+    B, T, Hq, D = q.shape
+    Hk = k.shape[2]
+    cos, sin = _orient_cos(cos, sin, q)
+    rd = cos.shape[-1]
+    c2, s2, cstride = _cos_sin_2d(cos, sin, T)
+    grad_q = grad_q.contiguous()
+    grad_k = grad_k.contiguous()
+    gq = torch.empty((B, T, Hq, D), dtype=q.dtype, device=dev)
+    gk = torch.empty((B, T, Hk, D), dtype=k.dtype, device=dev)
+    check(_lib_().hlm_qk_norm_rope_bwd(
+        _ptr(q), _ptr(k), _ptr(grad_q), _ptr(grad_k), _ptr(c2), _ptr(s2), _ptr(gq), _ptr(gk),
+        B, T, Hq, Hk, D, rd, _lib.int64_array(q.stride()), _lib.int64_array(k.stride()), cstride,
+        _code(c2.dtype), float(eps), _code(q.dtype), _stream(dev)), "hlm_qk_norm_rope_bwd")
+    return gq, gk
+
+
+@qk_norm_rope_backward.register_fake
+def _qk_norm_rope_backward_fake(q, k, grad_q, grad_k, cos, sin, eps):
+    return q.new_empty(q.shape), k.new_empty(k.shape)
+
+
+def _qk_setup(ctx, inputs, output):
+    q, k, cos, sin, eps = inputs
+    ctx.save_for_backward(q, k, cos, sin)
+    ctx.eps = eps
+
+
+def _qk_bwd(ctx, grad_q, grad_k):
+    q, k, cos, sin = ctx.saved_tensors
+    if grad_q is None:
+        grad_q = torch.zeros(q.shape, dtype=q.dtype, device=q.device)
+    if grad_k is None:
+        grad_k = torch.zeros(k.shape, dtype=k.dtype, device=k.device)
+    gq, gk = qk_norm_rope_backward(q, k, grad_q, grad_k, cos, sin, ctx.eps)
+    return gq, gk, None, None, None
+
+
+qk_norm_rope.register_autograd(_qk_bwd, setup_context=_qk_setup)
+
+
+# ---------------------------------------------------------------------------
+# Fused QKV projection + QK-norm + RoPE  (reference: model.py:78-126)
+# ---------------------------------------------------------------------------
+FUSED_QKV_ROTARY_DIMS = (0, 16, 32, 64, 128)
+FUSED_QKV_HEAD_DIM = 128
+
+
+def fused_qkv_supported(head_dim: int, rotary_dim: int, n_embd: int) -> bool:
+    return head_dim == FUSED_QKV_HEAD_DIM and rotary_dim in FUSED_QKV_ROTARY_DIMS and n_embd % 64 == 0
+
+
+@torch.library.custom_op("hackable_lm_b200::qkv_rope", mutates_args=())
+def qkv_rope(x: torch.Tensor, w_qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+             n_head: int, n_kv_head: int, eps: float
+             ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(x, w_qkv, cos, sin)
+    if x.dtype != torch.bfloat16 or w_qkv.dtype != torch.bfloat16:
+        raise RuntimeError("qkv_rope: x and w_qkv must be bfloat16")
+    B, T, C = x.shape
+    D = w_qkv.shape[0] // (n_head + 2 * n_kv_head)
+    rd = cos.shape[-1]
+    c2, s2, cstride = _cos_sin_2d(cos, sin, T)
+    x = x.contiguous()
+    w = w_qkv.contiguous()
+    q = torch.empty((B, T, n_head, D), dtype=x.dtype, device=dev)
+    k = torch.empty((B, T, n_kv_head, D), dtype=x.dtype, device=dev)
+    v = torch.empty((B, T, n_kv_head, D), dtype=x.dtype, device=dev)
+    rstd = torch.empty((B * T, n_head + n_kv_head), dtype=torch.float32, device=dev)
+    check(_lib_().hlm_qkv_rope_fwd(
+        _ptr(x), _ptr(w), _ptr(c2), _ptr(s2), _ptr(q), _ptr(k), _ptr(v), _ptr(rstd), B, T, C,
+        n_head, n_kv_head, D, rd, cstride, _code(c2.dtype), float(eps), _stream(dev)),
+        "hlm_qkv_rope_fwd")
+    return q, k, v, rstd
+
+
+@qkv_rope.register_fake
+def _qkv_rope_fake(x, w_qkv, cos, sin, n_head, n_kv_head, eps):
+    B, T, C = x.shape
+    D = w_qkv.shape[0] // (n_head + 2 * n_kv_head)
+    return (x.new_empty((B, T, n_head, D)), x.new_empty((B, T, n_kv_head, D)),
+            x.new_empty((B, T, n_kv_head, D)),
+            x.new_empty((B * T, n_head + n_kv_head), dtype=torch.float32))
+
+
+@torch.library.custom_op("hackable_lm_b200::qkv_rope_backward", mutates_args=())
+def qkv_rope_backward(x: torch.Tensor, w_qkv: torch.Tensor, q: torch.Tensor, k: torch.Tensor,
+                      rstd: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                      grad_q: torch.Tensor, grad_k: torch.Tensor, grad_v: torch.Tensor,
+                      n_head: int, n_kv_head: int, eps: float, need_dx: bool, need_dw: bool
+                      ) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(x, w_qkv, q, k, rstd, grad_q, grad_k, grad_v)
+    B, T, C = x.shape
+    D = q.shape[-1]
+    rd = cos.shape[-1]
+    c2, s2, cstride = _cos_sin_2d(cos, sin, T)
+    grad_q = grad_q.contiguous()
+    grad_k = grad_k.contiguous()
+    grad_v = grad_v.contiguous()
+    gx = torch.empty_like(x) if need_dx else x.new_empty(0)
+    gw = torch.empty_like(w_qkv) if need_dw else w_qkv.new_empty(0)
+    nbytes = _lib_().hlm_qkv_rope_bwd_workspace_bytes(B, T, C, n_head, n_kv_head, D)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    check(_lib_().hlm_qkv_rope_bwd(
+        _ptr(x.contiguous()), _ptr(w_qkv.contiguous()), _ptr(q), _ptr(k), _ptr(rstd), _ptr(c2),
+        _ptr(s2), _ptr(grad_q), _ptr(grad_k), _ptr(grad_v), _ptr(gx) if need_dx else None,
+        _ptr(gw) if need_dw else None, _ptr(ws), nbytes, B, T, C, n_head, n_kv_head, D, rd,
+        cstride, _code(c2.dtype), float(eps), _stream(dev)), "hlm_qkv_rope_bwd")
+    return gx, gw
+
+
+@qkv_rope_backward.register_fake
+def _qkv_rope_backward_fake(x, w_qkv, q, k, rstd, cos, sin, grad_q, grad_k, grad_v, n_head,
+                            n_kv_head, eps, need_dx, need_dw):
+    return (torch.empty_like(x) if need_dx else x.new_empty(0),
+            torch.empty_like(w_qkv) if need_dw else w_qkv.new_empty(0))
+
+
+def _qkv_setup(ctx, inputs, output):
+    x, w_qkv, cos, sin, n_head, n_kv_head, eps = inputs
+    q, k, v, rstd = output
+    ctx.save_for_backward(x, w_qkv, q, k, rstd, cos, sin)
+    ctx.n_head = n_head
+    ctx.n_kv_head = n_kv_head
+    ctx.eps = eps
+
+
+def _qkv_bwd(ctx, grad_q, grad_k, grad_v, grad_rstd):
+    x, w_qkv, q, k, rstd, cos, sin = ctx.saved_tensors
+    need_dx, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+    if not (need_dx or need_dw):
+        return None, None, None, None, None, None, None
+    if grad_q is None:
+        grad_q = torch.zeros_like(q)
+    if grad_k is None:
+        grad_k = torch.zeros_like(k)
+    if grad_v is None:
+        grad_v = torch.zeros(k.shape, dtype=k.dtype, device=k.device)
+    gx, gw = qkv_rope_backward(x, w_qkv, q, k, rstd, cos, sin, grad_q, grad_k, grad_v,
+                               ctx.n_head, ctx.n_kv_head, ctx.eps, need_dx, need_dw)
+    return (gx if need_dx else None), (gw if need_dw else None), None, None, None, None, None
+
+
+qkv_rope.register_autograd(_qkv_bwd, setup_context=_qkv_setup)
+
+
+# ---------------------------------------------------------------------------
+# Fused LM head + cross-entropy  (reference: kernels.py:872-959)
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("hackable_lm_b200::lm_head_ce", mutates_args=())
+def lm_head_ce(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
+               ignore_index: int, chunk_tokens: int, need_dx: bool, need_dw: bool
+               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(hidden, weight, targets)
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise RuntimeError("lm_head_ce: hidden and weight must be bfloat16")
+    hidden = hidden.contiguous()
+    weight = weight.contiguous()
+    targets = targets.to(torch.int64).contiguous()
+    n, C = hidden.shape
+    V = weight.shape[0]
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    gx = torch.empty_like(hidden) if need_dx else hidden.new_empty(0)
+    gw = torch.empty_like(weight) if need_dw else weight.new_empty(0)
+    nbytes = _lib_().hlm_lm_head_ce_workspace_bytes(n, C, V, chunk_tokens)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    check(_lib_().hlm_lm_head_ce(
+        _ptr(hidden), _ptr(weight), _ptr(targets), _ptr(loss), _ptr(gx) if need_dx else None,
+        _ptr(gw) if need_dw else None, _ptr(ws), nbytes, n, C, V, int(ignore_index),
+        int(chunk_tokens), _stream(dev)), "hlm_lm_head_ce")
+    return loss, gx, gw
+
+
+@lm_head_ce.register_fake
+def _lm_head_ce_fake(hidden, weight, targets, ignore_index, chunk_tokens, need_dx, need_dw):
+    return (hidden.new_empty((), dtype=torch.float32),
+            torch.empty_like(hidden) if need_dx else hidden.new_empty(0),
+            torch.empty_like(weight) if need_dw else weight.new_empty(0))
+
+
+@torch.library.custom_op("hackable_lm_b200::scale_", mutates_args=("x",))
+def scale_(x: torch.Tensor, scale: torch.Tensor) -> None:
+    dev = _require_cuda(x, scale)
+    if not x.is_contiguous():
+        raise RuntimeError("scale_: tensor must be contiguous")
+    s = scale.to(torch.float32).contiguous()
+    check(_lib_().hlm_scale_by_device_scalar(_ptr(x), _ptr(s), x.numel(), _code(x.dtype),
+                                              _stream(dev)), "hlm_scale_by_device_scalar")
+
+
+@scale_.register_fake
+def _scale_fake(x, scale):
+    return None
+
+
+# ---------------------------------------------------------------------------
+# Plain tcgen05 GEMM (building block, used by tests and the bench)
+# ---------------------------------------------------------------------------
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn_major: bool = False, b_mn_major: bool = False,
+         out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.bfloat16,
+         accumulate: bool = False) -> torch.Tensor:
+    """D = A @ B^T on the tensor cores.
+
+    a: [M, K] (or [K, M] with a_mn_major), b: [N, K] (or [K, N] with b_mn_major),
+    both bf16 row-major contiguous.  Returns D [M, N] in out_dtype (bf16/fp32).
+    """
+    dev = _require_cuda(a, b)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise RuntimeError("gemm: operands must be bfloat16")
+    a = a.contiguous()
+    b = b.contiguous()
+    M, K = (a.shape[1], a.shape[0]) if a_mn_major else (a.shape[0], a.shape[1])
+    N = b.shape[1] if b_mn_major else b.shape[0]
+    Kb = b.shape[0] if b_mn_major else b.shape[1]
+    if K != Kb:
+        raise RuntimeError(f"gemm: K mismatch {K} vs {Kb}")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=dev)
+    check(_lib_().hlm_gemm_bf16(
+        _ptr(a), _ptr(b), _ptr(out), M, N, K, int(a_mn_major), int(b_mn_major), a.shape[1],
+        b.shape[1], out.stride(0), _code(out.dtype), int(accumulate), _stream(dev)),
+        "hlm_gemm_bf16")
+    return out

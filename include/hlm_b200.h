@@ -1,0 +1,215 @@
+/*
+ * hlm_b200.h -- C ABI of the hackable-lm B200 operator library (libhlm_b200.so).
+ *
+ * Hand-written sm_100a CUDA kernels for the fused operator hot path of
+ * hackable-lm: residual-add + RMSNorm, QKV projection + QK-norm + RoPE,
+ * SwiGLU, and the fused LM-head + cross-entropy loss, each forward and
+ * backward.
+ *
+ * Conventions (every entry point):
+ *   - All tensor arguments are DEVICE pointers owned by the caller.  The
+ *     library never allocates or frees device memory; where a kernel needs
+ *     scratch memory the caller passes a workspace whose size comes from the
+ *     matching *_workspace_bytes() query.
+ *   - `stream` is a cudaStream_t passed as void*; work is enqueued on it and
+ *     nothing synchronises the host.
+ *   - Return value: HLM_OK (0) or a negative HLM_ERR_* code.  Nothing traps,
+ *     exits or throws across this boundary.  hlm_strerror() names a code.
+ *   - dtype codes: HLM_F32, HLM_BF16, HLM_F16.  The tensor-core paths
+ *     (QKV, LM head, GEMM) take bf16 operands.
+ *   - Kernels that wait on other warps bound every wait; a wait that runs out
+ *     records a code in a device error word read by hlm_device_error_get().
+ *
+ * Reference citations are paths inside the hackable-lm repository.
+ */
+#ifndef HLM_B200_H_
+#define HLM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HLM_OK 0
+#define HLM_ERR_INVALID_ARG (-1)  /* null pointer, negative size, bad rank */
+#define HLM_ERR_UNSUPPORTED (-2)  /* shape / dtype / stride / alignment not supported */
+#define HLM_ERR_LAUNCH (-3)       /* CUDA launch or runtime error */
+#define HLM_ERR_WORKSPACE (-4)    /* workspace smaller than required */
+#define HLM_ERR_DRIVER (-5)       /* driver entry point / tensor-map encode failed */
+
+#define HLM_F32 0
+#define HLM_BF16 1
+#define HLM_F16 2
+
+/* Library version (major*10000 + minor*100 + patch). */
+int hlm_version(void);
+
+/* Static string naming an HLM_* return code. */
+const char* hlm_strerror(int code);
+
+/* Copy the device error word (0 = none) to *out; synchronises `stream`.
+ * Test and diagnostics use only. */
+int hlm_device_error_get(int* out, void* stream);
+
+/* Reset the device error word to 0 (stream-ordered). */
+int hlm_device_error_clear(void* stream);
+
+/* ------------------------------------------------------------------------
+ * SwiGLU
+ * ------------------------------------------------------------------------ */
+
+/* out[r, j] = silu(gate_up[r, j]) * gate_up[r, hidden + j]
+ * gate_up: contiguous [rows, 2*hidden]; out: contiguous [rows, hidden].
+ * Replaces torch.ops.hackable_lm.swiglu (kernels.py:388-402) and its
+ * Triton kernel _swiglu_kernel (kernels.py:343-358). */
+int hlm_swiglu_fwd(const void* gate_up, void* out, int64_t rows, int64_t hidden, int dtype,
+                   void* stream);
+
+/* grad_gate_up[r, j]          = g * up * s * (1 + gate * (1 - s))
+ * grad_gate_up[r, hidden + j] = g * gate * s,   s = sigmoid(gate)
+ * Replaces torch.ops.hackable_lm.swiglu_backward (kernels.py:404-419) and
+ * _swiglu_backward_kernel (kernels.py:365-386). */
+int hlm_swiglu_bwd(const void* gate_up, const void* grad_out, void* grad_gate_up, int64_t rows,
+                   int64_t hidden, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Residual add + RMSNorm
+ * ------------------------------------------------------------------------ */
+
+/* out  = residual + branch                      (rounded to dtype)
+ * norm = out * rsqrt(mean(out^2) + eps) [* weight]
+ * residual may be NULL: then x = branch, `out` is not written, and the call
+ * is the plain RMSNorm of kernels.rms_norm (kernels.py:245-247) /
+ * model.rms_norm_torch (model.py:14-16).  weight may be NULL (weightless,
+ * as in the model).  All row-major contiguous [rows, cols].
+ * Replaces model.residual_rms_norm (model.py:73-75). */
+int hlm_residual_rms_norm_fwd(const void* residual, const void* branch, const void* weight,
+                              void* out, void* norm, int64_t rows, int64_t cols, float eps,
+                              int dtype, void* stream);
+
+/* Backward of hlm_residual_rms_norm_fwd, given the saved pre-norm x (= out).
+ *   grad_in = grad_out + r*(g*w) - x*r^3*mean((g*w)*x),   r = rsqrt(mean(x^2)+eps)
+ * grad_out may be NULL (treated as zero).  grad_in receives the gradient of
+ * both residual and branch.  If weight != NULL, grad_weight[cols] (dtype) is
+ * written = sum_rows g * x * r, reduced deterministically through `workspace`
+ * (fp32, hlm_rms_norm_bwd_workspace_bytes bytes). */
+int hlm_residual_rms_norm_bwd(const void* x, const void* weight, const void* grad_out,
+                              const void* grad_norm, void* grad_in, void* grad_weight,
+                              void* workspace, size_t workspace_bytes, int64_t rows,
+                              int64_t cols, float eps, int dtype, void* stream);
+size_t hlm_rms_norm_bwd_workspace_bytes(int64_t rows, int64_t cols);
+
+/* ------------------------------------------------------------------------
+ * QK-norm + partial rotate-half RoPE (standalone, strided inputs)
+ * ------------------------------------------------------------------------ */
+
+/* For every head vector x of q [B,T,Hq,D] and k [B,T,Hk,D] (element strides
+ * q_strides[4], k_strides[4], any layout):
+ *   z = x * rsqrt(mean(x^2) + eps)
+ *   out[d]        = z[d]*c[d] - z[d+h]*s[d]      for d <  h = rotary_dim/2
+ *   out[d]        = z[d]*c[d-h] + z[d-h]*s[d-h]  for h <= d < rotary_dim
+ *   out[d]        = z[d]                         for d >= rotary_dim
+ * with c/s = cos/sin[t, .] ([T, rotary_dim] tables of which only the first
+ * half is read, as in _apply_partial_rope (kernels.py:670-676); row stride
+ * cs_stride_t, dtype cs_dtype).  q_out/k_out are contiguous [B,T,H,D] in `dtype`.
+ * Replaces torch.ops.hackable_lm.qk_norm_rope (kernels.py:505-539) and
+ * _qk_norm_rope_kernel (kernels.py:446-503). */
+int hlm_qk_norm_rope_fwd(const void* q, const void* k, const void* cos, const void* sin,
+                         void* q_out, void* k_out, int64_t B, int64_t T, int64_t Hq, int64_t Hk,
+                         int64_t D, int64_t rotary_dim, const int64_t* q_strides,
+                         const int64_t* k_strides, int64_t cs_stride_t, int cs_dtype, float eps,
+                         int dtype, void* stream);
+
+/* Backward: g_n = inverse rotation of the output gradient, then
+ * dx = inv * (g_n - z * mean(g_n * z)).  q/k are the saved pre-norm inputs
+ * (strided as above); grad_q/grad_k and the results are contiguous.
+ * Replaces torch.ops.hackable_lm.qk_norm_rope_backward (kernels.py:614-658)
+ * and _qk_norm_rope_backward_kernel (kernels.py:546-612). */
+int hlm_qk_norm_rope_bwd(const void* q, const void* k, const void* grad_q, const void* grad_k,
+                         const void* cos, const void* sin, void* grad_q_in, void* grad_k_in,
+                         int64_t B, int64_t T, int64_t Hq, int64_t Hk, int64_t D,
+                         int64_t rotary_dim, const int64_t* q_strides, const int64_t* k_strides,
+                         int64_t cs_stride_t, int cs_dtype, float eps, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Fused QKV projection + QK-norm + RoPE (tcgen05 GEMM, head-split epilogue)
+ * ------------------------------------------------------------------------ */
+
+/* x [B*T, C] bf16 (row-major), w_qkv [(Hq+2*Hk)*D, C] bf16 (nn.Linear
+ * layout).  Computes qkv = x @ w_qkv^T in fp32 on the tensor cores and, per
+ * 128-wide head tile in the epilogue: q/k heads -> RMSNorm over D + RoPE
+ * (position t = row mod T) -> q_out/k_out; v heads -> v_out.  Outputs are
+ * contiguous [B,T,H,D] bf16.  rstd [B*T, Hq+Hk] fp32 receives the per-head
+ * 1/rms used by the backward.  D must be 128.
+ * Replaces QKVProjection._project + fwd_triton (model.py:92-99, 117-126). */
+int hlm_qkv_rope_fwd(const void* x, const void* w_qkv, const void* cos, const void* sin,
+                     void* q_out, void* k_out, void* v_out, float* rstd, int64_t B, int64_t T,
+                     int64_t C, int64_t Hq, int64_t Hk, int64_t D, int64_t rotary_dim,
+                     int64_t cs_stride_t, int cs_dtype, float eps, void* stream);
+
+/* Backward of hlm_qkv_rope_fwd.  From the saved outputs q_out/k_out and
+ * rstd, recovers the normalised vectors, applies the norm/RoPE backward to
+ * grad_q/grad_k (contiguous [B,T,H,D] bf16), then computes on the tensor
+ * cores grad_x = [dq|dk|dv] @ w_qkv and grad_w = [dq|dk|dv]^T @ x.
+ * grad_x or grad_w may be NULL (not needed).  Workspace bytes from
+ * hlm_qkv_rope_bwd_workspace_bytes.
+ * Replaces the autograd backward of QKVProjection.fwd_triton: view/split
+ * backward + _qk_norm_rope_backward (kernels.py:711-735) + the qkv_proj
+ * nn.Linear dgrad/wgrad. */
+int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_out, const void* k_out,
+                     const float* rstd, const void* cos, const void* sin, const void* grad_q,
+                     const void* grad_k, const void* grad_v, void* grad_x, void* grad_w,
+                     void* workspace, size_t workspace_bytes, int64_t B, int64_t T, int64_t C,
+                     int64_t Hq, int64_t Hk, int64_t D, int64_t rotary_dim, int64_t cs_stride_t,
+                     int cs_dtype, float eps, void* stream);
+size_t hlm_qkv_rope_bwd_workspace_bytes(int64_t B, int64_t T, int64_t C, int64_t Hq, int64_t Hk,
+                                        int64_t D);
+
+/* ------------------------------------------------------------------------
+ * Fused LM head + cross-entropy (forward and backward in one call)
+ * ------------------------------------------------------------------------ */
+
+/* hidden [n_tokens, C] bf16, weight [V, C] bf16, targets [n_tokens] int64.
+ * Rows whose target equals ignore_index contribute no loss and no gradient;
+ * the loss is the mean over the other rows (F.cross_entropy semantics with
+ * ignore_index).  Writes the scalar loss (fp32, device) and, when non-NULL,
+ * grad_hidden [n_tokens, C] and grad_weight [V, C] (bf16) = d(loss)/d(.).
+ * Logits are produced tile by tile on the tensor cores; full fp32 logits are
+ * never materialised.  chunk_tokens bounds the token rows processed per
+ * pass (0 = choose automatically); the workspace size depends on it.
+ * Replaces _TritonFusedLinearCrossEntropy.forward (kernels.py:878-931) and
+ * _linear_ce_kernel (kernels.py:291-318). */
+int hlm_lm_head_ce(const void* hidden, const void* weight, const int64_t* targets, float* loss,
+                   void* grad_hidden, void* grad_weight, void* workspace, size_t workspace_bytes,
+                   int64_t n_tokens, int64_t C, int64_t V, int64_t ignore_index,
+                   int64_t chunk_tokens, void* stream);
+size_t hlm_lm_head_ce_workspace_bytes(int64_t n_tokens, int64_t C, int64_t V,
+                                      int64_t chunk_tokens);
+
+/* data[i] *= *scale for i < n (scale is a device fp32 scalar).  Backward of
+ * the fused LM head, replacing _scale_saved_grad (kernels.py:872-875). */
+int hlm_scale_by_device_scalar(void* data, const float* scale, int64_t n, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Plain tcgen05 GEMM (building block; also used by tests)
+ * ------------------------------------------------------------------------ */
+
+/* D[M,N] = A[M,K] * B[N,K]^T (+ D if accumulate), bf16 operands, fp32
+ * accumulation.  A is K-major (row-major [M][lda]) unless a_mn_major, in
+ * which case it is stored [K][lda] with M contiguous; likewise B is
+ * [N][ldb] (K-major) or [K][ldb] (N-major).  D is row-major [M][ldd] of
+ * d_dtype (HLM_BF16 or HLM_F32).  Leading dimensions must be multiples of
+ * 8 elements and base pointers 16-byte aligned.
+ * Replaces the cuBLAS GEMMs under nn.Linear / torch.mm on this path
+ * (model.py:94; kernels.py:913, 920, 922). */
+int hlm_gemm_bf16(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K,
+                  int a_mn_major, int b_mn_major, int64_t lda, int64_t ldb, int64_t ldd,
+                  int d_dtype, int accumulate, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HLM_B200_H_ */
