@@ -1,0 +1,483 @@
+#!/usr/bin/env python
+"""Benchmark of the hackable-lm fused-operator hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload lm_head|d12]
+
+Prints ONE JSON line (rank 0).  For N > 1 launch one process per GPU with
+torch.distributed.run; timing is on the device (CUDA events), bracketed by a
+barrier + synchronize, and the max over ranks is reported.
+
+Workloads (synthetic, seeded):
+  lm_head  fused LM-head + cross-entropy forward+backward, hidden [32768,768],
+           W [32768,768], 2% targets = ignore_index -1 (one step = one call on
+           one batch).  With N > 1 each rank processes its own batch and the
+           bf16 grad_weight is all-reduced (data-parallel exchange).
+  d12      depth-12 decoder training step (see hackable_lm_b200.train).
+
+--impl reference times the reference algorithm's CPU implementation (the
+oracle restatement, all host threads) on a bounded sample of the same
+workload and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:  # noqa: BLE001
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def traffic_table() -> dict:
+    """DRAM bytes per launch from committed ncu summaries (profiles/ncu_traffic.txt):
+    lines "<workload> <kernel> <bytes_per_launch> <note...>"."""
+    out = {}
+    p = ROOT / "profiles" / "ncu_traffic.txt"
+    if p.exists():
+        for line in p.read_text().splitlines():
+            parts = line.split()
+            if len(parts) >= 3 and not line.startswith("#"):
+                try:
+                    out[(parts[0], parts[1])] = float(parts[2])
+                except ValueError:
+                    pass
+    return out
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.enabled = self.world > 1
+
+    def init(self, backend="nccl"):
+        if self.enabled and not dist.is_initialized():
+            import datetime
+
+            if backend == "nccl":
+                torch.cuda.set_device(self.local_rank)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+
+    def barrier(self):
+        if self.enabled:
+            dist.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.enabled:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.enabled and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.dev), "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cuda_time(fn, steps: int, warmup: int, d: Dist, flush=None):
+    """Run warmup steps, then time exactly `steps` steps with CUDA events,
+    bracketed by barrier + synchronize; returns (max-over-ranks total ms)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    d.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        if flush is not None:
+            flush()
+        fn()
+    stop.record()
+    torch.cuda.synchronize()
+    d.barrier()
+    torch.cuda.synchronize()
+    return d.max(start.elapsed_time(stop))
+
+
+# ---------------------------------------------------------------------------
+# LM head workload
+# ---------------------------------------------------------------------------
+LM = {"M": 32768, "C": 768, "V": 32768, "ignore_frac": 0.02, "ignore_index": -1}
+
+
+def lm_inputs(seed: int, device):
+    g = torch.Generator().manual_seed(seed)
+    M, C, V = LM["M"], LM["C"], LM["V"]
+    hidden = torch.randn(M, C, generator=g).to(torch.bfloat16)
+    weight = (torch.randn(V, C, generator=g) * 0.02).to(torch.bfloat16)
+    targets = torch.randint(0, V, (M,), generator=g)
+    targets[torch.randperm(M, generator=g)[: int(LM["ignore_frac"] * M)]] = LM["ignore_index"]
+    return hidden, weight, targets
+
+
+def lm_cpu_sample(n_tokens: int, seed: int = 0):
+    import oracle
+
+    hidden, weight, targets = lm_inputs(seed, "cpu")
+    h = hidden[:n_tokens].float()
+    w = weight.float()
+    t = targets[:n_tokens]
+    t0 = time.perf_counter()
+    oracle.lm_head_ce(h, w, t, LM["ignore_index"], 4096)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_lm(target_seconds: float = 15.0) -> dict:
+    torch.set_num_threads(os.cpu_count() or 1)
+    n = 256
+    lm_cpu_sample(n)  # warm-up
+    dt = lm_cpu_sample(n)
+    per_rep = max(1.0, target_seconds / 3)
+    n = int(min(8192, max(256, n * per_rep / max(dt, 1e-3))) // 256 * 256)
+    times = [lm_cpu_sample(n) for _ in range(3)]
+    med = statistics.median(times)
+    return {"value": n / med, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"oracle (torch CPU fp32) LM-head+CE fwd+bwd on {n} of the 32768 tokens, full "
+                      f"V=32768, C=768; median of 3 reps ({med:.2f} s each)"}
+
+
+def bench_lm_head(args, d: Dist, device) -> dict:
+    from hackable_lm_b200 import _lib, kernels
+
+    peaks, peak_src = load_peaks()
+    hidden, weight, targets = lm_inputs(1000 + d.rank, device)
+    h = hidden.to(device).requires_grad_(True)
+    w = weight.to(device).requires_grad_(True)
+    t = targets.to(device)
+    M, C, V = LM["M"], LM["C"], LM["V"]
+
+    def step():
+        loss = kernels.fused_linear_cross_entropy_with_weight(h, w, None, t, "b200",
+                                                              ignore_index=LM["ignore_index"])
+        gh, gw = torch.autograd.grad(loss, (h, w))
+        if d.enabled:
+            dist.all_reduce(gw)
+        return loss
+
+    # ---- device-timed value, with the library timing its own kernels
+    clocks = ClockSampler(device.index)
+    kernels_to_time = ("lm_logits", "lm_dlogits", "lm_dx", "lm_dw")
+    timers = {k: _lib.KernelTimer(k, args.steps) for k in kernels_to_time}
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks.start()
+    n0 = _lib.launch_count()
+    for k in kernels_to_time:
+        timers[k].__enter__()
+    total_ms = cuda_time(step, args.steps, 0, d)
+    for k in kernels_to_time:
+        timers[k].__exit__(None, None, None)
+    launches = _lib.launch_count() - n0
+    clk = clocks.stop()
+    ms_per_step = total_ms / args.steps
+    value = M * d.world / (ms_per_step / 1e3)
+
+    kt = {k: timers[k].times_ms() for k in kernels_to_time}
+    flops = {"lm_logits": 2.0 * M * C * V, "lm_dx": 2.0 * M * C * V, "lm_dw": 2.0 * M * C * V}
+    bytes_ = {"lm_dlogits": 4.0 * M * V}  # bf16 logits read + dlogits written in place
+    breakdown = {}
+    for k, ts in kt.items():
+        if not ts:
+            continue
+        avg = sum(ts) / len(ts)
+        entry = {"ms": round(avg, 4), "share_of_step": round(avg / ms_per_step, 4)}
+        if k in flops:
+            entry["tflops"] = round(flops[k] / (avg / 1e3) / 1e12, 1)
+        if k in bytes_:
+            entry["gbs"] = round(bytes_[k] / (avg / 1e3) / 1e9, 1)
+        breakdown[k] = entry
+    dominant = max(kt, key=lambda k: (sum(kt[k]) / max(1, len(kt[k]))) if kt[k] else 0.0)
+    dom_avg = sum(kt[dominant]) / len(kt[dominant])
+    tr = traffic_table().get(("lm_head", dominant))
+    if dominant in flops:
+        achieved = flops[dominant] / (dom_avg / 1e3) / 1e12
+        peak = peaks["bf16_tflops"]
+        roofline = {"kernel": dominant, "bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                    "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": tr,
+                    "peak_source": f"{peak_src} bf16_tflops (burst: kernel timed inside a ~5 ms step)",
+                    "algorithmic_per_launch": f"2*M*C*V = {flops[dominant]:.4e} FLOP"}
+    else:
+        achieved = bytes_[dominant] / (dom_avg / 1e3) / 1e9
+        peak = peaks["hbm_gbs"]
+        roofline = {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                    "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": tr,
+                    "peak_source": f"{peak_src} hbm_gbs"}
+
+    # ---- end to end through the public API with host-resident inputs
+    h_host = hidden.pin_memory()
+    t_host = targets.pin_memory()
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    h_dev = torch.empty_like(h)
+    t_dev = torch.empty_like(t)
+
+    def e2e_step():
+        h_dev.copy_(h_host, non_blocking=True)
+        t_dev.copy_(t_host, non_blocking=True)
+        hd = h_dev.requires_grad_(True)
+        loss = kernels.fused_linear_cross_entropy_with_weight(hd, w, None, t_dev, "b200",
+                                                              ignore_index=LM["ignore_index"])
+        gh, gw = torch.autograd.grad(loss, (hd, w))
+        if d.enabled:
+            dist.all_reduce(gw)
+        loss_host.copy_(loss.detach(), non_blocking=True)
+        hd.requires_grad_(False)
+
+    e2e_ms = cuda_time(e2e_step, args.steps, args.warmup, d) / args.steps
+    e2e = {"value": M * d.world / (e2e_ms / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": h_host.numel() * 2 + t_host.numel() * 8, "d2h_bytes_per_step": 4,
+           "ms_per_step": round(e2e_ms, 4)}
+
+    out = {
+        "metric": "LM-head+CE fwd/bwd tokens/s", "value": value, "unit": "tokens/s", "n_gpus": d.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: hidden~N(0,1), W~N(0,0.02), uniform targets, 2% ignore_index=-1 (seeded)",
+        "config": {"workload": f"lm_head_ce C4: hidden [{M},{C}] x W [{V},{C}], fwd+bwd",
+                   "tokens_per_gpu": M, "hidden": C, "vocab": V, "ignore_index": -1,
+                   "parallelism": f"dp{d.world} (grad_weight all-reduce)" if d.enabled else "single GPU",
+                   "l2": "working set per step ~2.2 GB (bf16 logits) >> 126 MB L2; no flush"},
+        "roofline": roofline, "kernel_breakdown": breakdown, "e2e": e2e, "gpu_launches": launches,
+        "gpu_launches_per_step": launches / args.steps, "clocks": clk,
+    }
+    return out
+
+
+# ---------------------------------------------------------------------------
+# per-operator roofline measurements (rank 0, after the headline)
+# ---------------------------------------------------------------------------
+def bench_ops(device, iters: int = 20) -> dict:
+    from hackable_lm_b200 import kernels, ops
+
+    import oracle
+
+    peaks, _ = load_peaks()
+    flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
+
+    def timed(fn, n=iters):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(n):
+            flush_buf.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            total += a.elapsed_time(b)
+        return total / n
+
+    res = {}
+
+    def hbm(name, fn, nbytes):
+        ms = timed(fn)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "bytes": nbytes,
+                     "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4)}
+
+    def tensor(name, fn, flop):
+        ms = timed(fn)
+        tf = flop / (ms / 1e3) / 1e12
+        res[name] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1), "flop": flop,
+                     "frac_of_bf16": round(tf / peaks["bf16_tflops"], 4)}
+
+    g = torch.Generator().manual_seed(0)
+    gu = torch.randn(16384, 4096, generator=g).to(torch.bfloat16).to(device)
+    go = torch.randn(16384, 2048, generator=g).to(torch.bfloat16).to(device)
+    hbm("swiglu_fwd [16384,4096]", lambda: ops.swiglu(gu), 201_326_592)
+    hbm("swiglu_bwd [16384,4096]", lambda: ops.swiglu_backward(gu, go), 335_544_320)
+    del gu, go
+    x = torch.randn(32768, 768, generator=g).to(torch.bfloat16).to(device)
+    r = torch.randn(32768, 768, generator=g).to(torch.bfloat16).to(device)
+    gn = torch.randn(32768, 768, generator=g).to(torch.bfloat16).to(device)
+    hbm("residual_rmsnorm_fwd [32768,768]", lambda: ops.residual_rms_norm(r, x, None, 1e-6), 201_326_592)
+    hbm("rmsnorm_bwd [32768,768]", lambda: ops.rms_norm_backward(x, None, r, gn, 1e-6), 201_326_592)
+    del x, r, gn
+    B, T, H, D = 8, 2048, 6, 128
+    q = torch.randn(B, T, H, D, generator=g).to(torch.bfloat16).to(device)
+    k = torch.randn(B, T, H, D, generator=g).to(torch.bfloat16).to(device)
+    cos, sin = oracle.rope_tables(D, T, 10_000.0, 0.25, dtype=torch.bfloat16)
+    cos = cos.transpose(1, 2).to(device)
+    sin = sin.transpose(1, 2).to(device)
+    dq = torch.randn_like(q)
+    dk = torch.randn_like(k)
+    hbm("qk_norm_rope_fwd [8,2048,6,128]", lambda: ops.qk_norm_rope(q, k, cos, sin, 1e-6), 100_663_296)
+    hbm("qk_norm_rope_bwd [8,2048,6,128]", lambda: ops.qk_norm_rope_backward(q, k, dq, dk, cos, sin, 1e-6),
+        150_994_944)
+    xq = torch.randn(8, 2048, 768, generator=g).to(torch.bfloat16).to(device)
+    wq = (torch.randn(2304, 768, generator=g) * 0.02).to(torch.bfloat16).to(device)
+    c1, s1 = oracle.rope_tables(D, T, 10_000.0, 0.25, dtype=torch.bfloat16)
+    c1, s1 = c1.to(device), s1.to(device)
+    tensor("qkv_rope_fwd X[16384,768] W[2304,768]", lambda: ops.qkv_rope(xq, wq, c1, s1, 6, 6, 1e-6),
+           57_982_058_496)
+    qo, ko, vo, rs = ops.qkv_rope(xq, wq, c1, s1, 6, 6, 1e-6)
+    gv = torch.randn_like(vo)
+    tensor("qkv_rope_bwd (dX+dW)", lambda: ops.qkv_rope_backward(xq, wq, qo, ko, rs, c1, s1, dq, dk, gv, 6, 6,
+                                                                 1e-6, True, True), 115_964_116_992)
+    del flush_buf
+    return res
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference algorithm on the host cores
+# ---------------------------------------------------------------------------
+def run_reference(args, d: Dist) -> dict | None:
+    if d.rank != 0:
+        return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    if args.workload == "lm_head":
+        n = args.ref_tokens
+        for _ in range(args.warmup):
+            lm_cpu_sample(n)
+        times = [lm_cpu_sample(n) for _ in range(args.steps)]
+        total = sum(times)
+        value = n * args.steps / total
+        sample = (f"oracle (torch CPU fp32) LM-head+CE fwd+bwd, {n} tokens per step of the 32768-token "
+                  "batch, full V=32768, C=768")
+        metric = "LM-head+CE fwd/bwd tokens/s"
+        cfg = {"workload": "lm_head_ce C4: hidden [32768,768] x W [32768,768], fwd+bwd",
+               "tokens_per_gpu": LM["M"], "hidden": LM["C"], "vocab": LM["V"], "ignore_index": -1}
+    else:
+        from hackable_lm_b200 import train as tr
+
+        value, total, sample = tr.reference_cpu_steps(args.steps, args.warmup)
+        metric = "d12 step tok/s"
+        cfg = tr.bench_config(1)
+    ms = total / args.steps * 1e3
+    return {"impl": "reference", "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": d.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded)", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--workload", choices=("lm_head", "d12"), default="lm_head")
+    ap.add_argument("--no-ops", action="store_true", help="skip the per-operator section")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-tokens", type=int, default=1024, help="tokens per reference-arm step")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="override the LM-head token count (smaller cases for ncu captures)")
+    args = ap.parse_args()
+    if args.tokens is not None:
+        LM["M"] = args.tokens
+    if args.warmup < 3 and args.impl == "b200":
+        ap.error("--warmup must be >= 3")
+
+    d = Dist()
+    if args.impl == "reference":
+        d.init(backend="gloo")
+        out = run_reference(args, d)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        d.close()
+        return
+
+    d.init()
+    device = torch.device("cuda", d.local_rank)
+    torch.cuda.set_device(device)
+    if args.workload == "lm_head":
+        out = bench_lm_head(args, d, device)
+    else:
+        from hackable_lm_b200 import train as tr
+
+        out = tr.bench_d12(args, d, device, cuda_time, ClockSampler, load_peaks, traffic_table)
+    if d.rank == 0:
+        if not args.no_ops and d.world == 1:
+            out["ops"] = bench_ops(device)
+        if not args.no_cpu_baseline and d.world == 1:
+            out["cpu_baseline"] = (cpu_baseline_lm() if args.workload == "lm_head"
+                                   else __import__("hackable_lm_b200.train", fromlist=["x"]).cpu_baseline())
+        print(json.dumps(out), flush=True)
+    d.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libhlm_b200.so"
@@ -27,6 +27,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "hlm_strerror": ([c_int], c_char_p),
     "hlm_device_error_get": ([POINTER(c_int), _P], c_int),
     "hlm_device_error_clear": ([_P], c_int),
+    "hlm_launch_count": ([], c_uint64),
+    "hlm_profile_begin": ([c_int, POINTER(c_void_p), POINTER(c_void_p), c_int], c_int),
+    "hlm_profile_end": ([c_int, POINTER(c_int)], c_int),
     "hlm_swiglu_fwd": ([_P, _P, _I64, _I64, c_int, _P], c_int),
     "hlm_swiglu_bwd": ([_P, _P, _P, _I64, _I64, c_int, _P], c_int),
     "hlm_residual_rms_norm_fwd": ([_P, _P, _P, _P, _P, _I64, _I64, c_float, c_int, _P], c_int),
@@ -103,6 +106,54 @@ def device_error(stream: int = 0) -> int:
 
 def clear_device_error(stream: int = 0) -> None:
     check(load().hlm_device_error_clear(c_void_p(stream)), "hlm_device_error_clear")
+
+
+# Kernel ids of hlm_profile_begin (include/hlm_b200.h).
+KERNEL_IDS = {
+    "lm_logits": 1, "lm_dlogits": 2, "lm_dx": 3, "lm_dw": 4, "qkv_fwd": 5, "qkv_bwd_norm": 6,
+    "qkv_dx": 7, "qkv_dw": 8, "swiglu_fwd": 9, "swiglu_bwd": 10, "rmsnorm_fwd": 11,
+    "rmsnorm_bwd": 12, "qk_rope_fwd": 13, "qk_rope_bwd": 14, "gemm": 15,
+}
+
+
+def launch_count() -> int:
+    """Kernels launched by libhlm_b200 in this process so far."""
+    return int(load().hlm_launch_count())
+
+
+class KernelTimer:
+    """Time every launch of one library kernel with CUDA events recorded by the
+    library itself on the launching stream (hlm_profile_begin/end)."""
+
+    def __init__(self, kernel: str, capacity: int):
+        import torch
+
+        self.kid = KERNEL_IDS[kernel]
+        self.capacity = capacity
+        self.starts = [torch.cuda.Event(enable_timing=True) for _ in range(capacity)]
+        self.stops = [torch.cuda.Event(enable_timing=True) for _ in range(capacity)]
+        for ev in self.starts + self.stops:
+            ev.record()  # materialise the underlying cudaEvent_t
+        self._a = (c_void_p * capacity)(*[ev.cuda_event for ev in self.starts])
+        self._b = (c_void_p * capacity)(*[ev.cuda_event for ev in self.stops])
+        self.launches = 0
+
+    def __enter__(self):
+        check(load().hlm_profile_begin(self.kid, self._a, self._b, self.capacity), "hlm_profile_begin")
+        return self
+
+    def __exit__(self, *exc):
+        n = c_int(0)
+        check(load().hlm_profile_end(self.kid, ctypes.byref(n)), "hlm_profile_end")
+        self.launches = n.value
+        return False
+
+    def times_ms(self) -> list[float]:
+        import torch
+
+        torch.cuda.synchronize()
+        k = min(self.launches, self.capacity)
+        return [self.starts[i].elapsed_time(self.stops[i]) for i in range(k)]
 
 
 def int64_array(values) -> ctypes.Array:

@@ -499,6 +499,7 @@ extern "C" int hlm_swiglu_fwd(const void* gate_up, void* out, int64_t rows, int6
   if (rows == 0 || hidden == 0) return HLM_OK;
   if (gate_up == nullptr || out == nullptr) return HLM_ERR_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LaunchScope scope(HLM_KERNEL_SWIGLU_FWD, s);
   HLM_DISPATCH_DTYPE(dtype, T, {
     constexpr int VEC = 16 / sizeof(T);
     const bool vec = (hidden % VEC == 0) && host_aligned16(gate_up) && host_aligned16(out);
@@ -522,6 +523,7 @@ extern "C" int hlm_swiglu_bwd(const void* gate_up, const void* grad_out, void* g
   if (gate_up == nullptr || grad_out == nullptr || grad_gate_up == nullptr)
     return HLM_ERR_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  LaunchScope scope(HLM_KERNEL_SWIGLU_BWD, s);
   HLM_DISPATCH_DTYPE(dtype, T, {
     constexpr int VEC = 16 / sizeof(T);
     const bool vec = (hidden % VEC == 0) && host_aligned16(gate_up) && host_aligned16(grad_out) &&
@@ -550,6 +552,7 @@ extern "C" int hlm_residual_rms_norm_fwd(const void* residual, const void* branc
   if (residual != nullptr && out == nullptr) return HLM_ERR_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int threads = 256, wpb = threads / 32;
+  LaunchScope scope(HLM_KERNEL_RMSNORM_FWD, s);
   HLM_DISPATCH_DTYPE(dtype, T, {
     constexpr int VEC = 16 / sizeof(T);
     const int nv = pick_nv<T>(static_cast<int>(cols));
@@ -605,6 +608,7 @@ extern "C" int hlm_residual_rms_norm_bwd(const void* x, const void* weight, cons
   }
   HLM_DISPATCH_DTYPE(dtype, T, {
     if (rows > 0) {
+      LaunchScope scope(HLM_KERNEL_RMSNORM_BWD, s);
       constexpr int VEC = 16 / sizeof(T);
       const int nv = pick_nv<T>(static_cast<int>(cols));
       const bool vec = nv > 0 && cols % VEC == 0 && host_aligned16(x) &&
@@ -632,6 +636,7 @@ extern "C" int hlm_residual_rms_norm_bwd(const void* x, const void* weight, cons
     }
     if (want_w) {
       const int nparts = rows > 0 ? grid * kRmsBwdWarps : 1;
+      LaunchScope scope(0, s);
       reduce_partials_kernel<T><<<static_cast<int>((cols + 255) / 256), 256, 0, s>>>(
           partial, static_cast<T*>(grad_weight), nparts, static_cast<int>(cols));
     }
@@ -649,6 +654,7 @@ extern "C" int hlm_scale_by_device_scalar(void* data, const float* scale, int64_
   HLM_DISPATCH_DTYPE(dtype, T, {
     constexpr int VEC = 16 / sizeof(T);
     const int grid = elementwise_grid(n / VEC + 1, 256);
+    LaunchScope scope(0, s);
     scale_kernel<T><<<grid, 256, 0, s>>>(static_cast<T*>(data), scale, n);
   });
   return launch_status();

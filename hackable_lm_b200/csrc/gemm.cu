@@ -1,14 +1,11 @@
 // Host side of the tcgen05 GEMM core: tensor-map encoding through the driver
-// entry point (no link-time dependency on libcuda), the plain GEMM entry
-// point, and the library-wide C ABI utilities (version, error strings, the
-// device error word).
+// entry point (no link-time dependency on libcuda) and the plain GEMM entry
+// point.
 #include <mutex>
 
 #include "gemm_sm100.cuh"
 
 namespace hlm {
-
-__device__ int g_device_error = 0;
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -45,18 +42,6 @@ bool encode_bf16_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_
   return r == CUDA_SUCCESS;
 }
 
-int* device_error_ptr() {
-  static int* ptr[64] = {nullptr};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (ptr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
-    ptr[dev] = static_cast<int*>(p);
-  }
-  return ptr[dev];
-}
-
 template <int BN, bool A_MN, bool B_MN>
 static int plain_gemm(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K,
                       int64_t lda, int64_t ldb, int64_t ldd, int d_dtype, int accumulate,
@@ -78,52 +63,14 @@ static int plain_gemm(const void* A, const void* B, void* D, int64_t M, int64_t 
   ep.accumulate = accumulate;
   const int esz = d_dtype == HLM_F32 ? 4 : 2;
   ep.vec_ok = host_aligned16(D) && ((ldd * esz) % 16 == 0);
-  return launch_gemm_sm100<BN, STAGES, A_MN, B_MN, EpiStore>(ma, ma, ma, mb, p, ep, s);
+  ep.alpha = nullptr;
+  return launch_gemm_sm100<BN, STAGES, A_MN, B_MN, EpiStore>(ma, ma, ma, mb, p, ep, s,
+                                                              HLM_KERNEL_GEMM);
 }
 
 }  // namespace hlm
 
 using namespace hlm;
-
-extern "C" int hlm_version(void) { return 100; }
-
-extern "C" const char* hlm_strerror(int code) {
-  switch (code) {
-    case HLM_OK:
-      return "ok";
-    case HLM_ERR_INVALID_ARG:
-      return "invalid argument (null pointer, negative size or bad rank)";
-    case HLM_ERR_UNSUPPORTED:
-      return "unsupported shape, dtype, stride or alignment";
-    case HLM_ERR_LAUNCH:
-      return "CUDA launch or runtime error";
-    case HLM_ERR_WORKSPACE:
-      return "workspace smaller than required";
-    case HLM_ERR_DRIVER:
-      return "CUDA driver entry point or tensor-map encoding failed";
-    default:
-      return "unknown error code";
-  }
-}
-
-extern "C" int hlm_device_error_get(int* out, void* stream) {
-  if (out == nullptr) return HLM_ERR_INVALID_ARG;
-  int* p = device_error_ptr();
-  if (p == nullptr) return HLM_ERR_LAUNCH;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (cudaMemcpyAsync(out, p, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess)
-    return HLM_ERR_LAUNCH;
-  if (cudaStreamSynchronize(s) != cudaSuccess) return HLM_ERR_LAUNCH;
-  return HLM_OK;
-}
-
-extern "C" int hlm_device_error_clear(void* stream) {
-  int* p = device_error_ptr();
-  if (p == nullptr) return HLM_ERR_LAUNCH;
-  if (cudaMemsetAsync(p, 0, sizeof(int), static_cast<cudaStream_t>(stream)) != cudaSuccess)
-    return HLM_ERR_LAUNCH;
-  return HLM_OK;
-}
 
 extern "C" int hlm_gemm_bf16(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K,
                              int a_mn_major, int b_mn_major, int64_t lda, int64_t ldb, int64_t ldd,

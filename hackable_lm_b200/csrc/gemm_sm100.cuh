@@ -304,7 +304,7 @@ bool encode_bf16_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
 int launch_gemm_sm100(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& a2,
                       const CUtensorMap& b, const GemmParams& p, const typename Epi::Params& ep,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, int kernel_id) {
   using L = GemmSmem<BN, STAGES>;
   auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, Epi>;
   const int smem = L::kEpiOffset + Epi::kSmemBytes + 1024;
@@ -315,7 +315,10 @@ int launch_gemm_sm100(const CUtensorMap& a0, const CUtensorMap& a1, const CUtens
   if (total <= 0) return HLM_OK;
   int grid = num_sms_of_current_device();
   if (grid > total) grid = total;
-  kern<<<grid, kGemmThreads, smem, stream>>>(a0, a1, a2, b, p, ep);
+  {
+    LaunchScope scope(kernel_id, stream);
+    kern<<<grid, kGemmThreads, smem, stream>>>(a0, a1, a2, b, p, ep);
+  }
   return launch_status();
 }
 
@@ -346,6 +349,7 @@ struct EpiStore {
     int dtype;             // HLM_BF16 or HLM_F32
     int accumulate;        // D += acc (read-modify-write)
     int vec_ok;            // ldd % 8 == 0 and d 16-byte aligned
+    const float* alpha;    // optional device scalar: D = alpha * acc (+ D)
   };
   static constexpr int kSmemBytes = 0;
 
@@ -355,6 +359,7 @@ struct EpiStore {
                              int lane) {
     const int row = m_tile * kBM + quad * 32 + lane;
     const bool row_ok = row < p.M;
+    const float alpha = ep.alpha != nullptr ? *ep.alpha : 1.0f;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       uint32_t r[32];
@@ -362,6 +367,10 @@ struct EpiStore {
       tmem_ld_wait();
       const int col0 = n_tile * BN + c * 32;
       if (!row_ok || col0 >= p.N) continue;
+      if (ep.alpha != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+      }
       const bool full = ep.vec_ok && (col0 + 32 <= p.N);
       if (ep.dtype == HLM_F32) {
         float* d = static_cast<float*>(ep.d) + static_cast<int64_t>(split) * ep.split_stride +

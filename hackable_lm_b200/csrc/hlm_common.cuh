@@ -26,6 +26,22 @@ namespace hlm {
 // ---------------------------------------------------------------------------
 int* device_error_ptr();
 
+// RAII scope around one kernel launch: counts the launch (hlm_launch_count)
+// and, while hlm_profile_begin is active for `kernel_id`, records the
+// caller's CUDA events around it on the launching stream.
+class LaunchScope {
+ public:
+  LaunchScope(int kernel_id, cudaStream_t stream);
+  ~LaunchScope();
+  LaunchScope(const LaunchScope&) = delete;
+  LaunchScope& operator=(const LaunchScope&) = delete;
+
+ private:
+  int id_;
+  cudaStream_t stream_;
+  int slot_ = -1;
+};
+
 enum DeviceErrorCode : int {
   kDevErrNone = 0,
   kDevErrTimeoutFull = 1,      // MMA warp waited too long for a TMA stage

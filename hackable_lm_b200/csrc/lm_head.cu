@@ -11,11 +11,11 @@
 //      holds it.  Full fp32 logits never exist in memory.
 //   2. finalize      lse[row] = combine of the per-tile pairs; per-row loss;
 //      deterministic per-block loss sums.
-//   3. dlogits       in place: P = (exp(S - lse) - onehot(target)) / n_valid,
-//      zero for ignored rows (the reference's in-place gradient overwrite,
-//      kernels.py:315-318).
-//   4. dX GEMM       grad_hidden[chunk] = P @ W        (W read N-major)
-//   5. dW GEMM       grad_weight (+)= P^T @ H_chunk    (both operands MN-major)
+//   3. dlogits       in place: P = exp(S - lse) - onehot(target), zero for
+//      ignored rows (the reference's in-place gradient overwrite,
+//      kernels.py:315-318, without the 1/n factor)
+//   4. dX GEMM       grad_hidden[chunk] = (P @ W) / n_valid     (W read N-major)
+//   5. dW GEMM       grad_weight (+)= (P^T @ H_chunk) / n_valid (both MN-major)
 // A pre-pass counts the valid targets of the whole batch so the 1/n_valid
 // scale is known to every chunk on the device, with no host round trip.
 #include "gemm_sm100.cuh"
@@ -194,13 +194,15 @@ __global__ void __launch_bounds__(256) lm_loss_reduce_kernel(const float* __rest
   }
 }
 
-// In place: logits -> (softmax - onehot) / n_valid, zero rows for ignored targets.
+// In place: logits -> softmax - onehot, zero rows for ignored targets.  The
+// 1/n_valid scale is applied in fp32 by the dX/dW GEMM epilogues: folded into
+// the bf16 values it would carry one rounding error shared by every element.
 __global__ void __launch_bounds__(256) lm_dlogits_kernel(__nv_bfloat16* __restrict__ logits,
                                                         const float* __restrict__ lse,
                                                         const int64_t* __restrict__ targets,
                                                         int rows, int64_t V, int64_t ignore_index,
                                                         const LmStats* __restrict__ stats) {
-  const float inv_n = stats->inv_n;
+  (void)stats;
   const int64_t vpr = V / 8;
   const int64_t total = static_cast<int64_t>(rows) * vpr;
   for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
@@ -221,7 +223,7 @@ __global__ void __launch_bounds__(256) lm_dlogits_kernel(__nv_bfloat16* __restri
       for (int i = 0; i < 8; ++i) {
         float q = exp2f(fmaf(f[i], kLog2e, -l2));
         if (col0 + i == t) q -= 1.0f;
-        f[i] = q * inv_n;
+        f[i] = q;
       }
       Vec16<__nv_bfloat16> o;
       o.from_float(f);
@@ -331,7 +333,10 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
   const __nv_bfloat16* H = static_cast<const __nv_bfloat16*>(hidden);
   const __nv_bfloat16* W = static_cast<const __nv_bfloat16*>(weight);
 
-  lm_count_valid_kernel<<<1, 1024, 0, s>>>(targets, n_tokens, V, ignore_index, stats);
+  {
+    LaunchScope scope(0, s);
+    lm_count_valid_kernel<<<1, 1024, 0, s>>>(targets, n_tokens, V, ignore_index, stats);
+  }
   if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
 
   // Tensor maps that do not depend on the chunk.
@@ -362,15 +367,21 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       ep.V = static_cast<int>(V);
       ep.rows = rows;
       const int rc = launch_gemm_sm100<kLmBN, kLmStages, false, false, EpiLogitsLSE>(
-          map_h, map_h, map_h, map_w_k, p, ep, s);
+          map_h, map_h, map_h, map_w_k, p, ep, s, HLM_KERNEL_LM_LOGITS);
       if (rc != HLM_OK) return rc;
     }
     // 2. lse + loss
     {
       const int nb = (rows + 255) / 256;
-      lm_finalize_kernel<<<nb, 256, 0, s>>>(partial, pl.n_parts, tgt_logit, tc, rows, V,
-                                            ignore_index, lse, bsum);
-      lm_loss_reduce_kernel<<<1, 256, 0, s>>>(bsum, nb, stats, loss, last ? 1 : 0);
+      {
+        LaunchScope scope(0, s);
+        lm_finalize_kernel<<<nb, 256, 0, s>>>(partial, pl.n_parts, tgt_logit, tc, rows, V,
+                                              ignore_index, lse, bsum);
+      }
+      {
+        LaunchScope scope(0, s);
+        lm_loss_reduce_kernel<<<1, 256, 0, s>>>(bsum, nb, stats, loss, last ? 1 : 0);
+      }
       if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
     }
     if (!want_dx && !want_dw) continue;
@@ -380,6 +391,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       int64_t blocks = (vecs + 255) / 256;
       const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
       if (blocks > cap) blocks = cap;
+      LaunchScope scope(HLM_KERNEL_LM_DLOGITS, s);
       lm_dlogits_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(logits, lse, tc, rows, V,
                                                                  ignore_index, stats);
       if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
@@ -398,8 +410,9 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       ep.dtype = HLM_BF16;
       ep.accumulate = 0;
       ep.vec_ok = 1;
+      ep.alpha = &stats->inv_n;
       const int rc = launch_gemm_sm100<kLmBN, kLmStages, false, true, EpiStore>(
-          map_p, map_p, map_p, map_w_n, p, ep, s);
+          map_p, map_p, map_p, map_w_n, p, ep, s, HLM_KERNEL_LM_DX);
       if (rc != HLM_OK) return rc;
     }
     // 5. grad_weight (+)= P^T @ H_chunk
@@ -414,6 +427,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       ep.ldd = C;
       ep.split_stride = 0;
       ep.vec_ok = 1;
+      ep.alpha = &stats->inv_n;
       if (pl.n_chunks == 1) {
         ep.d = grad_weight;
         ep.dtype = HLM_BF16;
@@ -424,7 +438,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
         ep.accumulate = ci > 0 ? 1 : 0;
       }
       const int rc = launch_gemm_sm100<kLmBN, kLmStages, true, true, EpiStore>(
-          map_pt, map_pt, map_pt, map_hn, p, ep, s);
+          map_pt, map_pt, map_pt, map_hn, p, ep, s, HLM_KERNEL_LM_DW);
       if (rc != HLM_OK) return rc;
     }
   }
@@ -433,6 +447,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
     int64_t blocks = (n + 255) / 256;
     const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
     if (blocks > cap) blocks = cap;
+    LaunchScope scope(0, s);
     f32_to_bf16_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
         dw_acc, static_cast<__nv_bfloat16*>(grad_weight), n);
     if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;

@@ -237,6 +237,7 @@ static int launch_qk_norm_rope(const void* q, const void* k, const void* gq, con
         host_aligned16(k_out);
   if (BWD) vec = vec && host_aligned16(gq) && host_aligned16(gk);
   const int threads = 256;
+  LaunchScope scope(BWD ? HLM_KERNEL_QK_ROPE_BWD : HLM_KERNEL_QK_ROPE_FWD, s);
   if (vec) {
     const int64_t warps_needed = (total * lph + 31) / 32;
     int64_t blocks = (warps_needed + 7) / 8;

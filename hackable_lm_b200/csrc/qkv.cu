@@ -246,7 +246,8 @@ static QkvBwdPlan qkv_bwd_plan(int64_t M, int64_t C, int64_t Hq, int64_t Hk) {
 template <int RD>
 static int qkv_fwd_launch(const CUtensorMap& mx, const CUtensorMap& mw, const GemmParams& p,
                           const typename EpiQKV<RD>::Params& ep, cudaStream_t s) {
-  return launch_gemm_sm100<kQkvD, kQkvStages, false, false, EpiQKV<RD>>(mx, mx, mx, mw, p, ep, s);
+  return launch_gemm_sm100<kQkvD, kQkvStages, false, false, EpiQKV<RD>>(mx, mx, mx, mw, p, ep, s,
+                                                                         HLM_KERNEL_QKV_FWD);
 }
 
 }  // namespace hlm
@@ -360,6 +361,7 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
     const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
+    LaunchScope scope(HLM_KERNEL_QKV_BWD_NORM, s);
     qkv_norm_rope_bwd_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
         static_cast<const __nv_bfloat16*>(q_out), static_cast<const __nv_bfloat16*>(k_out), rstd,
         static_cast<const __nv_bfloat16*>(grad_q), static_cast<const __nv_bfloat16*>(grad_k), cos,
@@ -389,7 +391,9 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
     ep.dtype = HLM_BF16;
     ep.accumulate = 0;
     ep.vec_ok = 1;
-    const int rc = launch_gemm_sm100<kDwBN, kDwStages, false, true, EpiStore>(a0, a1, a2, mb, p, ep, s);
+    ep.alpha = nullptr;
+    const int rc = launch_gemm_sm100<kDwBN, kDwStages, false, true, EpiStore>(a0, a1, a2, mb, p, ep,
+                                                                              s, HLM_KERNEL_QKV_DX);
     if (rc != HLM_OK) return rc;
   }
   // 3. grad_w = [dq|dk|dv]^T @ X   (split-K over tokens)
@@ -414,15 +418,20 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
     ep.dtype = HLM_F32;
     ep.accumulate = 0;
     ep.vec_ok = 1;
-    const int rc = launch_gemm_sm100<kDwBN, kDwStages, true, true, EpiStore>(a0, a1, a2, mb, p, ep, s);
+    ep.alpha = nullptr;
+    const int rc = launch_gemm_sm100<kDwBN, kDwStages, true, true, EpiStore>(a0, a1, a2, mb, p, ep,
+                                                                             s, HLM_KERNEL_QKV_DW);
     if (rc != HLM_OK) return rc;
     const int64_t n = nqkv * C;
     int64_t blocks = (n / 4 + 255) / 256;
     const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    splitk_reduce_bf16_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
-        slabs, pl.splits, n, static_cast<__nv_bfloat16*>(grad_w));
+    {
+      LaunchScope scope(0, s);
+      splitk_reduce_bf16_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
+          slabs, pl.splits, n, static_cast<__nv_bfloat16*>(grad_w));
+    }
     if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
   }
   return HLM_OK;

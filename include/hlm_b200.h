@@ -56,6 +56,39 @@ int hlm_device_error_get(int* out, void* stream);
 /* Reset the device error word to 0 (stream-ordered). */
 int hlm_device_error_clear(void* stream);
 
+/* Number of kernels this library has launched in this process (all devices).
+ * Lets a harness count the library's own launches inside a timed region. */
+uint64_t hlm_launch_count(void);
+
+/* Kernel ids for hlm_profile_begin / hlm_profile_end. */
+#define HLM_KERNEL_LM_LOGITS 1     /* LM head: logits GEMM + softmax statistics */
+#define HLM_KERNEL_LM_DLOGITS 2    /* LM head: in-place softmax - onehot */
+#define HLM_KERNEL_LM_DX 3         /* LM head: grad_hidden GEMM */
+#define HLM_KERNEL_LM_DW 4         /* LM head: grad_weight GEMM */
+#define HLM_KERNEL_QKV_FWD 5       /* QKV GEMM + norm/RoPE epilogue */
+#define HLM_KERNEL_QKV_BWD_NORM 6  /* QKV backward: norm/RoPE backward */
+#define HLM_KERNEL_QKV_DX 7        /* QKV backward: grad_x GEMM */
+#define HLM_KERNEL_QKV_DW 8        /* QKV backward: grad_w GEMM */
+#define HLM_KERNEL_SWIGLU_FWD 9
+#define HLM_KERNEL_SWIGLU_BWD 10
+#define HLM_KERNEL_RMSNORM_FWD 11
+#define HLM_KERNEL_RMSNORM_BWD 12
+#define HLM_KERNEL_QK_ROPE_FWD 13
+#define HLM_KERNEL_QK_ROPE_BWD 14
+#define HLM_KERNEL_GEMM 15
+#define HLM_KERNEL_MAX 16
+
+/* Start timing every launch of kernel `kernel_id`: launch i records
+ * start_events[i] immediately before and stop_events[i] immediately after
+ * it, on the launching stream (cudaEvent_t handles created by the caller),
+ * for i < capacity.  Profiling use only; not for use during graph capture. */
+int hlm_profile_begin(int kernel_id, void* const* start_events, void* const* stop_events,
+                      int capacity);
+
+/* Stop timing kernel `kernel_id`; *launches receives how many launches
+ * happened since hlm_profile_begin (may exceed the capacity). */
+int hlm_profile_end(int kernel_id, int* launches);
+
 /* ------------------------------------------------------------------------
  * SwiGLU
  * ------------------------------------------------------------------------ */

@@ -1,31 +1,55 @@
 """Tolerances shared by the parity tests.
 
-bf16 outputs and gradients: max-abs error <= 2e-2 after normalising by the
-RMS of the reference tensor.  Scalar losses: 1e-3 relative.  fp32 kernels:
-the reference GPU test's 1e-5 absolute/relative tolerance (test_kernels.py:78-79).
+bf16 outputs and gradients: every element must satisfy
+    |actual - expected| <= 2e-2 * (rms(expected) + |expected|)
+i.e. the "max-abs error <= 2e-2 after normalising by the reference RMS" bar,
+widened by 2e-2 relative for elements far above the RMS.  The widening is
+needed because bf16 itself cannot meet the pure RMS-normalised bar on
+heavy-tailed tensors: a correctly rounded bf16 value carries up to 2^-9 of
+its own magnitude, so a SwiGLU output whose max is 20x its RMS already sits
+at 4% of the RMS after exact rounding.  2e-2 relative is ~2.5 bf16 ulps.
+
+Scalar losses: 1e-3 relative.  fp32 kernels: 1e-5 absolute and relative,
+the reference GPU test's tolerance (tests/test_kernels.py:78-79 upstream).
 """
 from __future__ import annotations
 
 import torch
 
-BF16_RMS_TOL = 2e-2
+BF16_TOL = 2e-2
 LOSS_REL_TOL = 1e-3
 FP32_TOL = 1e-5
 
 
-def rms_normalised_max_err(actual: torch.Tensor, expected: torch.Tensor) -> float:
+def _pair(actual, expected):
     a = actual.detach().to("cpu", torch.float64)
     e = expected.detach().to("cpu", torch.float64)
     assert a.shape == e.shape, (tuple(a.shape), tuple(e.shape))
     assert torch.isfinite(a).all(), "non-finite values in the CUDA result"
+    return a, e
+
+
+def rms_normalised_max_err(actual, expected) -> float:
+    """max|a - e| / rms(e) (reported alongside the bf16-aware check)."""
+    a, e = _pair(actual, expected)
     rms = e.pow(2).mean().sqrt().item()
     err = (a - e).abs().max().item()
     return err / rms if rms > 0 else err
 
 
-def assert_bf16_close(actual, expected, tol: float = BF16_RMS_TOL, what: str = ""):
-    err = rms_normalised_max_err(actual, expected)
-    assert err <= tol, f"{what}: max|err|/rms = {err:.3e} > {tol:.1e}"
+def bf16_err(actual, expected) -> float:
+    """max_i |a_i - e_i| / (rms(e) + |e_i|)."""
+    a, e = _pair(actual, expected)
+    rms = e.pow(2).mean().sqrt()
+    denom = rms + e.abs()
+    denom = torch.where(denom > 0, denom, torch.ones_like(denom))
+    return ((a - e).abs() / denom).max().item()
+
+
+def assert_bf16_close(actual, expected, tol: float = BF16_TOL, what: str = ""):
+    err = bf16_err(actual, expected)
+    assert err <= tol, (f"{what}: max|err|/(rms+|ref|) = {err:.3e} > {tol:.1e} "
+                        f"(max|err|/rms = {rms_normalised_max_err(actual, expected):.3e})")
 
 
 def assert_loss_close(actual, expected, tol: float = LOSS_REL_TOL, what: str = "loss"):
@@ -35,6 +59,5 @@ def assert_loss_close(actual, expected, tol: float = LOSS_REL_TOL, what: str = "
 
 
 def assert_fp32_close(actual, expected, tol: float = FP32_TOL, what: str = ""):
-    a = actual.detach().to("cpu", torch.float64)
-    e = expected.detach().to("cpu", torch.float64)
+    a, e = _pair(actual, expected)
     torch.testing.assert_close(a, e, atol=tol, rtol=tol, msg=lambda m: f"{what}: {m}")
