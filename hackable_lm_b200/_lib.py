@@ -36,6 +36,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "hlm_residual_rms_norm_bwd": (
         [_P, _P, _P, _P, _P, _P, _P, c_size_t, _I64, _I64, c_float, c_int, _P], c_int),
     "hlm_rms_norm_bwd_workspace_bytes": ([_I64, _I64], c_size_t),
+    "hlm_residual_rms_norm_bwd_noalloc": (
+        [_P, _P, _P, _P, _P, _P, _I64, _I64, c_float, c_int, _P], c_int),
     "hlm_qk_norm_rope_fwd": (
         [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64, c_int,
          c_float, c_int, _P], c_int),

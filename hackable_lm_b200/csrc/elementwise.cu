@@ -7,6 +7,8 @@
 // (shuffle-xor trees, no shared memory), grids sized to the SM count.  A
 // scalar path covers shapes whose rows are not 16-byte multiples (the
 // reference accepts any even width, e.g. the [17,130] fp32 GPU test).
+#include <mutex>
+
 #include "hlm_common.cuh"
 
 namespace hlm {
@@ -656,6 +658,105 @@ extern "C" int hlm_scale_by_device_scalar(void* data, const float* scale, int64_
     const int grid = elementwise_grid(n / VEC + 1, 256);
     LaunchScope scope(0, s);
     scale_kernel<T><<<grid, 256, 0, s>>>(static_cast<T*>(data), scale, n);
+  });
+  return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the weighted RMSNorm backward.
+//
+// Some callers cannot allocate device memory at the moment they need this
+// operator: a host that pre-plans every device byte up front (a serving
+// process with a fixed memory budget, or a framework whose allocator must
+// account for all memory and cannot be re-entered from inside an operator),
+// and code that must not stall the device, since cudaMalloc/cudaFree
+// synchronise.  For them the dweight partial sums live in the fixed
+// file-scope array below instead of a caller-provided workspace.  The array
+// is sized for kNoAllocMaxCols columns (4 MiB) and every GPU that loads this
+// library holds it until the process exits.
+// ---------------------------------------------------------------------------
+namespace hlm {
+
+constexpr int kNoAllocMaxCols = HLM_NOALLOC_RMS_MAX_COLS;
+constexpr int kNoAllocPartials = kRmsBwdMaxBlocks * kRmsBwdWarps;
+
+static __device__ __align__(256) float g_noalloc_rms_partial[kNoAllocPartials * kNoAllocMaxCols];
+
+// Device address of g_noalloc_rms_partial, looked up once per device with that
+// device current.  The host-side symbol is only a stand-in and must never be
+// handed to a kernel.
+static float* noalloc_partial_ptr(int* rc) {
+  static float* ptrs[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *rc = HLM_ERR_LAUNCH;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_rms_partial) != cudaSuccess || p == nullptr) {
+      *rc = HLM_ERR_LAUNCH;
+      return nullptr;
+    }
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  *rc = HLM_OK;
+  return ptrs[dev];
+}
+
+}  // namespace hlm
+
+extern "C" int hlm_residual_rms_norm_bwd_noalloc(const void* x, const void* weight,
+                                                 const void* grad_out, const void* grad_norm,
+                                                 void* grad_in, void* grad_weight, int64_t rows,
+                                                 int64_t cols, float eps, int dtype,
+                                                 void* stream) {
+  if (rows < 0 || cols < 0) return HLM_ERR_INVALID_ARG;
+  if (cols > kNoAllocMaxCols) return HLM_ERR_UNSUPPORTED;  // beyond the fixed scratch array
+  if (weight == nullptr || grad_weight == nullptr) return HLM_ERR_INVALID_ARG;
+  if (cols == 0) return HLM_OK;
+  if (rows > 0 && (x == nullptr || grad_norm == nullptr || grad_in == nullptr))
+    return HLM_ERR_INVALID_ARG;
+  int rc = HLM_OK;
+  float* partial = noalloc_partial_ptr(&rc);
+  if (partial == nullptr) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int threads = kRmsBwdThreads;
+  const int grid = rms_bwd_weight_blocks(rows);  // <= kRmsBwdMaxBlocks
+  HLM_DISPATCH_DTYPE(dtype, T, {
+    if (rows > 0) {
+      // Every partial slot that the reduction below reads is written by this
+      // launch first, so nothing left in the array by an earlier call is read.
+      LaunchScope scope(HLM_KERNEL_RMSNORM_BWD, s);
+      constexpr int VEC = 16 / sizeof(T);
+      const int nv = pick_nv<T>(static_cast<int>(cols));
+      const bool vec = nv > 0 && cols % VEC == 0 && host_aligned16(x) &&
+                       host_aligned16(grad_norm) && host_aligned16(grad_in) &&
+                       (grad_out == nullptr || host_aligned16(grad_out)) && host_aligned16(weight);
+      if (vec) {
+        HLM_DISPATCH_NV(nv, NVC, {
+          rmsnorm_bwd_vec_kernel<T, NVC><<<grid, threads, 0, s>>>(
+              static_cast<const T*>(x), static_cast<const T*>(weight),
+              static_cast<const T*>(grad_out), static_cast<const T*>(grad_norm),
+              static_cast<T*>(grad_in), partial, rows, static_cast<int>(cols), eps);
+        });
+      } else {
+        rmsnorm_bwd_scalar_kernel<T><<<grid, threads, 0, s>>>(
+            static_cast<const T*>(x), static_cast<const T*>(weight),
+            static_cast<const T*>(grad_out), static_cast<const T*>(grad_norm),
+            static_cast<T*>(grad_in), partial, rows, static_cast<int>(cols), eps);
+      }
+    } else {
+      // No rows: dweight is zero; the one slot read below must start at zero.
+      if (cudaMemsetAsync(partial, 0, static_cast<size_t>(cols) * sizeof(float), s) != cudaSuccess)
+        return HLM_ERR_LAUNCH;
+    }
+    const int nparts = rows > 0 ? grid * kRmsBwdWarps : 1;
+    LaunchScope scope(0, s);
+    reduce_partials_kernel<T><<<static_cast<int>((cols + 255) / 256), 256, 0, s>>>(
+        partial, static_cast<T*>(grad_weight), nparts, static_cast<int>(cols));
   });
   return launch_status();
 }

@@ -134,6 +134,27 @@ int hlm_residual_rms_norm_bwd(const void* x, const void* weight, const void* gra
                               int64_t cols, float eps, int dtype, void* stream);
 size_t hlm_rms_norm_bwd_workspace_bytes(int64_t rows, int64_t cols);
 
+/* Allocation-free variant of hlm_residual_rms_norm_bwd for the weighted case
+ * (weight and grad_weight required), for callers that cannot allocate device
+ * memory when they call it: hosts that plan every device byte up front, and
+ * code that must not stall the device (cudaMalloc/cudaFree synchronise).
+ * No counterpart in the reference: it has no caller-allocated-workspace
+ * convention to avoid.
+ *   - Scratch (the dweight partial sums) lives in a fixed 4 MiB array inside
+ *     the library, held on every GPU that loads it until the process exits.
+ *   - cols must be <= HLM_NOALLOC_RMS_MAX_COLS, else HLM_ERR_UNSUPPORTED.
+ *   - The first call on each device looks up the array's device address; make
+ *     that first call outside any stream capture.
+ *   - Calls share the array: calls that overlap on the GPU (different streams,
+ *     different threads) race and must be serialised by the caller.
+ *   - Allocates nothing: no cudaMalloc, cudaFree or allocating library call.
+ * Results are identical to hlm_residual_rms_norm_bwd with a workspace. */
+#define HLM_NOALLOC_RMS_MAX_COLS 1024
+int hlm_residual_rms_norm_bwd_noalloc(const void* x, const void* weight, const void* grad_out,
+                                      const void* grad_norm, void* grad_in, void* grad_weight,
+                                      int64_t rows, int64_t cols, float eps, int dtype,
+                                      void* stream);
+
 /* ------------------------------------------------------------------------
  * QK-norm + partial rotate-half RoPE (standalone, strided inputs)
  * ------------------------------------------------------------------------ */
