@@ -2,18 +2,23 @@
 """Benchmark of the hackable-lm fused-operator hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload lm_head|d12]
+                    [--workload d12|lm_head]
 
 Prints ONE JSON line (rank 0).  For N > 1 launch one process per GPU with
 torch.distributed.run; timing is on the device (CUDA events), bracketed by a
 barrier + synchronize, and the max over ranks is reported.
 
 Workloads (synthetic, seeded):
+  d12      (default) depth-12 decoder data-parallel training step, BASELINE
+           config 5: global batch 2^20 tokens (micro-batch 16 x 2048 per GPU,
+           gradient accumulation 32/N), DDP bf16 buckets over NCCL, Muon+AdamW
+           step; all hot-path operators on the B200 kernels, attention via SDPA.
+           At N=1 the line also carries the LM-head C4 measurement
+           ("lm_head_c4") and per-operator rooflines ("ops").
   lm_head  fused LM-head + cross-entropy forward+backward, hidden [32768,768],
            W [32768,768], 2% targets = ignore_index -1 (one step = one call on
            one batch).  With N > 1 each rank processes its own batch and the
            bf16 grad_weight is all-reduced (data-parallel exchange).
-  d12      depth-12 decoder training step (see hackable_lm_b200.train).
 
 --impl reference times the reference algorithm's CPU implementation (the
 oracle restatement, all host threads) on a bounded sample of the same
@@ -321,6 +326,156 @@ def bench_lm_head(args, d: Dist, device) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# Depth-12 data-parallel training step
+# ---------------------------------------------------------------------------
+D12_FLOPS_PER_TOKEN = 887_095_296  # config.estimate_flops_per_token, full causal attention
+
+# per-layer kernels launch once per layer and micro-step; LM-head kernels once per micro-step
+D12_KERNELS = {"lm_logits": 1, "lm_dlogits": 1, "lm_dx": 1, "lm_dw": 1, "qkv_fwd": 12, "qkv_bwd_norm": 12,
+               "qkv_dx": 12, "qkv_dw": 12, "swiglu_fwd": 12, "swiglu_bwd": 12, "rmsnorm_fwd": 25,
+               "rmsnorm_bwd": 25}
+
+
+def d12_config(world: int, accum: int) -> dict:
+    return {"workload": "d12 DP training step: depth 12, C=768, 6x128 heads, SwiGLU 2048, vocab 32768, "
+                        "seq 2048, micro-batch 16/GPU, global batch 2^20 tokens, Muon+AdamW step",
+            "model": "hackable-lm d12 (random init)", "global_batch": 2**20, "seq_len": 2048,
+            "micro_batch_per_gpu": 16, "grad_accum_per_rank": accum,
+            "parallelism": f"dp{world}" + (" (DDP, bf16 25 MB buckets, NCCL)" if world > 1 else ""),
+            "attention": "torch SDPA, full causal",
+            "l2": "working set per micro-step >> 126 MB L2 (activations ~GBs); no flush"}
+
+
+def bench_d12(args, d: Dist, device) -> dict:
+    from hackable_lm_b200 import _lib
+    from hackable_lm_b200 import train as tr
+
+    peaks, peak_src = load_peaks()
+    s = tr.build(device, world=d.world)
+    batches = tr.synthetic_batches(4, s.micro_batch, s.seq_len, s.config.vocab_size, d.rank, device)
+    tokens_per_step = s.accum * s.micro_batch * s.seq_len * d.world
+
+    def step():
+        return tr.train_step(s, batches)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # per-kernel timing of the library's own launches during the first timed step
+    timers = {k: _lib.KernelTimer(k, n * s.accum) for k, n in D12_KERNELS.items()}
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    d.barrier()
+    torch.cuda.synchronize()
+    n0 = _lib.launch_count()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    first = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        if i == 0:
+            for t in timers.values():
+                t.__enter__()
+        loss = step()
+        if i == 0:
+            for t in timers.values():
+                t.__exit__(None, None, None)
+            first.record()
+    stop.record()
+    torch.cuda.synchronize()
+    d.barrier()
+    torch.cuda.synchronize()
+    total_ms = d.max(start.elapsed_time(stop))
+    step0_ms = start.elapsed_time(first)
+    launches = _lib.launch_count() - n0
+    clk = clocks.stop()
+    ms_per_step = total_ms / args.steps
+    value = tokens_per_step / (ms_per_step / 1e3)
+
+    M = s.micro_batch * s.seq_len
+    C, V, Hd = s.config.n_embd, s.config.vocab_size, 3 * s.config.n_head * s.config.head_dim
+    flops = {"lm_logits": 2.0 * M * C * V, "lm_dx": 2.0 * M * C * V, "lm_dw": 2.0 * M * C * V,
+             "qkv_fwd": 2.0 * M * C * Hd, "qkv_dx": 2.0 * M * C * Hd, "qkv_dw": 2.0 * M * C * Hd}
+    breakdown, totals = {}, {}
+    for k, t in timers.items():
+        ts = t.times_ms()
+        if not ts:
+            continue
+        totals[k] = sum(ts)
+        avg = sum(ts) / len(ts)
+        e = {"launches_in_step": t.launches, "avg_ms": round(avg, 4), "total_ms": round(sum(ts), 3),
+             "share_of_step": round(sum(ts) / step0_ms, 4)}
+        if k in flops:
+            e["tflops"] = round(flops[k] / (avg / 1e3) / 1e12, 1)
+        breakdown[k] = e
+    dominant = max(totals, key=totals.get)
+    dom_avg = breakdown[dominant]["avg_ms"]
+    roofline = {"kernel": dominant, "traffic": traffic_table().get(("d12", dominant))}
+    if dominant in flops:
+        achieved = flops[dominant] / (dom_avg / 1e3) / 1e12
+        peak = peaks["bf16_tflops_sustained"]
+        roofline.update({"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_src} bf16_tflops_sustained (kernel inside a seconds-long step)"})
+    else:
+        roofline.update({"bound": "hbm", "achieved": None, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": None, "peak_source": f"{peak_src} hbm_gbs"})
+
+    # ---- end to end: every micro-batch copied from pinned host memory, loss read back per step
+    host = [(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in batches]
+    xd = torch.empty_like(batches[0][0])
+    yd = torch.empty_like(batches[0][1])
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def fetch(i):
+        hx, hy = host[i % len(host)]
+        xd.copy_(hx, non_blocking=True)
+        yd.copy_(hy, non_blocking=True)
+        return xd, yd
+
+    def e2e_step():
+        l = tr.train_step(s, batches, fetch=fetch)
+        loss_host.copy_(l.float(), non_blocking=True)
+
+    e2e_ms = cuda_time(e2e_step, args.steps, 1, d) / args.steps
+    bytes_in = s.accum * (host[0][0].numel() + host[0][1].numel()) * 8
+    e2e = {"value": tokens_per_step / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": bytes_in,
+           "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 3)}
+    mfu = D12_FLOPS_PER_TOKEN * value / (peaks["bf16_tflops"] * 1e12 * d.world)
+    return {
+        "metric": "d12 step tok/s", "value": value, "unit": "tokens/s", "n_gpus": d.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: uniform token ids (seeded per rank), targets = ids shifted by one",
+        "config": d12_config(d.world, s.accum), "roofline": roofline, "kernel_breakdown": breakdown,
+        "mfu": round(mfu, 4), "mfu_basis": f"{D12_FLOPS_PER_TOKEN} FLOP/token / measured bf16 burst peak",
+        "loss": float(loss.float().item()), "e2e": e2e, "gpu_launches": launches,
+        "gpu_launches_per_step": launches / args.steps, "clocks": clk,
+    }
+
+
+def d12_cpu_sample(seq_len: int = 2048, seed: int = 0) -> float:
+    from oracle import model as om
+
+    p = om.init_params(seed=seed)
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, 32768, (1, seq_len + 1), generator=g)
+    t0 = time.perf_counter()
+    om.train_step_cpu(p, ids[:, :-1], ids[:, 1:])
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_d12(reps: int = 2) -> dict:
+    torch.set_num_threads(os.cpu_count() or 1)
+    d12_cpu_sample()  # warm-up
+    times = [d12_cpu_sample() for _ in range(reps)]
+    med = statistics.median(times)
+    return {"value": 2048 / med, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"oracle d12 model (torch CPU fp32) forward+backward on 1x2048 tokens, median of {reps} "
+                      f"({med:.2f} s each); the optimizer step is excluded"}
+
+
+# ---------------------------------------------------------------------------
 # per-operator roofline measurements (rank 0, after the headline)
 # ---------------------------------------------------------------------------
 def bench_ops(device, iters: int = 20) -> dict:
@@ -418,11 +573,15 @@ def run_reference(args, d: Dist) -> dict | None:
         cfg = {"workload": "lm_head_ce C4: hidden [32768,768] x W [32768,768], fwd+bwd",
                "tokens_per_gpu": LM["M"], "hidden": LM["C"], "vocab": LM["V"], "ignore_index": -1}
     else:
-        from hackable_lm_b200 import train as tr
-
-        value, total, sample = tr.reference_cpu_steps(args.steps, args.warmup)
+        for _ in range(args.warmup):
+            d12_cpu_sample()
+        times = [d12_cpu_sample() for _ in range(args.steps)]
+        total = sum(times)
+        value = 2048 * args.steps / total
+        sample = ("oracle d12 model (torch CPU fp32) forward+backward, 1x2048 tokens per step of the "
+                  "2^20-token global batch; optimizer step excluded")
         metric = "d12 step tok/s"
-        cfg = tr.bench_config(1)
+        cfg = d12_config(1, 32)
     ms = total / args.steps * 1e3
     return {"impl": "reference", "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": d.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
@@ -436,10 +595,10 @@ def run_reference(args, d: Dist) -> dict | None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--workload", choices=("lm_head", "d12"), default="lm_head")
+    ap.add_argument("--workload", choices=("lm_head", "d12"), default="d12")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-operator section")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-tokens", type=int, default=1024, help="tokens per reference-arm step")
@@ -466,15 +625,16 @@ def main() -> None:
     if args.workload == "lm_head":
         out = bench_lm_head(args, d, device)
     else:
-        from hackable_lm_b200 import train as tr
-
-        out = tr.bench_d12(args, d, device, cuda_time, ClockSampler, load_peaks, traffic_table)
+        out = bench_d12(args, d, device)
     if d.rank == 0:
         if not args.no_ops and d.world == 1:
+            if args.workload == "d12":
+                lm = bench_lm_head(argparse.Namespace(steps=10, warmup=3), d, device)
+                out["lm_head_c4"] = {k: lm[k] for k in ("metric", "value", "unit", "ms_per_step", "config",
+                                                        "roofline", "kernel_breakdown", "e2e", "gpu_launches")}
             out["ops"] = bench_ops(device)
         if not args.no_cpu_baseline and d.world == 1:
-            out["cpu_baseline"] = (cpu_baseline_lm() if args.workload == "lm_head"
-                                   else __import__("hackable_lm_b200.train", fromlist=["x"]).cpu_baseline())
+            out["cpu_baseline"] = cpu_baseline_lm() if args.workload == "lm_head" else cpu_baseline_d12()
         print(json.dumps(out), flush=True)
     d.close()
 

@@ -57,48 +57,54 @@ static inline int elementwise_grid(int64_t work_items, int threads) {
   return static_cast<int>(blocks);
 }
 
+// Grid for row-oriented kernels: enough blocks to cover every row group once,
+// capped at a multiple of the SM count for very tall inputs.
+static inline int rows_grid(int64_t rows, int rows_per_block) {
+  const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 64;
+  int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
 // ---------------------------------------------------------------------------
 // SwiGLU (kernels.py:343-386)
 // ---------------------------------------------------------------------------
-template <typename T>
+// Row-oriented: a block owns R consecutive rows per iteration and its threads
+// stride over the 16-byte vectors of each half-row, so every thread keeps 2*R
+// independent 16-byte loads in flight and no index division is needed.
+template <typename T, int R>
 __global__ void __launch_bounds__(256) swiglu_fwd_vec_kernel(const T* __restrict__ gate_up,
                                                             T* __restrict__ out, int64_t rows,
-                                                            int64_t hidden) {
+                                                            int hv) {
   constexpr int VEC = 16 / sizeof(T);
-  const int64_t hv = hidden / VEC;
-  const int64_t total = rows * hv;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
-       v += 2 * stride) {
-    uint4 g_raw[2], u_raw[2];
-    int64_t off_in[2], off_out[2];
-    bool ok[2];
+  const int64_t hidden = static_cast<int64_t>(hv) * VEC;
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.x) * R; r0 < rows;
+       r0 += static_cast<int64_t>(gridDim.x) * R) {
+    for (int cv = threadIdx.x; cv < hv; cv += blockDim.x) {
+      uint4 g_raw[R], u_raw[R];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int64_t vv = v + u * stride;
-      ok[u] = vv < total;
-      const int64_t row = ok[u] ? vv / hv : 0;
-      const int64_t cv = ok[u] ? vv - row * hv : 0;
-      off_in[u] = row * 2 * hidden + cv * VEC;
-      off_out[u] = row * hidden + cv * VEC;
-      if (ok[u]) {
-        g_raw[u] = ld_global_nc_v4(gate_up + off_in[u]);
-        u_raw[u] = ld_global_nc_v4(gate_up + off_in[u] + hidden);
+      for (int r = 0; r < R; ++r) {
+        if (r0 + r < rows) {
+          const T* src = gate_up + (r0 + r) * 2 * hidden + static_cast<int64_t>(cv) * VEC;
+          g_raw[r] = ld_global_nc_v4(src);
+          u_raw[r] = ld_global_nc_v4(src + hidden);
+        }
       }
-    }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      if (!ok[u]) continue;
-      Vec16<T> gv, uv, ov;
-      gv.raw = g_raw[u];
-      uv.raw = u_raw[u];
-      float g[VEC], up[VEC], o[VEC];
-      gv.to_float(g);
-      uv.to_float(up);
+      for (int r = 0; r < R; ++r) {
+        if (r0 + r >= rows) continue;
+        Vec16<T> gv, uv, ov;
+        gv.raw = g_raw[r];
+        uv.raw = u_raw[r];
+        float g[VEC], up[VEC], o[VEC];
+        gv.to_float(g);
+        uv.to_float(up);
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) o[i] = g[i] * sigmoidf_(g[i]) * up[i];
-      ov.from_float(o);
-      st_global_v4(out + off_out[u], ov.raw);
+        for (int i = 0; i < VEC; ++i) o[i] = g[i] * sigmoidf_(g[i]) * up[i];
+        ov.from_float(o);
+        st_global_v4(out + (r0 + r) * hidden + static_cast<int64_t>(cv) * VEC, ov.raw);
+      }
     }
   }
 }
@@ -117,41 +123,52 @@ __global__ void __launch_bounds__(256) swiglu_fwd_scalar_kernel(const T* __restr
   }
 }
 
-template <typename T>
+template <typename T, int R>
 __global__ void __launch_bounds__(256) swiglu_bwd_vec_kernel(const T* __restrict__ gate_up,
                                                             const T* __restrict__ grad_out,
                                                             T* __restrict__ grad_gate_up,
-                                                            int64_t rows, int64_t hidden) {
+                                                            int64_t rows, int hv) {
   constexpr int VEC = 16 / sizeof(T);
-  const int64_t hv = hidden / VEC;
-  const int64_t total = rows * hv;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
-       v += stride) {
-    const int64_t row = v / hv;
-    const int64_t cv = v - row * hv;
-    const int64_t off_in = row * 2 * hidden + cv * VEC;
-    const int64_t off_g = row * hidden + cv * VEC;
-    Vec16<T> gv, uv, dv, og, ou;
-    gv.raw = ld_global_nc_v4(gate_up + off_in);
-    uv.raw = ld_global_nc_v4(gate_up + off_in + hidden);
-    dv.raw = ld_global_nc_v4(grad_out + off_g);
-    float g[VEC], up[VEC], d[VEC], rg[VEC], ru[VEC];
-    gv.to_float(g);
-    uv.to_float(up);
-    dv.to_float(d);
+  const int64_t hidden = static_cast<int64_t>(hv) * VEC;
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.x) * R; r0 < rows;
+       r0 += static_cast<int64_t>(gridDim.x) * R) {
+    for (int cv = threadIdx.x; cv < hv; cv += blockDim.x) {
+      uint4 g_raw[R], u_raw[R], d_raw[R];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      const float s = sigmoidf_(g[i]);
-      const float silu = g[i] * s;
-      const float dsilu = s * (1.0f + g[i] * (1.0f - s));
-      rg[i] = d[i] * up[i] * dsilu;
-      ru[i] = d[i] * silu;
+      for (int r = 0; r < R; ++r) {
+        if (r0 + r < rows) {
+          const int64_t off_in = (r0 + r) * 2 * hidden + static_cast<int64_t>(cv) * VEC;
+          g_raw[r] = ld_global_nc_v4(gate_up + off_in);
+          u_raw[r] = ld_global_nc_v4(gate_up + off_in + hidden);
+          d_raw[r] = ld_global_nc_v4(grad_out + (r0 + r) * hidden + static_cast<int64_t>(cv) * VEC);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (r0 + r >= rows) continue;
+        Vec16<T> gv, uv, dv, og, ou;
+        gv.raw = g_raw[r];
+        uv.raw = u_raw[r];
+        dv.raw = d_raw[r];
+        float g[VEC], up[VEC], d[VEC], rg[VEC], ru[VEC];
+        gv.to_float(g);
+        uv.to_float(up);
+        dv.to_float(d);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          const float sg = sigmoidf_(g[i]);
+          const float silu = g[i] * sg;
+          const float dsilu = sg * (1.0f + g[i] * (1.0f - sg));
+          rg[i] = d[i] * up[i] * dsilu;
+          ru[i] = d[i] * silu;
+        }
+        og.from_float(rg);
+        ou.from_float(ru);
+        const int64_t off_in = (r0 + r) * 2 * hidden + static_cast<int64_t>(cv) * VEC;
+        st_global_v4(grad_gate_up + off_in, og.raw);
+        st_global_v4(grad_gate_up + off_in + hidden, ou.raw);
+      }
     }
-    og.from_float(rg);
-    ou.from_float(ru);
-    st_global_v4(grad_gate_up + off_in, og.raw);
-    st_global_v4(grad_gate_up + off_in + hidden, ou.raw);
   }
 }
 
@@ -189,6 +206,15 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_vec_kernel(
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); row < rows;
        row += static_cast<int64_t>(gridDim.x) * wpb) {
     const int64_t base = row * cols;
+    uint4 braw[NV], rraw[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * VEC;
+      if (c < cols) {
+        braw[j] = ld_global_nc_v4(branch + base + c);
+        if (residual != nullptr) rraw[j] = ld_global_nc_v4(residual + base + c);
+      }
+    }
     float x[NV][VEC];
     float ss = 0.0f;
 #pragma unroll
@@ -196,11 +222,11 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_vec_kernel(
       const int c = (lane + 32 * j) * VEC;
       if (c < cols) {
         Vec16<T> bv;
-        bv.raw = ld_global_nc_v4(branch + base + c);
+        bv.raw = braw[j];
         bv.to_float(x[j]);
         if (residual != nullptr) {
           Vec16<T> rv, ov;
-          rv.raw = ld_global_nc_v4(residual + base + c);
+          rv.raw = rraw[j];
           float r[VEC];
           rv.to_float(r);
 #pragma unroll
@@ -270,52 +296,67 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_scalar_kernel(
   }
 }
 
-// Backward.  partial (optional) receives per-warp sums of g*x*r for dweight:
-// partial[(blockIdx.x * wpb + warp) * cols + c].
-template <typename T, int NV>
+// Backward.  With HAS_W, partial receives per-warp sums of g*x*r for dweight:
+// partial[(blockIdx.x * wpb + warp) * cols + c].  Without a weight the
+// kernel keeps no weight or dweight registers (the model's norms are
+// weightless), which keeps occupancy high.
+template <typename T, int NV, bool HAS_W>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(
     const T* __restrict__ xin, const T* __restrict__ weight, const T* __restrict__ grad_out,
     const T* __restrict__ grad_norm, T* __restrict__ grad_in, float* __restrict__ partial,
     int64_t rows, int cols, float eps) {
   constexpr int VEC = 16 / sizeof(T);
+  constexpr int NW = HAS_W ? NV : 1;
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const float inv_cols = 1.0f / static_cast<float>(cols);
-  float wacc[NV][VEC];
+  float wacc[NW][VEC];
+  float w[NW][VEC];
+  if constexpr (HAS_W) {
 #pragma unroll
-  for (int j = 0; j < NV; ++j)
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * VEC;
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) wacc[j][i] = 0.0f;
-  float w[NV][VEC];
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int c = (lane + 32 * j) * VEC;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) w[j][i] = 1.0f;
-    if (weight != nullptr && c < cols) {
-      Vec16<T> wv;
-      wv.raw = ld_global_v4(weight + c);
-      wv.to_float(w[j]);
+      for (int i = 0; i < VEC; ++i) {
+        wacc[j][i] = 0.0f;
+        w[j][i] = 1.0f;
+      }
+      if (c < cols) {
+        Vec16<T> wv;
+        wv.raw = ld_global_v4(weight + c);
+        wv.to_float(w[j]);
+      }
     }
   }
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); row < rows;
        row += static_cast<int64_t>(gridDim.x) * wpb) {
     const int64_t base = row * cols;
-    float x[NV][VEC], g[NV][VEC];
+    uint4 xraw[NV], graw[NV], oraw[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (lane + 32 * j) * VEC;
+      if (c < cols) {
+        xraw[j] = ld_global_nc_v4(xin + base + c);
+        graw[j] = ld_global_nc_v4(grad_norm + base + c);
+        if (grad_out != nullptr) oraw[j] = ld_global_nc_v4(grad_out + base + c);
+      }
+    }
     float ss = 0.0f, dot = 0.0f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int c = (lane + 32 * j) * VEC;
       if (c < cols) {
         Vec16<T> xv, gv;
-        xv.raw = ld_global_nc_v4(xin + base + c);
-        gv.raw = ld_global_nc_v4(grad_norm + base + c);
-        xv.to_float(x[j]);
-        gv.to_float(g[j]);
+        xv.raw = xraw[j];
+        gv.raw = graw[j];
+        float x[VEC], g[VEC];
+        xv.to_float(x);
+        gv.to_float(g);
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-          ss += x[j][i] * x[j][i];
-          dot += g[j][i] * w[j][i] * x[j][i];
+          ss += x[i] * x[i];
+          const float gw = HAS_W ? g[i] * w[HAS_W ? j : 0][i] : g[i];
+          dot += gw * x[i];
         }
       }
     }
@@ -327,10 +368,15 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(
     for (int j = 0; j < NV; ++j) {
       const int c = (lane + 32 * j) * VEC;
       if (c < cols) {
-        float go[VEC];
+        Vec16<T> xv, gv;
+        xv.raw = xraw[j];
+        gv.raw = graw[j];
+        float x[VEC], g[VEC], go[VEC];
+        xv.to_float(x);
+        gv.to_float(g);
         if (grad_out != nullptr) {
           Vec16<T> ov;
-          ov.raw = ld_global_nc_v4(grad_out + base + c);
+          ov.raw = oraw[j];
           ov.to_float(go);
         } else {
 #pragma unroll
@@ -339,8 +385,9 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(
         float d[VEC];
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-          d[i] = go[i] + r * g[j][i] * w[j][i] - x[j][i] * k3;
-          wacc[j][i] += g[j][i] * x[j][i] * r;
+          const float gw = HAS_W ? g[i] * w[HAS_W ? j : 0][i] : g[i];
+          d[i] = go[i] + r * gw - x[i] * k3;
+          if constexpr (HAS_W) wacc[j][i] += g[i] * x[i] * r;
         }
         Vec16<T> dv;
         dv.from_float(d);
@@ -348,7 +395,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(
       }
     }
   }
-  if (partial != nullptr) {
+  if constexpr (HAS_W) {
     float* dst = partial + (static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5)) * cols;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
@@ -505,10 +552,12 @@ extern "C" int hlm_swiglu_fwd(const void* gate_up, void* out, int64_t rows, int6
   HLM_DISPATCH_DTYPE(dtype, T, {
     constexpr int VEC = 16 / sizeof(T);
     const bool vec = (hidden % VEC == 0) && host_aligned16(gate_up) && host_aligned16(out);
-    if (vec) {
-      const int grid = elementwise_grid(rows * (hidden / VEC) / 2 + 1, 256);
-      swiglu_fwd_vec_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(gate_up),
-                                                    static_cast<T*>(out), rows, hidden);
+    if (vec && hidden / VEC <= (1ll << 30)) {
+      constexpr int R = 4;
+      const int grid = rows_grid(rows, R);
+      swiglu_fwd_vec_kernel<T, R><<<grid, 256, 0, s>>>(static_cast<const T*>(gate_up),
+                                                       static_cast<T*>(out), rows,
+                                                       static_cast<int>(hidden / VEC));
     } else {
       const int grid = elementwise_grid(rows * hidden, 256);
       swiglu_fwd_scalar_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(gate_up),
@@ -530,11 +579,12 @@ extern "C" int hlm_swiglu_bwd(const void* gate_up, const void* grad_out, void* g
     constexpr int VEC = 16 / sizeof(T);
     const bool vec = (hidden % VEC == 0) && host_aligned16(gate_up) && host_aligned16(grad_out) &&
                      host_aligned16(grad_gate_up);
-    if (vec) {
-      const int grid = elementwise_grid(rows * (hidden / VEC), 256);
-      swiglu_bwd_vec_kernel<T><<<grid, 256, 0, s>>>(
+    if (vec && hidden / VEC <= (1ll << 30)) {
+      constexpr int R = 2;
+      const int grid = rows_grid(rows, R);
+      swiglu_bwd_vec_kernel<T, R><<<grid, 256, 0, s>>>(
           static_cast<const T*>(gate_up), static_cast<const T*>(grad_out),
-          static_cast<T*>(grad_gate_up), rows, hidden);
+          static_cast<T*>(grad_gate_up), rows, static_cast<int>(hidden / VEC));
     } else {
       const int grid = elementwise_grid(rows * hidden, 256);
       swiglu_bwd_scalar_kernel<T><<<grid, 256, 0, s>>>(
@@ -561,8 +611,7 @@ extern "C" int hlm_residual_rms_norm_fwd(const void* residual, const void* branc
     const bool vec = nv > 0 && cols % VEC == 0 && host_aligned16(branch) && host_aligned16(norm) &&
                      (residual == nullptr || (host_aligned16(residual) && host_aligned16(out))) &&
                      (weight == nullptr || host_aligned16(weight));
-    const int grid = elementwise_grid(rows * 32, threads);
-    (void)wpb;
+    const int grid = rows_grid(rows, wpb);
     if (vec) {
       HLM_DISPATCH_NV(nv, NVC, {
         rmsnorm_fwd_vec_kernel<T, NVC><<<grid, threads, 0, s>>>(
@@ -606,7 +655,7 @@ extern "C" int hlm_residual_rms_norm_bwd(const void* x, const void* weight, cons
     partial = static_cast<float*>(workspace);
     grid = rms_bwd_weight_blocks(rows);
   } else {
-    grid = elementwise_grid(rows * 32, threads);
+    grid = rows_grid(rows, kRmsBwdWarps);
   }
   HLM_DISPATCH_DTYPE(dtype, T, {
     if (rows > 0) {
@@ -618,12 +667,21 @@ extern "C" int hlm_residual_rms_norm_bwd(const void* x, const void* weight, cons
                        (grad_out == nullptr || host_aligned16(grad_out)) &&
                        (weight == nullptr || host_aligned16(weight));
       if (vec) {
-        HLM_DISPATCH_NV(nv, NVC, {
-          rmsnorm_bwd_vec_kernel<T, NVC><<<grid, threads, 0, s>>>(
-              static_cast<const T*>(x), static_cast<const T*>(weight),
-              static_cast<const T*>(grad_out), static_cast<const T*>(grad_norm),
-              static_cast<T*>(grad_in), partial, rows, static_cast<int>(cols), eps);
-        });
+        if (want_w) {
+          HLM_DISPATCH_NV(nv, NVC, {
+            rmsnorm_bwd_vec_kernel<T, NVC, true><<<grid, threads, 0, s>>>(
+                static_cast<const T*>(x), static_cast<const T*>(weight),
+                static_cast<const T*>(grad_out), static_cast<const T*>(grad_norm),
+                static_cast<T*>(grad_in), partial, rows, static_cast<int>(cols), eps);
+          });
+        } else {
+          HLM_DISPATCH_NV(nv, NVC, {
+            rmsnorm_bwd_vec_kernel<T, NVC, false><<<grid, threads, 0, s>>>(
+                static_cast<const T*>(x), nullptr, static_cast<const T*>(grad_out),
+                static_cast<const T*>(grad_norm), static_cast<T*>(grad_in), nullptr, rows,
+                static_cast<int>(cols), eps);
+          });
+        }
       } else {
         rmsnorm_bwd_scalar_kernel<T><<<grid, threads, 0, s>>>(
             static_cast<const T*>(x), static_cast<const T*>(weight),
@@ -737,7 +795,7 @@ extern "C" int hlm_residual_rms_norm_bwd_noalloc(const void* x, const void* weig
                        (grad_out == nullptr || host_aligned16(grad_out)) && host_aligned16(weight);
       if (vec) {
         HLM_DISPATCH_NV(nv, NVC, {
-          rmsnorm_bwd_vec_kernel<T, NVC><<<grid, threads, 0, s>>>(
+          rmsnorm_bwd_vec_kernel<T, NVC, true><<<grid, threads, 0, s>>>(
               static_cast<const T*>(x), static_cast<const T*>(weight),
               static_cast<const T*>(grad_out), static_cast<const T*>(grad_norm),
               static_cast<T*>(grad_in), partial, rows, static_cast<int>(cols), eps);

@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                       const __grid_constant__ CUtensorMap tmA1,
                       const __grid_constant__ CUtensorMap tmA2,
                       const __grid_constant__ CUtensorMap tmB, const GemmParams p,
-                      const typename Epi::Params ep) {
+                      const __grid_constant__ typename Epi::Params ep) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -277,6 +277,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(TEMPTY_BAR(acc));
     }
+    // Epilogues that store through TMA must see their bulk stores finish
+    // reading shared memory before the CTA exits.
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -141,6 +141,29 @@ HLM_DEVICE void tma_load_2d(uint32_t dst_smem, const CUtensorMap* map, int c0, i
       : "memory");
 }
 
+// TMA store of a 2-D box from shared memory (bulk async group of the issuing thread).
+HLM_DEVICE void tma_store_2d(const CUtensorMap* map, int c0, int c1, uint32_t src_smem) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(src_smem)
+      : "memory");
+}
+HLM_DEVICE void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups still read their shared-memory source.
+template <int N>
+HLM_DEVICE void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until every committed bulk group has fully completed.
+HLM_DEVICE void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+HLM_DEVICE void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
 HLM_DEVICE void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -34,37 +34,48 @@ struct LmStats {
   int bad_target; // count of targets outside [0, V) that are not ignore_index
 };
 
+// Epilogue of the logits GEMM.  Per warp (32 accumulator rows) and 64-column
+// group: two tcgen05.ld, round to bf16 (the reference's logits dtype), fold the
+// rounded values into the row's running (max, sum exp), pick up the target
+// logit, and write the bf16 group into a 128B-swizzled shared-memory staging
+// buffer (conflict-free 16-byte stores) that one lane then writes to global
+// memory with a TMA tensor store -- full 128-byte lines instead of per-thread
+// partial-sector stores.  Two staging buffers per warp alternate so the
+// conversion of group g+1 overlaps the store of group g.
 struct EpiLogitsLSE {
   struct Params {
-    __nv_bfloat16* logits;   // [rows][ld]
-    int64_t ld;              // = V
+    alignas(64) CUtensorMap store_map;  // logits [rows][V] bf16, box {64, 32}, 128B swizzle
     float2* partial;         // [n_tiles][rows] (max, sum exp(x - max))
     float* tgt_logit;        // [rows]
     const int64_t* targets;  // [rows]
     int V;
     int rows;
   };
-  static constexpr int kSmemBytes = 0;
+  static constexpr int kStageBytes = 32 * 128;                 // one 32x64 bf16 box
+  static constexpr int kSmemBytes = 4 * 2 * kStageBytes;       // 4 warps x 2 buffers
 
   template <int BN>
-  static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t*, uint32_t taddr,
+  static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t* smem, uint32_t taddr,
                              int m_tile, int n_tile, int, int quad, int lane) {
     const int row = m_tile * kBM + quad * 32 + lane;
     const bool row_ok = row < p.M;
     const int64_t tgt = row_ok ? ep.targets[row] : -1;
     const int n0 = n_tile * BN;
+    const uint32_t stage0 = smem_u32(smem) + static_cast<uint32_t>(quad * 2 * kStageBytes);
     float m_run = -INFINITY, s_run = 0.0f;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), r);
+    for (int g = 0; g < BN / 64; ++g) {
+      uint32_t r[64];
+      tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(g * 64), *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(g * 64 + 32),
+                         *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
       tmem_ld_wait();
-      const int col0 = n0 + c * 32;
-      float v[32];
+      const int col0 = n0 + g * 64;
+      float v[64];
       float cmax = -INFINITY;
-      uint32_t packed[16];
+      uint32_t packed[32];
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) {
+      for (int j = 0; j < 64; j += 2) {
         const __nv_bfloat162 h2 =
             __floats2bfloat162_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
         packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h2);
@@ -73,35 +84,43 @@ struct EpiLogitsLSE {
         v[j + 1] = (col0 + j + 1 < ep.V) ? f2.y : -INFINITY;
         cmax = fmaxf(cmax, fmaxf(v[j], v[j + 1]));
       }
-      if (tgt >= col0 && tgt < col0 + 32) {
+      if (tgt >= col0 && tgt < col0 + 64) {
         float tl = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
+        for (int j = 0; j < 64; ++j)
           if (col0 + j == tgt) tl = v[j];
         ep.tgt_logit[row] = tl;
       }
       if (cmax > -INFINITY) {
         const float new_m = fmaxf(m_run, cmax);
         const float nm2 = new_m * kLog2e;
-        float s = 0.0f;
+        float sum = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) s += exp2f(fmaf(v[j], kLog2e, -nm2));
-        s_run = s_run * exp2f((m_run - new_m) * kLog2e) + s;
+        for (int j = 0; j < 64; ++j) sum += exp2f(fmaf(v[j], kLog2e, -nm2));
+        s_run = s_run * exp2f((m_run - new_m) * kLog2e) + sum;
         m_run = new_m;
       }
-      if (row_ok && col0 < ep.V) {
-        __nv_bfloat16* dst = ep.logits + static_cast<int64_t>(row) * ep.ld + col0;
-        if (col0 + 32 <= ep.V) {
+      // ---- stage the bf16 group (row = lane, 8 chunks of 16 B, 128B swizzle) and store it
+      const uint32_t buf = stage0 + static_cast<uint32_t>((g & 1) * kStageBytes);
+      if (g >= 2) {
+        if (lane == 0) bulk_wait_group_read<1>();  // the store that last used `buf` has read it
+        __syncwarp();
+      }
 #pragma unroll
-          for (int j = 0; j < 16; j += 4)
-            st_global_v4(dst + 2 * j, make_uint4(packed[j], packed[j + 1], packed[j + 2], packed[j + 3]));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < ep.V) dst[j] = __float2bfloat16_rn(v[j]);
-        }
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t addr = buf + static_cast<uint32_t>(lane * 128 + ((c ^ (lane & 7)) << 4));
+        st_shared_v4(addr, make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
+                                      packed[4 * c + 3]));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&ep.store_map, col0, m_tile * kBM + quad * 32, buf);
+        bulk_commit_group();
       }
     }
+    if (lane == 0) bulk_wait_group_read<0>();  // staging buffers free for the next tile
+    __syncwarp();
     if (row_ok) ep.partial[static_cast<int64_t>(n_tile) * ep.rows + row] = make_float2(m_run, s_run);
   }
 };
@@ -359,8 +378,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       gemm_tiling(p, rows, static_cast<int>(V), static_cast<int>(C), kLmBN, 1);
       p.err = err;
       EpiLogitsLSE::Params ep;
-      ep.logits = logits;
-      ep.ld = V;
+      if (!encode_bf16_map(&ep.store_map, logits, V, rows, V, 32)) return HLM_ERR_DRIVER;
       ep.partial = partial;
       ep.tgt_logit = tgt_logit;
       ep.targets = tc;

@@ -11,6 +11,8 @@
 // `half/VEC` lanes away and is fetched with a shuffle instead of being
 // re-read from memory; the sum of squares and the backward dot product are
 // shuffle-xor reductions inside the LPH-lane group.
+#include <type_traits>
+
 #include "hlm_common.cuh"
 
 namespace hlm {
@@ -30,67 +32,76 @@ HLM_DEVICE float group_sum(float v) {
   return v;
 }
 
-// Work item i in [0, B*T*(Hq+Hk)) -> (b, t, head index h over q then k).
-template <typename T, int LPH, bool BWD>
+// VEC consecutive cos/sin entries as fp32 (16-byte vector loads; the host
+// checks alignment before choosing this path).
+template <typename CS, int VEC>
+HLM_DEVICE void load_cs_vec(const CS* p, float (&out)[VEC]) {
+  constexpr int PER = 16 / sizeof(CS);
+#pragma unroll
+  for (int v = 0; v < VEC / PER; ++v) {
+    Vec16<CS> raw;
+    raw.raw = ld_global_v4(p + v * PER);
+    float f[PER];
+    raw.to_float(f);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) out[v * PER + i] = f[i];
+  }
+}
+
+// One warp per token: the warp's LPH-lane groups take head vectors
+// h = j*HPW + group for j < J, covering all Hq+Hk heads of q then k.  A lane
+// keeps the same dims d0..d0+VEC-1 for every head, so its cos/sin values are
+// loaded once per token, and all J head loads (2J in the backward) are issued
+// before any math so each lane has J independent 16-byte loads in flight.
+template <typename T, typename CS, int LPH, bool BWD, int J>
 __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ gq,
-    const T* __restrict__ gk, const void* __restrict__ cosp, const void* __restrict__ sinp,
+    const T* __restrict__ gk, const CS* __restrict__ cosp, const CS* __restrict__ sinp,
     T* __restrict__ q_out, T* __restrict__ k_out, QKShape sh) {
   constexpr int VEC = 16 / sizeof(T);
-  constexpr int HPW = 32 / LPH;  // head vectors per warp per iteration
+  constexpr int HPW = 32 / LPH;  // head vectors per warp per j
   const int lane = threadIdx.x & 31;
   const int slot = lane / LPH;
   const int li = lane % LPH;
-  const int64_t H = sh.Hq + sh.Hk;
-  const int64_t total = sh.B * sh.T * H;
+  const int H = static_cast<int>(sh.Hq + sh.Hk);
+  const int Hq = static_cast<int>(sh.Hq);
+  const uint32_t T_ = static_cast<uint32_t>(sh.T);
+  const uint32_t tokens = static_cast<uint32_t>(sh.B * sh.T);
   const int half = static_cast<int>(sh.rd / 2);
   const int d0 = li * VEC;
   const int pdelta = half / VEC;  // lane distance of the rotation partner
-  // This lane's role in the rotation (identical for every element of its vector).
   const int role = d0 < half ? 0 : (d0 < sh.rd ? 1 : 2);
   const int src_lane = role == 0 ? lane + pdelta : (role == 1 ? lane - pdelta : lane);
+  const int cbase = role == 0 ? d0 : d0 - half;
   const float inv_d = 1.0f / static_cast<float>(sh.D);
-  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
 
-  for (int64_t base_item = warp_id * HPW; base_item < total; base_item += warps_total * HPW) {
-    const int64_t item = base_item + slot;
-    const bool valid = item < total;
-    int64_t h = 0, t = 0, b = 0;
-    if (valid) {
-      h = item % H;
-      const int64_t bt = item / H;
-      t = bt % sh.T;
-      b = bt / sh.T;
-    }
-    const bool is_q = h < sh.Hq;
-    const int64_t hh = is_q ? h : h - sh.Hq;
-    const int64_t* st = is_q ? sh.qs : sh.ks;
-    const T* src = is_q ? q : k;
-    float x[VEC];
-    if (valid) {
-      Vec16<T> xv;
-      xv.raw = ld_global_nc_v4(src + b * st[0] + t * st[1] + hh * st[2] + d0);
-      xv.to_float(x);
-    } else {
+  for (uint32_t tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tok < tokens;
+       tok += warps_total) {
+    const uint32_t b = tok / T_;
+    const uint32_t t = tok - b * T_;
+    const int64_t qbase = b * sh.qs[0] + t * sh.qs[1] + d0;
+    const int64_t kbase = b * sh.ks[0] + t * sh.ks[1] + d0;
+    uint4 xraw[J], graw[J];
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) x[i] = 0.0f;
-    }
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) ss += x[i] * x[i];
-    ss = group_sum<LPH>(ss);
-    const float inv = rsqrtf(ss * inv_d + sh.eps);
-    const int64_t Hsel = is_q ? sh.Hq : sh.Hk;
-    const int64_t out_off = ((b * sh.T + t) * Hsel + hh) * sh.D + d0;
-    float c[VEC], s[VEC];
-    if (role != 2 && valid) {
-      const int cbase = role == 0 ? d0 : d0 - half;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        c[i] = load_cs(cosp, t * sh.cs_stride + cbase + i, sh.cs_dtype);
-        s[i] = load_cs(sinp, t * sh.cs_stride + cbase + i, sh.cs_dtype);
+    for (int j = 0; j < J; ++j) {
+      const int h = j * HPW + slot;
+      xraw[j] = make_uint4(0, 0, 0, 0);
+      graw[j] = make_uint4(0, 0, 0, 0);
+      if (h < H) {
+        const bool is_q = h < Hq;
+        const int hh = is_q ? h : h - Hq;
+        xraw[j] = ld_global_nc_v4(is_q ? q + qbase + hh * sh.qs[2] : k + kbase + hh * sh.ks[2]);
+        if constexpr (BWD) {
+          const int64_t off = (static_cast<int64_t>(tok) * (is_q ? sh.Hq : sh.Hk) + hh) * sh.D + d0;
+          graw[j] = ld_global_nc_v4((is_q ? gq : gk) + off);
+        }
       }
+    }
+    float c[VEC], s[VEC];
+    if (role != 2) {
+      load_cs_vec<CS, VEC>(cosp + t * sh.cs_stride + cbase, c);
+      load_cs_vec<CS, VEC>(sinp + t * sh.cs_stride + cbase, s);
     } else {
 #pragma unroll
       for (int i = 0; i < VEC; ++i) {
@@ -98,46 +109,56 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(
         s[i] = 0.0f;
       }
     }
-    float res[VEC];
-    if constexpr (!BWD) {
-      float z[VEC], pz[VEC];
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) z[i] = x[i] * inv;
+    for (int j = 0; j < J; ++j) {
+      const int h = j * HPW + slot;
+      float x[VEC];
+      Vec16<T> xv;
+      xv.raw = xraw[j];
+      xv.to_float(x);
+      float ss = 0.0f;
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) pz[i] = __shfl_sync(0xffffffffu, z[i], src_lane);
+      for (int i = 0; i < VEC; ++i) ss += x[i] * x[i];
+      ss = group_sum<LPH>(ss);
+      const float inv = rsqrtf(ss * inv_d + sh.eps);
+      float res[VEC];
+      if constexpr (!BWD) {
+        float z[VEC], pz[VEC];
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        res[i] = role == 0 ? z[i] * c[i] - pz[i] * s[i]
-                           : (role == 1 ? z[i] * c[i] + pz[i] * s[i] : z[i]);
-      }
-    } else {
-      const T* gsrc = is_q ? gq : gk;
-      float g[VEC], pg[VEC], gn[VEC];
-      if (valid) {
-        Vec16<T> gv;
-        gv.raw = ld_global_nc_v4(gsrc + out_off);
-        gv.to_float(g);
+        for (int i = 0; i < VEC; ++i) z[i] = x[i] * inv;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) pz[i] = __shfl_sync(0xffffffffu, z[i], src_lane);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          res[i] = role == 0 ? z[i] * c[i] - pz[i] * s[i]
+                             : (role == 1 ? z[i] * c[i] + pz[i] * s[i] : z[i]);
+        }
       } else {
+        float g[VEC], pg[VEC], gn[VEC];
+        Vec16<T> gv;
+        gv.raw = graw[j];
+        gv.to_float(g);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) g[i] = 0.0f;
+        for (int i = 0; i < VEC; ++i) pg[i] = __shfl_sync(0xffffffffu, g[i], src_lane);
+        float dot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          gn[i] = role == 0 ? g[i] * c[i] + pg[i] * s[i]
+                            : (role == 1 ? g[i] * c[i] - pg[i] * s[i] : g[i]);
+          dot += gn[i] * x[i] * inv;
+        }
+        dot = group_sum<LPH>(dot) * inv_d;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) res[i] = inv * (gn[i] - x[i] * inv * dot);
       }
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) pg[i] = __shfl_sync(0xffffffffu, g[i], src_lane);
-      float dot = 0.0f;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        gn[i] = role == 0 ? g[i] * c[i] + pg[i] * s[i]
-                          : (role == 1 ? g[i] * c[i] - pg[i] * s[i] : g[i]);
-        dot += gn[i] * x[i] * inv;
+      if (h < H) {
+        const bool is_q = h < Hq;
+        const int hh = is_q ? h : h - Hq;
+        const int64_t off = (static_cast<int64_t>(tok) * (is_q ? sh.Hq : sh.Hk) + hh) * sh.D + d0;
+        Vec16<T> ov;
+        ov.from_float(res);
+        st_global_v4((is_q ? q_out : k_out) + off, ov.raw);
       }
-      dot = group_sum<LPH>(dot) * inv_d;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) res[i] = inv * (gn[i] - x[i] * inv * dot);
-    }
-    if (valid) {
-      Vec16<T> ov;
-      ov.from_float(res);
-      st_global_v4((is_q ? q_out : k_out) + out_off, ov.raw);
     }
   }
 }
@@ -222,42 +243,76 @@ __global__ void __launch_bounds__(256) qk_norm_rope_scalar_kernel(
   }
 }
 
+template <typename T, typename CS, int LPH, bool BWD, int J>
+static void launch_qk_vec(const void* q, const void* k, const void* gq, const void* gk,
+                          const void* cosp, const void* sinp, void* q_out, void* k_out,
+                          const QKShape& sh, int blocks, cudaStream_t s) {
+  qk_norm_rope_vec_kernel<T, CS, LPH, BWD, J><<<blocks, 256, 0, s>>>(
+      static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(gq),
+      static_cast<const T*>(gk), static_cast<const CS*>(cosp), static_cast<const CS*>(sinp),
+      static_cast<T*>(q_out), static_cast<T*>(k_out), sh);
+}
+
+template <typename T, typename CS, int LPH, bool BWD>
+static void launch_qk_vec_j(int j, const void* q, const void* k, const void* gq, const void* gk,
+                            const void* cosp, const void* sinp, void* q_out, void* k_out,
+                            const QKShape& sh, int blocks, cudaStream_t s) {
+  if (j <= 2)
+    launch_qk_vec<T, CS, LPH, BWD, 2>(q, k, gq, gk, cosp, sinp, q_out, k_out, sh, blocks, s);
+  else if (j <= 4)
+    launch_qk_vec<T, CS, LPH, BWD, 4>(q, k, gq, gk, cosp, sinp, q_out, k_out, sh, blocks, s);
+  else if (j <= 6)
+    launch_qk_vec<T, CS, LPH, BWD, 6>(q, k, gq, gk, cosp, sinp, q_out, k_out, sh, blocks, s);
+  else
+    launch_qk_vec<T, CS, LPH, BWD, 8>(q, k, gq, gk, cosp, sinp, q_out, k_out, sh, blocks, s);
+}
+
 template <typename T, bool BWD>
 static int launch_qk_norm_rope(const void* q, const void* k, const void* gq, const void* gk,
                                const void* cosp, const void* sinp, void* q_out, void* k_out,
                                const QKShape& sh, cudaStream_t s) {
   constexpr int VEC = 16 / sizeof(T);
-  const int64_t total = sh.B * sh.T * (sh.Hq + sh.Hk);
+  const int64_t tokens = sh.B * sh.T;
+  const int64_t total = tokens * (sh.Hq + sh.Hk);
   const int64_t lph = sh.D / VEC;
-  bool vec = sh.D % VEC == 0 && (lph == 1 || lph == 2 || lph == 4 || lph == 8 || lph == 16 ||
-                                 lph == 32);
+  const bool cs_same = (sh.cs_dtype == HLM_F32 && sizeof(T) == 4) ||
+                       (sh.cs_dtype == HLM_BF16 && std::is_same<T, __nv_bfloat16>::value) ||
+                       (sh.cs_dtype == HLM_F16 && std::is_same<T, __half>::value);
+  const bool cs_f32 = sh.cs_dtype == HLM_F32;
+  const int cs_size = cs_f32 ? 4 : 2;
+  bool vec = sh.D % VEC == 0 && (lph == 8 || lph == 16 || lph == 32);
+  const int64_t hpw = lph > 0 ? 32 / lph : 0;
+  const int64_t jneed = hpw > 0 ? (sh.Hq + sh.Hk + hpw - 1) / hpw : 0;
+  vec = vec && jneed <= 8;
   vec = vec && (sh.rd / 2) % VEC == 0 && sh.qs[3] == 1 && sh.ks[3] == 1;
   for (int i = 0; i < 3; ++i) vec = vec && sh.qs[i] % VEC == 0 && sh.ks[i] % VEC == 0;
   vec = vec && host_aligned16(q) && host_aligned16(k) && host_aligned16(q_out) &&
         host_aligned16(k_out);
   if (BWD) vec = vec && host_aligned16(gq) && host_aligned16(gk);
+  vec = vec && (cs_same || cs_f32) && tokens < (1ll << 31);
+  if (sh.rd > 0)
+    vec = vec && host_aligned16(cosp) && host_aligned16(sinp) && (sh.cs_stride * cs_size) % 16 == 0;
   const int threads = 256;
   LaunchScope scope(BWD ? HLM_KERNEL_QK_ROPE_BWD : HLM_KERNEL_QK_ROPE_FWD, s);
   if (vec) {
-    const int64_t warps_needed = (total * lph + 31) / 32;
-    int64_t blocks = (warps_needed + 7) / 8;
-    const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
+    int64_t blocks = (tokens + 7) / 8;  // one warp per token
+    const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 64;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-#define HLM_QK_LAUNCH(L)                                                                     \
-  qk_norm_rope_vec_kernel<T, L, BWD><<<static_cast<int>(blocks), threads, 0, s>>>(           \
-      static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(gq),         \
-      static_cast<const T*>(gk), cosp, sinp, static_cast<T*>(q_out), static_cast<T*>(k_out), \
-      sh)
-    switch (lph) {
-      case 1: HLM_QK_LAUNCH(1); break;
-      case 2: HLM_QK_LAUNCH(2); break;
-      case 4: HLM_QK_LAUNCH(4); break;
-      case 8: HLM_QK_LAUNCH(8); break;
-      case 16: HLM_QK_LAUNCH(16); break;
-      default: HLM_QK_LAUNCH(32); break;
+    const int nb = static_cast<int>(blocks);
+    const int j = static_cast<int>(jneed);
+#define HLM_QK_CS(CS)                                                                          \
+  switch (lph) {                                                                               \
+    case 8: launch_qk_vec_j<T, CS, 8, BWD>(j, q, k, gq, gk, cosp, sinp, q_out, k_out, sh, nb, s); break; \
+    case 16: launch_qk_vec_j<T, CS, 16, BWD>(j, q, k, gq, gk, cosp, sinp, q_out, k_out, sh, nb, s); break; \
+    default: launch_qk_vec_j<T, CS, 32, BWD>(j, q, k, gq, gk, cosp, sinp, q_out, k_out, sh, nb, s); break; \
+  }
+    if (cs_f32) {
+      HLM_QK_CS(float)
+    } else {
+      HLM_QK_CS(T)
     }
-#undef HLM_QK_LAUNCH
+#undef HLM_QK_CS
   } else {
     int64_t blocks = (total + 7) / 8;
     const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
