@@ -80,15 +80,6 @@ HLM_DEVICE void select_segment(const GemmParams& p, int& c, const CUtensorMap*& 
   }
 }
 
-// Wait by lane 0, result broadcast to the warp (keeps .sync.aligned tcgen05
-// instructions that follow convergent even when a wait times out).
-HLM_DEVICE bool warp_wait(uint32_t bar, uint32_t parity, int* err, int code, int lane) {
-  int ok = 1;
-  if (lane == 0) ok = mbar_wait(bar, parity, err, code) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  return ok != 0;
-}
-
 // Wait that ignores the error word (used only to drain in-flight TMA copies
 // before the CTA exits); bounded by the same timeout.
 HLM_DEVICE bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {

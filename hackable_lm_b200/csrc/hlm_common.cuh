@@ -130,6 +130,15 @@ HLM_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
   return true;
 }
 
+// Wait by lane 0, result broadcast to the warp (keeps .sync.aligned
+// instructions that follow convergent even when a wait times out).
+HLM_DEVICE bool warp_wait(uint32_t bar, uint32_t parity, int* err, int code, int lane) {
+  int ok = 1;
+  if (lane == 0) ok = mbar_wait(bar, parity, err, code) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  return ok != 0;
+}
+
 // ---------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), plain CTA-local loads only.
 // ---------------------------------------------------------------------------
@@ -162,6 +171,22 @@ HLM_DEVICE void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)
                : "memory");
+}
+
+HLM_DEVICE void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_smem),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+HLM_DEVICE uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
 }
 
 HLM_DEVICE void prefetch_tensormap(const CUtensorMap* map) {

@@ -13,7 +13,7 @@
 // shuffle-xor reductions inside the LPH-lane group.
 #include <type_traits>
 
-#include "hlm_common.cuh"
+#include "rope_vec.cuh"
 
 namespace hlm {
 
@@ -48,117 +48,128 @@ HLM_DEVICE void load_cs_vec(const CS* p, float (&out)[VEC]) {
   }
 }
 
-// One warp per token: the warp's LPH-lane groups take head vectors
-// h = j*HPW + group for j < J, covering all Hq+Hk heads of q then k.  A lane
-// keeps the same dims d0..d0+VEC-1 for every head, so its cos/sin values are
-// loaded once per token, and all J head loads (2J in the backward) are issued
-// before any math so each lane has J independent 16-byte loads in flight.
-template <typename T, typename CS, int LPH, bool BWD, int J>
-__global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(
-    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ gq,
-    const T* __restrict__ gk, const CS* __restrict__ cosp, const CS* __restrict__ sinp,
-    T* __restrict__ q_out, T* __restrict__ k_out, QKShape sh) {
+// Item-based vector kernel: one LPH-lane group per head vector (lane = 8
+// consecutive dims), HPW = 32/LPH vectors per warp per step, persistent grid.
+// Every load of a step is issued up front -- the lane's 16 bytes, the 16 bytes
+// of its rotation partner (re-read from memory: an L1 hit, cheaper than
+// shuffles), and its cos/sin vectors -- and the rotation is branch-free:
+//   out = inv * (x*c' + sgn*s*px),  c' = cos (rotated dims) or 1 (pass-through),
+//   sgn = -1 for d < rd/2, +1 for rd/2 <= d < rd, 0 beyond.
+// Modes: kRopeFwd (x -> rotated norm), kRopeBwdX (x, g -> dx),
+//        kRopeBwdY (saved output y, saved 1/rms, g -> dx; the normalised
+//        vector z is the inverse rotation of y).
+template <typename T, typename CS, int LPH, int MODE>
+__global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(const RopeArgs a) {
   constexpr int VEC = 16 / sizeof(T);
-  constexpr int HPW = 32 / LPH;  // head vectors per warp per j
+  constexpr int HPW = 32 / LPH;
   const int lane = threadIdx.x & 31;
-  const int slot = lane / LPH;
-  const int li = lane % LPH;
-  const int H = static_cast<int>(sh.Hq + sh.Hk);
-  const int Hq = static_cast<int>(sh.Hq);
-  const uint32_t T_ = static_cast<uint32_t>(sh.T);
-  const uint32_t tokens = static_cast<uint32_t>(sh.B * sh.T);
-  const int half = static_cast<int>(sh.rd / 2);
-  const int d0 = li * VEC;
-  const int pdelta = half / VEC;  // lane distance of the rotation partner
-  const int role = d0 < half ? 0 : (d0 < sh.rd ? 1 : 2);
-  const int src_lane = role == 0 ? lane + pdelta : (role == 1 ? lane - pdelta : lane);
-  const int cbase = role == 0 ? d0 : d0 - half;
-  const float inv_d = 1.0f / static_cast<float>(sh.D);
-  const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
-
-  for (uint32_t tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tok < tokens;
-       tok += warps_total) {
-    const uint32_t b = tok / T_;
-    const uint32_t t = tok - b * T_;
-    const int64_t qbase = b * sh.qs[0] + t * sh.qs[1] + d0;
-    const int64_t kbase = b * sh.ks[0] + t * sh.ks[1] + d0;
-    uint4 xraw[J], graw[J];
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int h = j * HPW + slot;
-      xraw[j] = make_uint4(0, 0, 0, 0);
-      graw[j] = make_uint4(0, 0, 0, 0);
-      if (h < H) {
-        const bool is_q = h < Hq;
-        const int hh = is_q ? h : h - Hq;
-        xraw[j] = ld_global_nc_v4(is_q ? q + qbase + hh * sh.qs[2] : k + kbase + hh * sh.ks[2]);
-        if constexpr (BWD) {
-          const int64_t off = (static_cast<int64_t>(tok) * (is_q ? sh.Hq : sh.Hk) + hh) * sh.D + d0;
-          graw[j] = ld_global_nc_v4((is_q ? gq : gk) + off);
-        }
-      }
+  const int slot = lane / LPH, li = lane % LPH;
+  const uint32_t H = static_cast<uint32_t>(a.Hq + a.Hk);
+  const uint32_t Hq = static_cast<uint32_t>(a.Hq);
+  const uint32_t total = a.tokens * H;
+  const int half = a.rd / 2, d0 = li * VEC;
+  const int role = d0 < half ? 0 : (d0 < a.rd ? 1 : 2);
+  const int pdim = role == 0 ? d0 + half : (role == 1 ? d0 - half : d0);
+  const int cb = role == 2 ? 0 : (role == 0 ? d0 : d0 - half);
+  const float sgn = role == 0 ? -1.0f : (role == 1 ? 1.0f : 0.0f);
+  const float cpass = role == 2 ? 1.0f : 0.0f;  // c' = cpass + crot * cos
+  const float crot = 1.0f - cpass;
+  const bool has_rot = a.rd > 0;
+  const float inv_d = 1.0f / static_cast<float>(a.D);
+  const T* xq = static_cast<const T*>(a.xq);
+  const T* xk = static_cast<const T*>(a.xk);
+  const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
+  for (uint32_t base = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * HPW; base < total;
+       base += nwarps * HPW) {
+    const uint32_t item = base + slot;
+    const bool ok = item < total;
+    const uint32_t it = ok ? item : 0;
+    const uint32_t tok = it / H, h = it - tok * H;
+    const uint32_t b = tok / a.T, t = tok - b * a.T;
+    const bool is_q = h < Hq;
+    const uint32_t hh = is_q ? h : h - Hq;
+    const T* row = is_q ? xq + b * a.qs0 + t * a.qs1 + hh * a.qs2 : xk + b * a.ks0 + t * a.ks1 + hh * a.ks2;
+    const int64_t off = (static_cast<int64_t>(tok) * (is_q ? a.Hq : a.Hk) + hh) * a.D + d0;
+    const uint4 xr = ld_global_nc_v4(row + d0);
+    const uint4 pr = ld_global_nc_v4(row + pdim);
+    uint4 gr = make_uint4(0, 0, 0, 0), pgr = make_uint4(0, 0, 0, 0);
+    if constexpr (MODE != kRopeFwd) {
+      const T* grow = static_cast<const T*>(is_q ? a.gq : a.gk) +
+                      (static_cast<int64_t>(tok) * (is_q ? a.Hq : a.Hk) + hh) * a.D;
+      gr = ld_global_nc_v4(grow + d0);
+      pgr = ld_global_nc_v4(grow + pdim);
     }
     float c[VEC], s[VEC];
-    if (role != 2) {
-      load_cs_vec<CS, VEC>(cosp + t * sh.cs_stride + cbase, c);
-      load_cs_vec<CS, VEC>(sinp + t * sh.cs_stride + cbase, s);
+    if (has_rot) {
+      load_cs_vec<CS, VEC>(static_cast<const CS*>(a.cosp) + t * a.cs_stride + cb, c);
+      load_cs_vec<CS, VEC>(static_cast<const CS*>(a.sinp) + t * a.cs_stride + cb, s);
     } else {
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        c[i] = 1.0f;
-        s[i] = 0.0f;
-      }
+      for (int i = 0; i < VEC; ++i) c[i] = s[i] = 0.0f;
+    }
+    float rs = 0.0f;
+    if constexpr (MODE == kRopeBwdY) rs = a.rstd[static_cast<int64_t>(tok) * H + h];
+    float x[VEC], px[VEC];
+    {
+      Vec16<T> v, pv;
+      v.raw = xr;
+      pv.raw = pr;
+      v.to_float(x);
+      pv.to_float(px);
     }
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int h = j * HPW + slot;
-      float x[VEC];
-      Vec16<T> xv;
-      xv.raw = xraw[j];
-      xv.to_float(x);
+    for (int i = 0; i < VEC; ++i) {
+      c[i] = fmaf(crot, c[i], cpass);
+      s[i] *= sgn;
+    }
+    float res[VEC];
+    if constexpr (MODE == kRopeFwd) {
       float ss = 0.0f;
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) ss += x[i] * x[i];
+      for (int i = 0; i < VEC; ++i) ss = fmaf(x[i], x[i], ss);
       ss = group_sum<LPH>(ss);
-      const float inv = rsqrtf(ss * inv_d + sh.eps);
-      float res[VEC];
-      if constexpr (!BWD) {
-        float z[VEC], pz[VEC];
+      const float inv = rsqrtf(ss * inv_d + a.eps);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) res[i] = inv * fmaf(s[i], px[i], x[i] * c[i]);
+    } else {
+      float g[VEC], pg[VEC];
+      {
+        Vec16<T> v, pv;
+        v.raw = gr;
+        pv.raw = pgr;
+        v.to_float(g);
+        pv.to_float(pg);
+      }
+      float inv, z[VEC];
+      if constexpr (MODE == kRopeBwdX) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) ss = fmaf(x[i], x[i], ss);
+        ss = group_sum<LPH>(ss);
+        inv = rsqrtf(ss * inv_d + a.eps);
 #pragma unroll
         for (int i = 0; i < VEC; ++i) z[i] = x[i] * inv;
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) pz[i] = __shfl_sync(0xffffffffu, z[i], src_lane);
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) {
-          res[i] = role == 0 ? z[i] * c[i] - pz[i] * s[i]
-                             : (role == 1 ? z[i] * c[i] + pz[i] * s[i] : z[i]);
-        }
       } else {
-        float g[VEC], pg[VEC], gn[VEC];
-        Vec16<T> gv;
-        gv.raw = graw[j];
-        gv.to_float(g);
+        inv = rs;
+        // inverse rotation of the saved output y gives the normalised vector
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) pg[i] = __shfl_sync(0xffffffffu, g[i], src_lane);
-        float dot = 0.0f;
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) {
-          gn[i] = role == 0 ? g[i] * c[i] + pg[i] * s[i]
-                            : (role == 1 ? g[i] * c[i] - pg[i] * s[i] : g[i]);
-          dot += gn[i] * x[i] * inv;
-        }
-        dot = group_sum<LPH>(dot) * inv_d;
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) res[i] = inv * (gn[i] - x[i] * inv * dot);
+        for (int i = 0; i < VEC; ++i) z[i] = fmaf(-s[i], px[i], x[i] * c[i]);
       }
-      if (h < H) {
-        const bool is_q = h < Hq;
-        const int hh = is_q ? h : h - Hq;
-        const int64_t off = (static_cast<int64_t>(tok) * (is_q ? sh.Hq : sh.Hk) + hh) * sh.D + d0;
-        Vec16<T> ov;
-        ov.from_float(res);
-        st_global_v4((is_q ? q_out : k_out) + off, ov.raw);
+      // inverse rotation of the output gradient
+      float dot = 0.0f, gn[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        gn[i] = fmaf(-s[i], pg[i], g[i] * c[i]);
+        dot = fmaf(gn[i], z[i], dot);
       }
+      dot = group_sum<LPH>(dot) * inv_d;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) res[i] = inv * fmaf(-z[i], dot, gn[i]);
+    }
+    if (ok) {
+      Vec16<T> o;
+      o.from_float(res);
+      st_global_v4(static_cast<T*>(is_q ? a.oq : a.ok) + off, o.raw);
     }
   }
 }
@@ -243,86 +254,101 @@ __global__ void __launch_bounds__(256) qk_norm_rope_scalar_kernel(
   }
 }
 
-template <typename T, typename CS, int LPH, bool BWD, int J>
-static void launch_qk_vec(const void* q, const void* k, const void* gq, const void* gk,
-                          const void* cosp, const void* sinp, void* q_out, void* k_out,
-                          const QKShape& sh, int blocks, cudaStream_t s) {
-  qk_norm_rope_vec_kernel<T, CS, LPH, BWD, J><<<blocks, 256, 0, s>>>(
-      static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(gq),
-      static_cast<const T*>(gk), static_cast<const CS*>(cosp), static_cast<const CS*>(sinp),
-      static_cast<T*>(q_out), static_cast<T*>(k_out), sh);
+template <typename T, typename CS, int MODE>
+static void launch_rope_vec(int lph, const RopeArgs& a, int blocks, cudaStream_t s) {
+  switch (lph) {
+    case 8:
+      qk_norm_rope_vec_kernel<T, CS, 8, MODE><<<blocks, 256, 0, s>>>(a);
+      break;
+    case 16:
+      qk_norm_rope_vec_kernel<T, CS, 16, MODE><<<blocks, 256, 0, s>>>(a);
+      break;
+    default:
+      qk_norm_rope_vec_kernel<T, CS, 32, MODE><<<blocks, 256, 0, s>>>(a);
+      break;
+  }
 }
 
-template <typename T, typename CS, int LPH, bool BWD>
-static void launch_qk_vec_j(int j, const void* q, const void* k, const void* gq, const void* gk,
-                            const void* cosp, const void* sinp, void* q_out, void* k_out,
-                            const QKShape& sh, int blocks, cudaStream_t s) {
-  if (j <= 2)
-    launch_qk_vec<T, CS, LPH, BWD, 2>(q, k, gq, gk, cosp, sinp, q_out, k_out, sh, blocks, s);
-  else if (j <= 4)
-    launch_qk_vec<T, CS, LPH, BWD, 4>(q, k, gq, gk, cosp, sinp, q_out, k_out, sh, blocks, s);
-  else if (j <= 6)
-    launch_qk_vec<T, CS, LPH, BWD, 6>(q, k, gq, gk, cosp, sinp, q_out, k_out, sh, blocks, s);
+// Vector-path launch shared by the standalone op and the fused QKV backward.
+// Returns HLM_ERR_UNSUPPORTED when the layout does not allow 16-byte vectors.
+template <typename T, int MODE>
+int rope_vec_launch(const RopeArgs& a, int cs_dtype, int kernel_id, cudaStream_t s) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int lph = a.D / VEC;
+  bool vec = a.D % VEC == 0 && (lph == 8 || lph == 16 || lph == 32);
+  vec = vec && (a.rd / 2) % VEC == 0 && a.rd <= a.D;
+  const int64_t strides[] = {a.qs0, a.qs1, a.qs2, a.ks0, a.ks1, a.ks2};
+  for (int64_t st : strides) vec = vec && st % VEC == 0;
+  vec = vec && host_aligned16(a.xq) && host_aligned16(a.xk) && host_aligned16(a.oq) &&
+        host_aligned16(a.ok);
+  if (MODE != kRopeFwd) vec = vec && host_aligned16(a.gq) && host_aligned16(a.gk);
+  const bool cs_same = (cs_dtype == HLM_F32 && sizeof(T) == 4) ||
+                       (cs_dtype == HLM_BF16 && std::is_same<T, __nv_bfloat16>::value) ||
+                       (cs_dtype == HLM_F16 && std::is_same<T, __half>::value);
+  const bool cs_f32 = cs_dtype == HLM_F32;
+  vec = vec && (cs_same || cs_f32);
+  vec = vec && static_cast<int64_t>(a.tokens) * (a.Hq + a.Hk) < (1ll << 31);
+  if (a.rd > 0)
+    vec = vec && host_aligned16(a.cosp) && host_aligned16(a.sinp) &&
+          (a.cs_stride * (cs_f32 ? 4 : 2)) % 16 == 0;
+  if (!vec) return HLM_ERR_UNSUPPORTED;
+  const int64_t warps = (static_cast<int64_t>(a.tokens) * (a.Hq + a.Hk) * lph + 31) / 32;
+  int64_t blocks = (warps + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  LaunchScope scope(kernel_id, s);
+  if (cs_f32)
+    launch_rope_vec<T, float, MODE>(lph, a, static_cast<int>(blocks), s);
   else
-    launch_qk_vec<T, CS, LPH, BWD, 8>(q, k, gq, gk, cosp, sinp, q_out, k_out, sh, blocks, s);
+    launch_rope_vec<T, T, MODE>(lph, a, static_cast<int>(blocks), s);
+  return launch_status();
 }
+
+template int rope_vec_launch<__nv_bfloat16, kRopeBwdY>(const RopeArgs&, int, int, cudaStream_t);
 
 template <typename T, bool BWD>
 static int launch_qk_norm_rope(const void* q, const void* k, const void* gq, const void* gk,
                                const void* cosp, const void* sinp, void* q_out, void* k_out,
                                const QKShape& sh, cudaStream_t s) {
-  constexpr int VEC = 16 / sizeof(T);
-  const int64_t tokens = sh.B * sh.T;
-  const int64_t total = tokens * (sh.Hq + sh.Hk);
-  const int64_t lph = sh.D / VEC;
-  const bool cs_same = (sh.cs_dtype == HLM_F32 && sizeof(T) == 4) ||
-                       (sh.cs_dtype == HLM_BF16 && std::is_same<T, __nv_bfloat16>::value) ||
-                       (sh.cs_dtype == HLM_F16 && std::is_same<T, __half>::value);
-  const bool cs_f32 = sh.cs_dtype == HLM_F32;
-  const int cs_size = cs_f32 ? 4 : 2;
-  bool vec = sh.D % VEC == 0 && (lph == 8 || lph == 16 || lph == 32);
-  const int64_t hpw = lph > 0 ? 32 / lph : 0;
-  const int64_t jneed = hpw > 0 ? (sh.Hq + sh.Hk + hpw - 1) / hpw : 0;
-  vec = vec && jneed <= 8;
-  vec = vec && (sh.rd / 2) % VEC == 0 && sh.qs[3] == 1 && sh.ks[3] == 1;
-  for (int i = 0; i < 3; ++i) vec = vec && sh.qs[i] % VEC == 0 && sh.ks[i] % VEC == 0;
-  vec = vec && host_aligned16(q) && host_aligned16(k) && host_aligned16(q_out) &&
-        host_aligned16(k_out);
-  if (BWD) vec = vec && host_aligned16(gq) && host_aligned16(gk);
-  vec = vec && (cs_same || cs_f32) && tokens < (1ll << 31);
-  if (sh.rd > 0)
-    vec = vec && host_aligned16(cosp) && host_aligned16(sinp) && (sh.cs_stride * cs_size) % 16 == 0;
-  const int threads = 256;
+  if (sh.qs[3] == 1 && sh.ks[3] == 1 && sh.B * sh.T < (1ll << 31) && sh.T < (1ll << 31)) {
+    RopeArgs a{};
+    a.xq = q;
+    a.xk = k;
+    a.gq = gq;
+    a.gk = gk;
+    a.rstd = nullptr;
+    a.cosp = cosp;
+    a.sinp = sinp;
+    a.oq = q_out;
+    a.ok = k_out;
+    a.qs0 = sh.qs[0];
+    a.qs1 = sh.qs[1];
+    a.qs2 = sh.qs[2];
+    a.ks0 = sh.ks[0];
+    a.ks1 = sh.ks[1];
+    a.ks2 = sh.ks[2];
+    a.cs_stride = sh.cs_stride;
+    a.tokens = static_cast<uint32_t>(sh.B * sh.T);
+    a.T = static_cast<uint32_t>(sh.T);
+    a.Hq = static_cast<int>(sh.Hq);
+    a.Hk = static_cast<int>(sh.Hk);
+    a.D = static_cast<int>(sh.D);
+    a.rd = static_cast<int>(sh.rd);
+    a.eps = sh.eps;
+    const int rc = BWD ? rope_vec_launch<T, kRopeBwdX>(a, sh.cs_dtype, HLM_KERNEL_QK_ROPE_BWD, s)
+                       : rope_vec_launch<T, kRopeFwd>(a, sh.cs_dtype, HLM_KERNEL_QK_ROPE_FWD, s);
+    if (rc != HLM_ERR_UNSUPPORTED) return rc;
+  }
+  const int64_t total = sh.B * sh.T * (sh.Hq + sh.Hk);
+  int64_t blocks = (total + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
   LaunchScope scope(BWD ? HLM_KERNEL_QK_ROPE_BWD : HLM_KERNEL_QK_ROPE_FWD, s);
-  if (vec) {
-    int64_t blocks = (tokens + 7) / 8;  // one warp per token
-    const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 64;
-    if (blocks > cap) blocks = cap;
-    if (blocks < 1) blocks = 1;
-    const int nb = static_cast<int>(blocks);
-    const int j = static_cast<int>(jneed);
-#define HLM_QK_CS(CS)                                                                          \
-  switch (lph) {                                                                               \
-    case 8: launch_qk_vec_j<T, CS, 8, BWD>(j, q, k, gq, gk, cosp, sinp, q_out, k_out, sh, nb, s); break; \
-    case 16: launch_qk_vec_j<T, CS, 16, BWD>(j, q, k, gq, gk, cosp, sinp, q_out, k_out, sh, nb, s); break; \
-    default: launch_qk_vec_j<T, CS, 32, BWD>(j, q, k, gq, gk, cosp, sinp, q_out, k_out, sh, nb, s); break; \
-  }
-    if (cs_f32) {
-      HLM_QK_CS(float)
-    } else {
-      HLM_QK_CS(T)
-    }
-#undef HLM_QK_CS
-  } else {
-    int64_t blocks = (total + 7) / 8;
-    const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
-    if (blocks > cap) blocks = cap;
-    if (blocks < 1) blocks = 1;
-    qk_norm_rope_scalar_kernel<T, BWD><<<static_cast<int>(blocks), threads, 0, s>>>(
-        static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(gq),
-        static_cast<const T*>(gk), cosp, sinp, static_cast<T*>(q_out), static_cast<T*>(k_out),
-        sh);
-  }
+  qk_norm_rope_scalar_kernel<T, BWD><<<static_cast<int>(blocks), 256, 0, s>>>(
+      static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(gq),
+      static_cast<const T*>(gk), cosp, sinp, static_cast<T*>(q_out), static_cast<T*>(k_out), sh);
   return launch_status();
 }
 

@@ -9,13 +9,15 @@
 // strided split -> qk_norm_rope chain (model.py:92-99, 117-126;
 // kernels.py:446-503) with one pass over the output.
 //
-// Backward: a memory-bound kernel recovers the normalised vectors from the
-// saved outputs (inverse rotation) and the saved 1/rms, applies the
-// norm/RoPE backward (kernels.py:546-612) to produce dq_pre/dk_pre, then two
+// Backward: a memory-bound kernel (qk_norm_rope.cu, mode kRopeBwdY) recovers
+// the normalised vectors from the saved outputs (inverse rotation) and the
+// saved 1/rms, applies the norm/RoPE backward (kernels.py:546-612) to produce
+// dq_pre/dk_pre, then two
 // tcgen05 GEMMs read [dq_pre | dk_pre | dv] as one segmented operand:
 //   grad_x = [dq|dk|dv] @ W_qkv          (W read N-major)
 //   grad_w = [dq|dk|dv]^T @ X            (split-K, fp32 slabs, fixed-order sum)
 #include "gemm_sm100.cuh"
+#include "rope_vec.cuh"
 
 namespace hlm {
 
@@ -104,136 +106,6 @@ struct EpiQKV {
     }
   }
 };
-
-// Backward of the norm + RoPE part, from saved outputs y and 1/rms.
-// 16 lanes per head vector (8 bf16 each), two head vectors per warp; cos/sin
-// read as 16-byte vectors of CS (bf16 or fp32); 32-bit item arithmetic.
-template <typename CS>
-HLM_DEVICE void load_cs8(const CS* p, float (&out)[8]) {
-  constexpr int PER = 16 / sizeof(CS);
-#pragma unroll
-  for (int v = 0; v < 8 / PER; ++v) {
-    Vec16<CS> raw;
-    raw.raw = ld_global_v4(p + v * PER);
-    float f[PER];
-    raw.to_float(f);
-#pragma unroll
-    for (int i = 0; i < PER; ++i) out[v * PER + i] = f[i];
-  }
-}
-
-// One warp per token (all Hq+Hk head vectors, two per j step), cos/sin
-// loaded once per token, every head's loads issued before any math.
-template <typename CS, int J>
-__global__ void __launch_bounds__(256) qkv_norm_rope_bwd_kernel(
-    const __nv_bfloat16* __restrict__ q_out, const __nv_bfloat16* __restrict__ k_out,
-    const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ gq,
-    const __nv_bfloat16* __restrict__ gk, const CS* __restrict__ cosp,
-    const CS* __restrict__ sinp, int64_t cs_stride, __nv_bfloat16* __restrict__ dq,
-    __nv_bfloat16* __restrict__ dk, uint32_t M, uint32_t T, int Hq, int Hk, int rd) {
-  constexpr int VEC = 8, LPH = kQkvD / VEC, HPW = 32 / LPH;
-  const int lane = threadIdx.x & 31;
-  const int slot = lane / LPH, li = lane % LPH;
-  const int H = Hq + Hk;
-  const int half = rd / 2;
-  const int d0 = li * VEC;
-  const int pdelta = half / VEC;
-  const int role = d0 < half ? 0 : (d0 < rd ? 1 : 2);
-  const int src_lane = role == 0 ? lane + pdelta : (role == 1 ? lane - pdelta : lane);
-  const int cb = role == 0 ? d0 : d0 - half;
-  const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
-  for (uint32_t m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += warps_total) {
-    uint4 yraw[J], graw[J];
-    float inv[J];
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int h = j * HPW + slot;
-      yraw[j] = make_uint4(0, 0, 0, 0);
-      graw[j] = make_uint4(0, 0, 0, 0);
-      inv[j] = 0.0f;
-      if (h < H) {
-        const bool is_q = h < Hq;
-        const int hh = is_q ? h : h - Hq;
-        const int64_t off = (static_cast<int64_t>(m) * (is_q ? Hq : Hk) + hh) * kQkvD + d0;
-        yraw[j] = ld_global_nc_v4((is_q ? q_out : k_out) + off);
-        graw[j] = ld_global_nc_v4((is_q ? gq : gk) + off);
-        inv[j] = rstd[static_cast<int64_t>(m) * H + h];
-      }
-    }
-    float c[VEC], s[VEC];
-    if (role != 2) {
-      const uint32_t t = m % T;
-      load_cs8<CS>(cosp + t * cs_stride + cb, c);
-      load_cs8<CS>(sinp + t * cs_stride + cb, s);
-    } else {
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        c[i] = 1.0f;
-        s[i] = 0.0f;
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int h = j * HPW + slot;
-      float y[VEC], g[VEC];
-      Vec16<__nv_bfloat16> yv, gv;
-      yv.raw = yraw[j];
-      gv.raw = graw[j];
-      yv.to_float(y);
-      gv.to_float(g);
-      float py[VEC], pg[VEC], z[VEC], gn[VEC];
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        py[i] = __shfl_sync(0xffffffffu, y[i], src_lane);
-        pg[i] = __shfl_sync(0xffffffffu, g[i], src_lane);
-      }
-      float dot = 0.0f;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        // inverse rotation (rotation by -theta) of the output and of its gradient
-        z[i] = role == 0 ? y[i] * c[i] + py[i] * s[i] : (role == 1 ? y[i] * c[i] - py[i] * s[i] : y[i]);
-        gn[i] = role == 0 ? g[i] * c[i] + pg[i] * s[i] : (role == 1 ? g[i] * c[i] - pg[i] * s[i] : g[i]);
-        dot += gn[i] * z[i];
-      }
-#pragma unroll
-      for (int o = LPH / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      dot *= 1.0f / kQkvD;
-      if (h < H) {
-        const bool is_q = h < Hq;
-        const int hh = is_q ? h : h - Hq;
-        const int64_t off = (static_cast<int64_t>(m) * (is_q ? Hq : Hk) + hh) * kQkvD + d0;
-        float res[VEC];
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) res[i] = inv[j] * (gn[i] - z[i] * dot);
-        Vec16<__nv_bfloat16> o;
-        o.from_float(res);
-        st_global_v4((is_q ? dq : dk) + off, o.raw);
-      }
-    }
-  }
-}
-
-template <typename CS>
-static void launch_qkv_bwd_norm(int j, int blocks, cudaStream_t s, const __nv_bfloat16* q_out,
-                                const __nv_bfloat16* k_out, const float* rstd,
-                                const __nv_bfloat16* gq, const __nv_bfloat16* gk, const void* cosp,
-                                const void* sinp, int64_t cs_stride, __nv_bfloat16* dq,
-                                __nv_bfloat16* dk, uint32_t M, uint32_t T, int Hq, int Hk, int rd) {
-  const CS* c = static_cast<const CS*>(cosp);
-  const CS* sn = static_cast<const CS*>(sinp);
-#define HLM_QKVB(JV)                                                                              \
-  qkv_norm_rope_bwd_kernel<CS, JV><<<blocks, 256, 0, s>>>(q_out, k_out, rstd, gq, gk, c, sn,       \
-                                                           cs_stride, dq, dk, M, T, Hq, Hk, rd)
-  if (j <= 2)
-    HLM_QKVB(2);
-  else if (j <= 4)
-    HLM_QKVB(4);
-  else if (j <= 6)
-    HLM_QKVB(6);
-  else
-    HLM_QKVB(8);
-#undef HLM_QKVB
-}
 
 __global__ void __launch_bounds__(256) splitk_reduce_bf16_kernel(const float* __restrict__ slabs,
                                                                 int splits, int64_t n,
@@ -369,7 +241,6 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
                                 size_t workspace_bytes, int64_t B, int64_t T, int64_t C,
                                 int64_t Hq, int64_t Hk, int64_t D, int64_t rotary_dim,
                                 int64_t cs_stride_t, int cs_dtype, float eps, void* stream) {
-  (void)eps;
   if (B < 0 || T <= 0 || C <= 0 || Hq <= 0 || Hk <= 0 || D <= 0) return HLM_ERR_INVALID_ARG;
   if (D != kQkvD) return HLM_ERR_UNSUPPORTED;
   if (rotary_dim < 0 || rotary_dim > D || (rotary_dim / 2) % 8 != 0 || (rotary_dim & 1))
@@ -386,7 +257,7 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
   if (rotary_dim > 0 && (!host_aligned16(cos) || !host_aligned16(sin) ||
                          (cs_stride_t * (cs_dtype == HLM_F32 ? 4 : 2)) % 16 != 0))
     return HLM_ERR_UNSUPPORTED;
-  if (B * T * (Hq + Hk) >= (1ll << 31) || Hq + Hk > 16) return HLM_ERR_UNSUPPORTED;
+  if (B * T * (Hq + Hk) >= (1ll << 31)) return HLM_ERR_UNSUPPORTED;
   const void* ptrs[] = {x, w_qkv, q_out, k_out, grad_q, grad_k, grad_v, workspace};
   for (const void* ptr : ptrs)
     if (!host_aligned16(ptr)) return HLM_ERR_UNSUPPORTED;
@@ -403,33 +274,34 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
   if (err == nullptr) return HLM_ERR_LAUNCH;
   const int64_t nqkv = (Hq + 2 * Hk) * kQkvD;
 
-  // 1. norm + RoPE backward -> dq_pre, dk_pre
+  // 1. norm + RoPE backward -> dq_pre, dk_pre, from the saved outputs and 1/rms
   {
-    int64_t blocks = (M + 7) / 8;  // one warp per token
-    const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 64;
-    if (blocks > cap) blocks = cap;
-    if (blocks < 1) blocks = 1;
-    LaunchScope scope(HLM_KERNEL_QKV_BWD_NORM, s);
-    const int jneed = static_cast<int>((Hq + Hk + 1) / 2);
-    if (cs_dtype == HLM_F32)
-      launch_qkv_bwd_norm<float>(jneed, static_cast<int>(blocks), s,
-                                 static_cast<const __nv_bfloat16*>(q_out),
-                                 static_cast<const __nv_bfloat16*>(k_out), rstd,
-                                 static_cast<const __nv_bfloat16*>(grad_q),
-                                 static_cast<const __nv_bfloat16*>(grad_k), cos, sin, cs_stride_t, dq,
-                                 dk, static_cast<uint32_t>(M), static_cast<uint32_t>(T),
-                                 static_cast<int>(Hq), static_cast<int>(Hk),
-                                 static_cast<int>(rotary_dim));
-    else
-      launch_qkv_bwd_norm<__nv_bfloat16>(jneed, static_cast<int>(blocks), s,
-                                         static_cast<const __nv_bfloat16*>(q_out),
-                                         static_cast<const __nv_bfloat16*>(k_out), rstd,
-                                         static_cast<const __nv_bfloat16*>(grad_q),
-                                         static_cast<const __nv_bfloat16*>(grad_k), cos, sin,
-                                         cs_stride_t, dq, dk, static_cast<uint32_t>(M),
-                                         static_cast<uint32_t>(T), static_cast<int>(Hq),
-                                         static_cast<int>(Hk), static_cast<int>(rotary_dim));
-    if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
+    RopeArgs a{};
+    a.xq = q_out;
+    a.xk = k_out;
+    a.gq = grad_q;
+    a.gk = grad_k;
+    a.rstd = rstd;
+    a.cosp = cos;
+    a.sinp = sin;
+    a.oq = dq;
+    a.ok = dk;
+    a.qs0 = T * Hq * kQkvD;
+    a.qs1 = Hq * kQkvD;
+    a.qs2 = kQkvD;
+    a.ks0 = T * Hk * kQkvD;
+    a.ks1 = Hk * kQkvD;
+    a.ks2 = kQkvD;
+    a.cs_stride = cs_stride_t;
+    a.tokens = static_cast<uint32_t>(M);
+    a.T = static_cast<uint32_t>(T);
+    a.Hq = static_cast<int>(Hq);
+    a.Hk = static_cast<int>(Hk);
+    a.D = kQkvD;
+    a.rd = static_cast<int>(rotary_dim);
+    a.eps = eps;
+    const int rc = rope_vec_launch<__nv_bfloat16, kRopeBwdY>(a, cs_dtype, HLM_KERNEL_QKV_BWD_NORM, s);
+    if (rc != HLM_OK) return rc;
   }
   const int seg1 = static_cast<int>(Hq * kQkvD);
   const int seg2 = static_cast<int>((Hq + Hk) * kQkvD);
