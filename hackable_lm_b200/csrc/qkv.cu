@@ -1,11 +1,11 @@
 // Fused QKV projection + QK-norm + RoPE (forward) and its backward.
 //
-// Forward = one tcgen05 GEMM  qkv = X @ W_qkv^T  with BN = 128 = head_dim, so
-// each output tile is exactly one head of 128 token rows.  The epilogue owns
+// Forward = one tcgen05 GEMM  qkv = X @ W_qkv^T  with BN = 256, so each
+// output tile is exactly two heads of 128 token rows.  The epilogue owns
 // whole head rows (one row per thread): for q/k heads it computes the RMS
 // over the 128 fp32 accumulators, normalises, rotates the first rotary_dim
-// dims (rotate-half, cos/sin[t, d mod half]) and writes [B,T,H,D]; v heads are
-// written as they are.  This replaces the reference's GEMM -> bf16 qkv ->
+// dims (rotate-half, cos/sin[t, d mod half]) and writes [B,T,H,D] through TMA
+// stores; v heads are written as they are.  This replaces the reference's GEMM -> bf16 qkv ->
 // strided split -> qk_norm_rope chain (model.py:92-99, 117-126;
 // kernels.py:446-503) with one pass over the output.
 //
@@ -22,17 +22,24 @@
 namespace hlm {
 
 constexpr int kQkvD = 128;
-constexpr int kQkvStages = 6;
+constexpr int kQkvBN = 2 * kQkvD;  // two heads per output tile
+constexpr int kQkvStages = 4;
 constexpr int kDwBN = 256;
 constexpr int kDwStages = 4;
 constexpr int kDwTargetUnits = 2 * 148;
 
+// Forward epilogue: the tile holds 128 token rows x 2 heads (BN = 256).  Each
+// thread owns one row.  Per head: 4 x tcgen05.ld (128 fp32), then for q/k
+// heads RMSNorm over the 128 values + rotate-half RoPE on the first RD dims
+// (cos/sin of the row's position loaded once per tile), v heads pass through;
+// the bf16 row is staged in 128B-swizzled shared memory (two 32x64 boxes per
+// warp) and written with TMA tensor stores (full 128-byte lines).
 template <int RD>
 struct EpiQKV {
   struct Params {
-    __nv_bfloat16* q_out;
-    __nv_bfloat16* k_out;
-    __nv_bfloat16* v_out;
+    alignas(64) CUtensorMap map_q;  // q_out as [M][Hq*128] bf16, box {64, 32}
+    alignas(64) CUtensorMap map_k;  // k_out as [M][Hk*128]
+    alignas(64) CUtensorMap map_v;  // v_out as [M][Hk*128]
     float* rstd;
     const void* cosp;
     const void* sinp;
@@ -41,69 +48,121 @@ struct EpiQKV {
     int T, Hq, Hk;
     float eps;
   };
-  static constexpr int kSmemBytes = 0;
+  static constexpr int kBoxBytes = 32 * 128;
+  static constexpr int kSmemBytes = 4 * 2 * kBoxBytes;  // per warp: one head = 2 boxes
 
   template <int BN>
-  static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t*, uint32_t taddr,
+  static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t* smem, uint32_t taddr,
                              int m_tile, int n_tile, int, int quad, int lane) {
-    static_assert(BN == kQkvD, "one head per tile");
+    static_assert(BN == 2 * kQkvD, "two heads per tile");
     const int row = m_tile * kBM + quad * 32 + lane;
     const bool row_ok = row < p.M;
-    uint32_t r0[32], r1[32], r2[32], r3[32];
-    tmem_ld_32x32b_x32(taddr + 0u, r0);
-    tmem_ld_32x32b_x32(taddr + 32u, r1);
-    tmem_ld_32x32b_x32(taddr + 64u, r2);
-    tmem_ld_32x32b_x32(taddr + 96u, r3);
-    tmem_ld_wait();
-    float v[kQkvD];
+    const int Hq = ep.Hq, Hk = ep.Hk, nqk = Hq + Hk, nh = Hq + 2 * Hk;
+    const float eps = ep.eps;
+    float* const rstd = ep.rstd;
+    const uint32_t buf = smem_u32(smem) + static_cast<uint32_t>(quad * 2 * kBoxBytes);
+    // cos/sin of this row's position, first RD/2 entries (shared by both heads)
+    float cv[RD > 0 ? RD / 2 : 1], sv[RD > 0 ? RD / 2 : 1];
+    if constexpr (RD > 0) {
+      const int64_t t = row_ok ? row % ep.T : 0;
+      if (ep.cs_dtype == HLM_F32) {
+        const float* cp = static_cast<const float*>(ep.cosp) + t * ep.cs_stride;
+        const float* sp = static_cast<const float*>(ep.sinp) + t * ep.cs_stride;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      v[i] = __uint_as_float(r0[i]);
-      v[32 + i] = __uint_as_float(r1[i]);
-      v[64 + i] = __uint_as_float(r2[i]);
-      v[96 + i] = __uint_as_float(r3[i]);
-    }
-    const int head = n_tile;
-    const int nqk = ep.Hq + ep.Hk;
-    __nv_bfloat16* dst;
-    if (head < nqk) {
-      float ss = 0.0f;
+        for (int i = 0; i < RD / 2; i += 4) {
+          const float4 c4 = *reinterpret_cast<const float4*>(cp + i);
+          const float4 s4 = *reinterpret_cast<const float4*>(sp + i);
+          cv[i] = c4.x; cv[i + 1] = c4.y; cv[i + 2] = c4.z; cv[i + 3] = c4.w;
+          sv[i] = s4.x; sv[i + 1] = s4.y; sv[i + 2] = s4.z; sv[i + 3] = s4.w;
+        }
+      } else {
+        const __nv_bfloat16* cp = static_cast<const __nv_bfloat16*>(ep.cosp) + t * ep.cs_stride;
+        const __nv_bfloat16* sp = static_cast<const __nv_bfloat16*>(ep.sinp) + t * ep.cs_stride;
 #pragma unroll
-      for (int i = 0; i < kQkvD; ++i) ss = fmaf(v[i], v[i], ss);
-      const float inv = rsqrtf(ss * (1.0f / kQkvD) + ep.eps);
+        for (int i = 0; i < RD / 2; i += 8) {
+          Vec16<__nv_bfloat16> c8, s8;
+          c8.raw = ld_global_nc_v4(cp + i);
+          s8.raw = ld_global_nc_v4(sp + i);
+          float cf[8], sf[8];
+          c8.to_float(cf);
+          s8.to_float(sf);
 #pragma unroll
-      for (int i = 0; i < kQkvD; ++i) v[i] *= inv;
-      if constexpr (RD > 0) {
-        if (row_ok) {
-          const int64_t t = row % ep.T;
-#pragma unroll
-          for (int i = 0; i < RD / 2; ++i) {
-            const float c = load_cs(ep.cosp, t * ep.cs_stride + i, ep.cs_dtype);
-            const float s = load_cs(ep.sinp, t * ep.cs_stride + i, ep.cs_dtype);
-            const float a = v[i], b = v[i + RD / 2];
-            v[i] = a * c - b * s;
-            v[i + RD / 2] = b * c + a * s;
+          for (int j = 0; j < 8; ++j) {
+            cv[i + j] = cf[j];
+            sv[i + j] = sf[j];
           }
         }
       }
-      if (row_ok) ep.rstd[static_cast<int64_t>(row) * nqk + head] = inv;
-      dst = head < ep.Hq
-                ? ep.q_out + (static_cast<int64_t>(row) * ep.Hq + head) * kQkvD
-                : ep.k_out + (static_cast<int64_t>(row) * ep.Hk + (head - ep.Hq)) * kQkvD;
-    } else {
-      dst = ep.v_out + (static_cast<int64_t>(row) * ep.Hk + (head - nqk)) * kQkvD;
     }
-    if (row_ok) {
+#pragma unroll 1
+    for (int hs = 0; hs < 2; ++hs) {
+      const int head = n_tile * 2 + hs;
+      uint32_t r0[32], r1[32], r2[32], r3[32];
+      const uint32_t ta = taddr + static_cast<uint32_t>(hs * kQkvD);
+      tmem_ld_32x32b_x32(ta + 0u, r0);
+      tmem_ld_32x32b_x32(ta + 32u, r1);
+      tmem_ld_32x32b_x32(ta + 64u, r2);
+      tmem_ld_32x32b_x32(ta + 96u, r3);
+      tmem_ld_wait();
+      if (head >= nh) continue;  // past the last head (odd head count): nothing to store
+      float v[kQkvD];
 #pragma unroll
-      for (int j = 0; j < kQkvD; j += 8) {
-        Vec16<__nv_bfloat16> o;
-        float f[8];
+      for (int i = 0; i < 32; ++i) {
+        v[i] = __uint_as_float(r0[i]);
+        v[32 + i] = __uint_as_float(r1[i]);
+        v[64 + i] = __uint_as_float(r2[i]);
+        v[96 + i] = __uint_as_float(r3[i]);
+      }
+      if (head < nqk) {
+        float ss = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = v[j + i];
-        o.from_float(f);
-        st_global_v4(dst + j, o.raw);
+        for (int i = 0; i < kQkvD; ++i) ss = fmaf(v[i], v[i], ss);
+        const float inv = rsqrtf(ss * (1.0f / kQkvD) + eps);
+#pragma unroll
+        for (int i = 0; i < kQkvD; ++i) v[i] *= inv;
+        if constexpr (RD > 0) {
+#pragma unroll
+          for (int i = 0; i < RD / 2; ++i) {
+            const float a = v[i], b = v[i + RD / 2];
+            v[i] = a * cv[i] - b * sv[i];
+            v[i + RD / 2] = b * cv[i] + a * sv[i];
+          }
+        }
+        if (row_ok) rstd[static_cast<int64_t>(row) * nqk + head] = inv;
+      }
+      // stage the bf16 row as two 32x64 boxes (128B swizzle) and store with TMA
+      if (hs > 0) {
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+      }
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int e = b * 64 + c * 8;
+          uint32_t w[4];
+#pragma unroll
+          for (int k2 = 0; k2 < 4; ++k2) {
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[e + 2 * k2], v[e + 2 * k2 + 1]);
+            w[k2] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          st_shared_v4(buf + static_cast<uint32_t>(b * kBoxBytes + lane * 128 + ((c ^ (lane & 7)) << 4)),
+                       make_uint4(w[0], w[1], w[2], w[3]));
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const CUtensorMap* map = head < Hq ? &ep.map_q : (head < nqk ? &ep.map_k : &ep.map_v);
+        const int hh = head < Hq ? head : (head < nqk ? head - Hq : head - nqk);
+        const int r0w = m_tile * kBM + quad * 32;
+        tma_store_2d(map, hh * kQkvD, r0w, buf);
+        tma_store_2d(map, hh * kQkvD + 64, r0w, buf + kBoxBytes);
+        bulk_commit_group();
       }
     }
+    if (lane == 0) bulk_wait_group_read<0>();
+    __syncwarp();
   }
 };
 
@@ -163,8 +222,8 @@ static QkvBwdPlan qkv_bwd_plan(int64_t M, int64_t C, int64_t Hq, int64_t Hk) {
 template <int RD>
 static int qkv_fwd_launch(const CUtensorMap& mx, const CUtensorMap& mw, const GemmParams& p,
                           const typename EpiQKV<RD>::Params& ep, cudaStream_t s) {
-  return launch_gemm_sm100<kQkvD, kQkvStages, false, false, EpiQKV<RD>>(mx, mx, mx, mw, p, ep, s,
-                                                                         HLM_KERNEL_QKV_FWD);
+  return launch_gemm_sm100<kQkvBN, kQkvStages, false, false, EpiQKV<RD>>(mx, mx, mx, mw, p, ep, s,
+                                                                          HLM_KERNEL_QKV_FWD);
 }
 
 }  // namespace hlm
@@ -192,18 +251,23 @@ extern "C" int hlm_qkv_rope_fwd(const void* x, const void* w_qkv, const void* co
   const int64_t nqkv = (Hq + 2 * Hk) * kQkvD;
   CUtensorMap mx, mw;
   if (!encode_bf16_map(&mx, x, C, M, C, kBM)) return HLM_ERR_DRIVER;
-  if (!encode_bf16_map(&mw, w_qkv, C, nqkv, C, kQkvD)) return HLM_ERR_DRIVER;
+  if (!encode_bf16_map(&mw, w_qkv, C, nqkv, C, kQkvBN)) return HLM_ERR_DRIVER;
+  if (rotary_dim > 0 && (!host_aligned16(cos) || !host_aligned16(sin) ||
+                         (cs_stride_t * (cs_dtype == HLM_F32 ? 4 : 2)) % 16 != 0))
+    return HLM_ERR_UNSUPPORTED;
+  if (cs_dtype == HLM_F16) return HLM_ERR_UNSUPPORTED;
   GemmParams p;
-  gemm_tiling(p, static_cast<int>(M), static_cast<int>(nqkv), static_cast<int>(C), kQkvD, 1);
+  gemm_tiling(p, static_cast<int>(M), static_cast<int>(nqkv), static_cast<int>(C), kQkvBN, 1);
   p.err = device_error_ptr();
   if (p.err == nullptr) return HLM_ERR_LAUNCH;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 #define HLM_QKV_CASE(RDV)                                  \
   case RDV: {                                              \
     EpiQKV<RDV>::Params ep;                                \
-    ep.q_out = static_cast<__nv_bfloat16*>(q_out);         \
-    ep.k_out = static_cast<__nv_bfloat16*>(k_out);         \
-    ep.v_out = static_cast<__nv_bfloat16*>(v_out);         \
+    if (!encode_bf16_map(&ep.map_q, q_out, Hq * kQkvD, M, Hq * kQkvD, 32) ||   \
+        !encode_bf16_map(&ep.map_k, k_out, Hk * kQkvD, M, Hk * kQkvD, 32) ||   \
+        !encode_bf16_map(&ep.map_v, v_out, Hk * kQkvD, M, Hk * kQkvD, 32))     \
+      return HLM_ERR_DRIVER;                               \
     ep.rstd = rstd;                                        \
     ep.cosp = cos;                                         \
     ep.sinp = sin;                                         \

@@ -174,14 +174,16 @@ def qkv_projection_rope(x: torch.Tensor, w_qkv: torch.Tensor, cos: torch.Tensor,
     """Fused x @ w_qkv^T + head split + QK-norm + RoPE (QKVProjection, model.py:92-126).
 
     Runs as one tcgen05 GEMM with the norm/RoPE in its epilogue when
-    head_dim == 128 and rotary_dim is 0/16/32/64/128; otherwise as the tcgen05
-    GEMM followed by the standalone qk_norm_rope kernel.
+    head_dim == 128, rotary_dim is 0/16/32/64/128 and cos/sin are bf16 or fp32;
+    otherwise as the reference structure (nn.Linear GEMM, strided split) feeding
+    the standalone qk_norm_rope kernel.
     """
     _cuda_only(x, "qkv_projection_rope")
     B, T, C = x.shape
     head_dim = w_qkv.shape[0] // (n_head + 2 * n_kv_head)
     rd = cos.shape[-1]
-    if ops.fused_qkv_supported(head_dim, rd, C) and x.dtype == torch.bfloat16:
+    if (ops.fused_qkv_supported(head_dim, rd, C) and x.dtype == torch.bfloat16
+            and cos.dtype in (torch.bfloat16, torch.float32)):
         q, k, v, _ = ops.qkv_rope(x, w_qkv, cos, sin, n_head, n_kv_head, eps)
         return q, k, v
     qkv = F.linear(x, w_qkv)
