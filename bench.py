@@ -396,6 +396,18 @@ def bench_d12(args, d: Dist, device) -> dict:
     C, V, Hd = s.config.n_embd, s.config.vocab_size, 3 * s.config.n_head * s.config.head_dim
     flops = {"lm_logits": 2.0 * M * C * V, "lm_dx": 2.0 * M * C * V, "lm_dw": 2.0 * M * C * V,
              "qkv_fwd": 2.0 * M * C * Hd, "qkv_dx": 2.0 * M * C * Hd, "qkv_dw": 2.0 * M * C * Hd}
+    # algorithmic HBM bytes per launch of the memory-bound kernels (bf16 = 2 bytes)
+    Hm, Dq = s.config.mlp_hidden, s.config.n_head * s.config.head_dim
+    n_fwd = D12_KERNELS["rmsnorm_fwd"]
+    bytes_ = {
+        "swiglu_fwd": 2.0 * M * 3 * Hm,           # read gate_up [M,2H], write [M,H]
+        "swiglu_bwd": 2.0 * M * 5 * Hm,           # read gate_up + grad [M,H], write [M,2H]
+        # one weightless norm (read x, write norm) + residual variants (read 2, write 2)
+        "rmsnorm_fwd": 2.0 * M * C * (2 + 4 * (n_fwd - 1)) / n_fwd,
+        "rmsnorm_bwd": 2.0 * M * C * 3,           # read out + grad_norm, write grad (residual grad fused)
+        "qkv_bwd_norm": 2.0 * M * Dq * 6,         # read q, k, dq, dk; write dq_in, dk_in
+        "lm_dlogits": 4.0 * M * V,                # bf16 logits read + dlogits written in place
+    }
     breakdown, totals = {}, {}
     for k, t in timers.items():
         ts = t.times_ms()
@@ -407,8 +419,10 @@ def bench_d12(args, d: Dist, device) -> dict:
              "share_of_step": round(sum(ts) / step0_ms, 4)}
         if k in flops:
             e["tflops"] = round(flops[k] / (avg / 1e3) / 1e12, 1)
+        if k in bytes_:
+            e["gbs"] = round(bytes_[k] / (avg / 1e3) / 1e9, 1)
         breakdown[k] = e
-    dominant = max(totals, key=totals.get)
+    dominant = max((k for k in totals if k in flops or k in bytes_), key=totals.get)
     dom_avg = breakdown[dominant]["avg_ms"]
     roofline = {"kernel": dominant, "traffic": traffic_table().get(("d12", dominant))}
     if dominant in flops:
@@ -418,8 +432,10 @@ def bench_d12(args, d: Dist, device) -> dict:
                          "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_src} bf16_tflops_sustained (kernel inside a seconds-long step)"})
     else:
-        roofline.update({"bound": "hbm", "achieved": None, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": None, "peak_source": f"{peak_src} hbm_gbs"})
+        achieved = bytes_[dominant] / (dom_avg / 1e3) / 1e9
+        roofline.update({"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "peak_source": f"{peak_src} hbm_gbs"})
 
     # ---- end to end: every micro-batch copied from pinned host memory, loss read back per step
     host = [(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in batches]

@@ -2,13 +2,14 @@
 //
 //   D[M, N] (+)= A[M, K] * B[N, K]^T      bf16 operands, fp32 accumulation in TMEM
 //
-// Roles (192 threads, one CTA per SM, grid = min(#tiles, #SMs)):
+// Roles (one CTA per SM, grid = min(#tiles, #SMs)):
 //   warp 0      : one thread issues TMA loads (cp.async.bulk.tensor, 128-byte
 //                 swizzle) into a STAGES-deep shared-memory ring
 //   warp 1      : allocates TMEM; one thread issues tcgen05.mma (M=128, N=BN,
 //                 K=16) and tcgen05.commit to release stages / publish tiles
-//   warps 2..5  : epilogue; warp w reads TMEM lanes 32*(w%4)..+31 (one
-//                 accumulator row per thread) and runs the Epi functor
+//   next EPI_WARPS warps (4 or 8): epilogue; warp w reads TMEM lanes
+//                 32*(w%4)..+31 (one accumulator row per thread); with 8
+//                 warps two warps share a lane quadrant and split its columns
 // Two accumulators of BN columns each live in TMEM, so the epilogue of tile i
 // overlaps the MMAs of tile i+1.
 //
@@ -31,8 +32,12 @@ namespace hlm {
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int kUmmaK = 16;
-constexpr int kGemmThreads = 192;
 constexpr int kEpiWarp0 = 2;
+
+template <int EPI_WARPS>
+constexpr int gemm_threads() {
+  return 32 * (2 + EPI_WARPS);
+}
 
 struct GemmParams {
   int M, N, K;
@@ -93,14 +98,15 @@ HLM_DEVICE bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
   return true;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS = 4>
+__global__ void __launch_bounds__(gemm_threads<EPI_WARPS>(), 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA0,
                       const __grid_constant__ CUtensorMap tmA1,
                       const __grid_constant__ CUtensorMap tmA2,
                       const __grid_constant__ CUtensorMap tmB, const GemmParams p,
                       const __grid_constant__ typename Epi::Params ep) {
   using L = GemmSmem<BN, STAGES>;
+  static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -123,7 +129,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(TFULL_BAR(a), 1);
-      mbar_init(TEMPTY_BAR(a), 4);  // one arrival per epilogue warp
+      mbar_init(TEMPTY_BAR(a), EPI_WARPS);  // one arrival per epilogue warp
     }
     fence_mbar_init();
     prefetch_tensormap(&tmA0);
@@ -251,7 +257,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    constexpr int kParts = EPI_WARPS / 4;
     const int quad = warp & 3;
+    const int part = (warp - kEpiWarp0) >> 2;
     int it = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++it) {
       int m_tile, n_tile, split;
@@ -262,8 +270,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      Epi::template run<BN>(ep, p, base_ptr + L::kEpiOffset, taddr, m_tile, n_tile, split, quad,
-                            lane);
+      Epi::template run<BN, kParts>(ep, p, base_ptr + L::kEpiOffset, taddr, m_tile, n_tile, split,
+                                    quad, part, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(TEMPTY_BAR(acc));
@@ -296,14 +304,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 bool encode_bf16_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                      uint64_t ld, uint32_t box_outer);
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS = 4>
 int launch_gemm_sm100(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& a2,
                       const CUtensorMap& b, const GemmParams& p, const typename Epi::Params& ep,
                       cudaStream_t stream, int kernel_id) {
   using L = GemmSmem<BN, STAGES>;
-  auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, Epi>;
-  const int smem = L::kEpiOffset + Epi::kSmemBytes + 1024;
-  static_assert(L::kEpiOffset + Epi::kSmemBytes + 1024 <= 232448, "shared memory budget exceeded");
+  auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, Epi, EPI_WARPS>;
+  const int smem = L::kEpiOffset + Epi::template smem_bytes<EPI_WARPS>() + 1024;
+  static_assert(L::kEpiOffset + Epi::template smem_bytes<EPI_WARPS>() + 1024 <= 232448,
+                "shared memory budget exceeded");
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return HLM_ERR_LAUNCH;
   const int total = p.m_tiles * p.n_tiles * p.splits;
@@ -312,7 +321,7 @@ int launch_gemm_sm100(const CUtensorMap& a0, const CUtensorMap& a1, const CUtens
   if (grid > total) grid = total;
   {
     LaunchScope scope(kernel_id, stream);
-    kern<<<grid, kGemmThreads, smem, stream>>>(a0, a1, a2, b, p, ep);
+    kern<<<grid, gemm_threads<EPI_WARPS>(), smem, stream>>>(a0, a1, a2, b, p, ep);
   }
   return launch_status();
 }
@@ -346,17 +355,22 @@ struct EpiStore {
     int vec_ok;            // ldd % 8 == 0 and d 16-byte aligned
     const float* alpha;    // optional device scalar: D = alpha * acc (+ D)
   };
-  static constexpr int kSmemBytes = 0;
+  template <int EPI_WARPS>
+  static constexpr int smem_bytes() {
+    return 0;
+  }
 
-  template <int BN>
+  // Warp `part` of kParts sharing this lane quadrant takes every kParts-th
+  // 32-column group.
+  template <int BN, int kParts>
   static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t* /*smem*/,
-                             uint32_t taddr, int m_tile, int n_tile, int split, int quad,
+                             uint32_t taddr, int m_tile, int n_tile, int split, int quad, int part,
                              int lane) {
     const int row = m_tile * kBM + quad * 32 + lane;
     const bool row_ok = row < p.M;
     const float alpha = ep.alpha != nullptr ? *ep.alpha : 1.0f;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = part; c < BN / 32; c += kParts) {
       uint32_t r[32];
       tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), r);
       tmem_ld_wait();

@@ -113,6 +113,24 @@ HLM_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `hint_ns`; it
+// resumes as soon as the phase completes.  Waiting this way keeps idle roles
+// (e.g. an epilogue warp waiting out a long K loop) from spinning and taking
+// issue slots and shared-memory cycles from the warps that do work.
+HLM_DEVICE bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kWaitSliceNs = 20000;  // suspend slice between timeout checks
+
 // Bounded wait on phase `parity` of an mbarrier.  Returns false (and records
 // `code` in the error word) if the phase did not complete within the timeout.
 // The error word is sticky across launches, so it is not used to cut waits
@@ -120,9 +138,33 @@ HLM_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 HLM_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
-  uint32_t n = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if (((++n) & 63u) == 0u && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+  while (!mbar_try_wait_sleep(bar, parity, kWaitSliceNs)) {
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      record_error(err, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+// try_wait with cluster-scope acquire (pairs with mbar_arrive_cluster).
+HLM_DEVICE bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire, for barriers that the peer CTA of a
+// pair arrives on.
+HLM_DEVICE bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* err, int code) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait_cluster(bar, parity, kWaitSliceNs)) {
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
       record_error(err, code);
       return false;
     }
@@ -189,6 +231,14 @@ HLM_DEVICE uint4 ld_shared_v4(uint32_t addr) {
   return v;
 }
 
+// L2 prefetch of a 2-D box described by a tensor map (no shared-memory write).
+HLM_DEVICE void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
 HLM_DEVICE void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -235,6 +285,73 @@ HLM_DEVICE void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, ui
 HLM_DEVICE void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    bar)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// CTA pairs (clusters of two CTAs on one TPC) for tcgen05 cta_group::2: one
+// thread of the even CTA issues an MMA with M = 256 whose A rows 0..127 and
+// 128..255 live in the two CTAs' shared memory at the same offset, B columns
+// split likewise, and D rows in each CTA's own TMEM.  No TMA load here reads
+// another CTA's memory or fans out to several CTAs: every load stays CTA-local.
+// ---------------------------------------------------------------------------
+HLM_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+HLM_DEVICE uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+HLM_DEVICE uint32_t num_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+HLM_DEVICE uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier given by a cluster address (possibly the peer CTA's),
+// releasing this thread's prior writes at cluster scope.
+HLM_DEVICE void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+HLM_DEVICE void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+HLM_DEVICE void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+HLM_DEVICE void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+HLM_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+HLM_DEVICE void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the mbarrier at cluster address `bar_cluster` (this CTA's or the
+// peer's) once every pair MMA issued so far by this thread has completed.
+HLM_DEVICE void tc_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar_cluster)
                : "memory");
 }
 
@@ -348,6 +465,37 @@ HLM_DEVICE float load_cs(const void* p, int64_t idx, int cs_dtype) {
     default:
       return static_cast<const float*>(p)[idx];
   }
+}
+
+// 2^x with the hardware approximation (PTX ex2.approx.ftz.f32): results below
+// the smallest normal float flush to zero, which is harmless where the values
+// are softmax terms.
+HLM_DEVICE float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// bf16 pair (packed, low half first) -> two floats; exact.
+HLM_DEVICE float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+HLM_DEVICE float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+HLM_DEVICE uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// Round-to-nearest-even of two finite floats to a bf16 pair on the integer
+// pipe (add 0x7fff plus the lsb of the kept half, keep the high halves), for
+// loops where the conversion unit is already busy with ex2.  Not for NaN/inf.
+HLM_DEVICE uint32_t pack_bf16x2_alu(float lo, float hi) {
+  uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
+  a += 0x7fffu + ((a >> 16) & 1u);
+  b += 0x7fffu + ((b >> 16) & 1u);
+  return __byte_perm(a, b, 0x7632);
+}
+HLM_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h2);
 }
 
 HLM_DEVICE float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }

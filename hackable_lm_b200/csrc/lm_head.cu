@@ -10,7 +10,7 @@
 //      (max, sum exp) pair; the target logit is picked up in the tile that
 //      holds it.  Full fp32 logits never exist in memory.
 //   2. finalize      lse[row] = combine of the per-tile pairs; per-row loss;
-//      deterministic per-block loss sums.
+//      deterministic per-block loss sums; per-row softmax data.
 //   3. dlogits       in place: P = exp(S - lse) - onehot(target), zero for
 //      ignored rows (the reference's in-place gradient overwrite,
 //      kernels.py:315-318, without the 1/n factor)
@@ -24,6 +24,8 @@ namespace hlm {
 
 constexpr int kLmBN = 256;
 constexpr int kLmStages = 4;
+constexpr int kLmEpiWarps = 8;
+constexpr int kLmEpiParts = kLmEpiWarps / 4;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -34,94 +36,120 @@ struct LmStats {
   int bad_target; // count of targets outside [0, V) that are not ignore_index
 };
 
-// Epilogue of the logits GEMM.  Per warp (32 accumulator rows) and 64-column
-// group: two tcgen05.ld, round to bf16 (the reference's logits dtype), fold the
-// rounded values into the row's running (max, sum exp), pick up the target
-// logit, and write the bf16 group into a 128B-swizzled shared-memory staging
-// buffer (conflict-free 16-byte stores) that one lane then writes to global
-// memory with a TMA tensor store -- full 128-byte lines instead of per-thread
-// partial-sector stores.  Two staging buffers per warp alternate so the
-// conversion of group g+1 overlaps the store of group g.
+// Epilogue of the logits GEMM, run by 8 warps: two per TMEM lane quadrant,
+// each taking every other 64-column group of the 256-column tile.  Per group:
+// two tcgen05.ld (64 fp32), round to bf16 pairs (the reference's logits
+// dtype), group max on the packed pairs, fold the rounded values into the
+// row's running (max, sum 2^(x log2 e - max log2 e)), pick up the target logit
+// in the group that holds it, and stage the bf16 group in a 128B-swizzled
+// buffer (conflict-free 16-byte stores) that one lane writes to global memory
+// with a TMA tensor store -- full 128-byte lines instead of per-thread
+// partial-sector stores.
 struct EpiLogitsLSE {
   struct Params {
     alignas(64) CUtensorMap store_map;  // logits [rows][V] bf16, box {64, 32}, 128B swizzle
-    float2* partial;         // [n_tiles][rows] (max, sum exp(x - max))
+    float2* partial;         // [n_tiles * parts][rows] (max, sum exp(x - max))
     float* tgt_logit;        // [rows]
     const int64_t* targets;  // [rows]
     int V;
     int rows;
   };
-  static constexpr int kStageBytes = 32 * 128;                 // one 32x64 bf16 box
-  static constexpr int kSmemBytes = 4 * 2 * kStageBytes;       // 4 warps x 2 buffers
+  static constexpr int kStageBytes = 32 * 128;  // one 32x64 bf16 box per warp
+  template <int EPI_WARPS>
+  static constexpr int smem_bytes() {
+    return EPI_WARPS * kStageBytes;
+  }
 
-  template <int BN>
+  template <int BN, int kParts>
   static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t* smem, uint32_t taddr,
-                             int m_tile, int n_tile, int, int quad, int lane) {
+                             int m_tile, int n_tile, int, int quad, int part, int lane) {
     const int row = m_tile * kBM + quad * 32 + lane;
     const bool row_ok = row < p.M;
-    const int64_t tgt = row_ok ? ep.targets[row] : -1;
     const int n0 = n_tile * BN;
-    const uint32_t stage0 = smem_u32(smem) + static_cast<uint32_t>(quad * 2 * kStageBytes);
+    // target column relative to this tile (-1: not in this tile)
+    int trel = -1;
+    if (row_ok) {
+      const int64_t rel = ep.targets[row] - n0;
+      if (rel >= 0 && rel < BN) trel = static_cast<int>(rel);
+    }
+    const uint32_t buf = smem_u32(smem) + static_cast<uint32_t>((part * 4 + quad) * kStageBytes);
     float m_run = -INFINITY, s_run = 0.0f;
 #pragma unroll 1
-    for (int g = 0; g < BN / 64; ++g) {
-      uint32_t r[64];
-      tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(g * 64), *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(g * 64 + 32),
-                         *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      tmem_ld_wait();
+    for (int g = part; g < BN / 64; g += kParts) {
       const int col0 = n0 + g * 64;
-      float v[64];
-      float cmax = -INFINITY;
-      uint32_t packed[32];
+      uint32_t pk[32];
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(g * 64), r0);
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(g * 64 + 32), r1);
+        tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 64; j += 2) {
-        const __nv_bfloat162 h2 =
-            __floats2bfloat162_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
-        packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h2);
-        const float2 f2 = __bfloat1622float2(h2);
-        v[j] = (col0 + j < ep.V) ? f2.x : -INFINITY;
-        v[j + 1] = (col0 + j + 1 < ep.V) ? f2.y : -INFINITY;
-        cmax = fmaxf(cmax, fmaxf(v[j], v[j + 1]));
+        for (int j = 0; j < 16; ++j) {
+          pk[j] = pack_bf16x2(__uint_as_float(r0[2 * j]), __uint_as_float(r0[2 * j + 1]));
+          pk[16 + j] = pack_bf16x2(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1]));
+        }
       }
-      if (tgt >= col0 && tgt < col0 + 64) {
-        float tl = 0.0f;
+      if (col0 + 64 > ep.V) {
+        // ragged last group: columns at or past V (V is even) read as -inf
 #pragma unroll
-        for (int j = 0; j < 64; ++j)
-          if (col0 + j == tgt) tl = v[j];
-        ep.tgt_logit[row] = tl;
+        for (int j = 0; j < 32; ++j)
+          if (col0 + 2 * j >= ep.V) pk[j] = 0xff80ff80u;
       }
-      if (cmax > -INFINITY) {
-        const float new_m = fmaxf(m_run, cmax);
+      // group max on the packed pairs (tree), then across the pair
+      float gmax;
+      {
+        uint32_t t[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) t[j] = max_bf16x2(pk[j], pk[j + 16]);
+#pragma unroll
+        for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+          for (int j = 0; j < w; ++j) t[j] = max_bf16x2(t[j], t[j + w]);
+        gmax = fmaxf(bf16_lo(t[0]), bf16_hi(t[0]));
+      }
+      const float new_m = fmaxf(m_run, gmax);
+      if (new_m > -INFINITY) {
         const float nm2 = new_m * kLog2e;
-        float sum = 0.0f;
+        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 64; ++j) sum += exp2f(fmaf(v[j], kLog2e, -nm2));
-        s_run = s_run * exp2f((m_run - new_m) * kLog2e) + sum;
+        for (int j = 0; j < 32; j += 2) {
+          s0 += ex2_ftz(fmaf(bf16_lo(pk[j]), kLog2e, -nm2));
+          s1 += ex2_ftz(fmaf(bf16_hi(pk[j]), kLog2e, -nm2));
+          s2 += ex2_ftz(fmaf(bf16_lo(pk[j + 1]), kLog2e, -nm2));
+          s3 += ex2_ftz(fmaf(bf16_hi(pk[j + 1]), kLog2e, -nm2));
+        }
+        s_run = s_run * ex2_ftz((m_run - new_m) * kLog2e) + ((s0 + s1) + (s2 + s3));
         m_run = new_m;
       }
-      // ---- stage the bf16 group (row = lane, 8 chunks of 16 B, 128B swizzle) and store it
-      const uint32_t buf = stage0 + static_cast<uint32_t>((g & 1) * kStageBytes);
-      if (g >= 2) {
-        if (lane == 0) bulk_wait_group_read<1>();  // the store that last used `buf` has read it
+      if (col0 < ep.V) {
+        // the store that last used `buf` must have read it
+        if (lane == 0) bulk_wait_group_read<0>();
         __syncwarp();
-      }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t addr = buf + static_cast<uint32_t>(lane * 128 + ((c ^ (lane & 7)) << 4));
-        st_shared_v4(addr, make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2],
-                                      packed[4 * c + 3]));
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_store_2d(&ep.store_map, col0, m_tile * kBM + quad * 32, buf);
-        bulk_commit_group();
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t addr = buf + static_cast<uint32_t>(lane * 128 + ((c ^ (lane & 7)) << 4));
+          st_shared_v4(addr, make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]));
+        }
+        // the target logit, read back from this thread's own staged row
+        const int d = trel - g * 64;
+        if (static_cast<unsigned>(d) < 64u) {
+          const uint32_t addr = buf + static_cast<uint32_t>(lane * 128 + (((d >> 3) ^ (lane & 7)) << 4) +
+                                                           (d & 7) * 2);
+          uint16_t h;
+          asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(addr) : "memory");
+          ep.tgt_logit[row] = __uint_as_float(static_cast<uint32_t>(h) << 16);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&ep.store_map, col0, m_tile * kBM + quad * 32, buf);
+          bulk_commit_group();
+        }
       }
     }
-    if (lane == 0) bulk_wait_group_read<0>();  // staging buffers free for the next tile
-    __syncwarp();
-    if (row_ok) ep.partial[static_cast<int64_t>(n_tile) * ep.rows + row] = make_float2(m_run, s_run);
+    if (row_ok)
+      ep.partial[static_cast<int64_t>(n_tile * kParts + part) * ep.rows + row] =
+          make_float2(m_run, s_run);
   }
 };
 
@@ -162,26 +190,36 @@ __global__ void __launch_bounds__(1024) lm_count_valid_kernel(const int64_t* __r
   }
 }
 
-// One thread per row: lse, per-row loss, per-block loss sums.
+// One thread per row: lse, per-row loss, per-block loss sums, and the row's
+// softmax data for the backward: {bits of lse*log2(e), target} for a valid
+// row, {+inf, -1} for an ignored row (its gradient row is then exactly zero).
 __global__ void __launch_bounds__(256) lm_finalize_kernel(
     const float2* __restrict__ partial, int n_parts, const float* __restrict__ tgt_logit,
-    const int64_t* __restrict__ targets, int rows, int64_t V, int64_t ignore_index,
-    float* __restrict__ lse_out, float* __restrict__ block_sums) {
+    const int64_t* __restrict__ targets, int rows, int info_rows, int64_t V, int64_t ignore_index,
+    int2* __restrict__ info_out, float* __restrict__ block_sums) {
   __shared__ float s_sum[8];
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   float loss = 0.0f;
+  if (row >= rows && row < info_rows) info_out[row] = make_int2(__float_as_int(INFINITY), -1);
   if (row < rows) {
-    float m = -INFINITY;
-    for (int t = 0; t < n_parts; ++t) m = fmaxf(m, partial[static_cast<int64_t>(t) * rows + row].x);
-    float s = 0.0f;
+    // one pass: online combine of the per-(tile, part) (max, sum) pairs
+    float m = -INFINITY, s = 0.0f;
     for (int t = 0; t < n_parts; ++t) {
       const float2 pr = partial[static_cast<int64_t>(t) * rows + row];
-      if (pr.y > 0.0f) s += pr.y * exp2f((pr.x - m) * kLog2e);
+      if (!(pr.y > 0.0f)) continue;
+      if (pr.x > m) {
+        s = s * exp2f((m - pr.x) * kLog2e) + pr.y;
+        m = pr.x;
+      } else {
+        s += pr.y * exp2f((pr.x - m) * kLog2e);
+      }
     }
     const float lse = m + log2f(s) * kLn2;
-    lse_out[row] = lse;
     const int64_t t = targets[row];
-    if (t != ignore_index && t >= 0 && t < V) loss = lse - tgt_logit[row];
+    const bool valid = t != ignore_index && t >= 0 && t < V;
+    if (valid) loss = lse - tgt_logit[row];
+    info_out[row] = valid ? make_int2(__float_as_int(lse * kLog2e), static_cast<int>(t))
+                          : make_int2(__float_as_int(INFINITY), -1);
   }
   loss = warp_sum(loss);
   if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = loss;
@@ -213,42 +251,43 @@ __global__ void __launch_bounds__(256) lm_loss_reduce_kernel(const float* __rest
   }
 }
 
-// In place: logits -> softmax - onehot, zero rows for ignored targets.  The
-// 1/n_valid scale is applied in fp32 by the dX/dW GEMM epilogues: folded into
-// the bf16 values it would carry one rounding error shared by every element.
+// Rows of the per-row softmax data are padded to a multiple of 128.
+static inline int64_t lm_info_rows(int64_t rows) { return (rows + kBM - 1) / kBM * kBM; }
+
+// In place: S -> P = softmax - onehot = 2^(S log2 e - lse log2 e) - [col == target],
+// rounded to bf16 (the reference's in-place gradient overwrite,
+// kernels.py:315-318); ignored rows carry lse log2 e = +inf and become zero.
+// The 1/n_valid scale is applied in fp32 by the dX/dW GEMM epilogues: folded
+// into the bf16 values it would carry one rounding error shared by every
+// element.
 __global__ void __launch_bounds__(256) lm_dlogits_kernel(__nv_bfloat16* __restrict__ logits,
-                                                        const float* __restrict__ lse,
-                                                        const int64_t* __restrict__ targets,
-                                                        int rows, int64_t V, int64_t ignore_index,
-                                                        const LmStats* __restrict__ stats) {
-  (void)stats;
+                                                        const int2* __restrict__ info, int rows,
+                                                        int64_t V) {
   const int64_t vpr = V / 8;
   const int64_t total = static_cast<int64_t>(rows) * vpr;
   for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
        v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t row = v / vpr;
-    const int64_t col0 = (v - row * vpr) * 8;
-    const int64_t t = targets[row];
-    const bool valid = t != ignore_index && t >= 0 && t < V;
+    const int col0 = static_cast<int>((v - row * vpr) * 8);
+    const int2 ri = info[row];
+    const float nl2 = __int_as_float(ri.x);
     __nv_bfloat16* p = logits + row * V + col0;
-    uint4 out = make_uint4(0, 0, 0, 0);
-    if (valid) {
-      const float l2 = lse[row] * kLog2e;
-      Vec16<__nv_bfloat16> in;
-      in.raw = ld_global_v4(p);
-      float f[8];
-      in.to_float(f);
+    const uint4 x = ld_global_v4(p);
+    const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+    float q[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float q = exp2f(fmaf(f[i], kLog2e, -l2));
-        if (col0 + i == t) q -= 1.0f;
-        f[i] = q;
-      }
-      Vec16<__nv_bfloat16> o;
-      o.from_float(f);
-      out = o.raw;
+    for (int e = 0; e < 4; ++e) {
+      q[2 * e] = ex2_ftz(fmaf(bf16_lo(xw[e]), kLog2e, -nl2));
+      q[2 * e + 1] = ex2_ftz(fmaf(bf16_hi(xw[e]), kLog2e, -nl2));
     }
-    st_global_v4(p, out);
+    const int d = ri.y - col0;
+    if (static_cast<unsigned>(d) < 8u) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e == d) q[e] -= 1.0f;
+    }
+    st_global_v4(p, make_uint4(pack_bf16x2(q[0], q[1]), pack_bf16x2(q[2], q[3]),
+                               pack_bf16x2(q[4], q[5]), pack_bf16x2(q[6], q[7])));
   }
 }
 
@@ -269,7 +308,7 @@ struct LmPlan {
   int64_t chunk;
   int n_chunks;
   int n_parts;
-  size_t off_logits, off_partial, off_tgt, off_lse, off_bsum, off_stats, off_dw, total;
+  size_t off_logits, off_partial, off_tgt, off_info, off_bsum, off_stats, off_dw, total;
 };
 
 static inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -288,7 +327,7 @@ static LmPlan lm_plan(int64_t n_tokens, int64_t C, int64_t V, int64_t chunk_toke
   if (chunk < 1) chunk = 1;
   pl.chunk = chunk;
   pl.n_chunks = static_cast<int>((n_tokens + chunk - 1) / chunk);
-  pl.n_parts = static_cast<int>((V + kLmBN - 1) / kLmBN);
+  pl.n_parts = static_cast<int>((V + kLmBN - 1) / kLmBN) * kLmEpiParts;
   size_t off = 0;
   pl.off_logits = off;
   off = align256(off + static_cast<size_t>(chunk) * V * 2);
@@ -296,10 +335,10 @@ static LmPlan lm_plan(int64_t n_tokens, int64_t C, int64_t V, int64_t chunk_toke
   off = align256(off + static_cast<size_t>(pl.n_parts) * chunk * sizeof(float2));
   pl.off_tgt = off;
   off = align256(off + static_cast<size_t>(chunk) * 4);
-  pl.off_lse = off;
-  off = align256(off + static_cast<size_t>(chunk) * 4);
+  pl.off_info = off;
+  off = align256(off + static_cast<size_t>(lm_info_rows(chunk)) * 8);
   pl.off_bsum = off;
-  off = align256(off + static_cast<size_t>((chunk + 255) / 256) * 4);
+  off = align256(off + static_cast<size_t>((lm_info_rows(chunk) + 255) / 256) * 4);
   pl.off_stats = off;
   off = align256(off + sizeof(LmStats));
   pl.off_dw = off;
@@ -342,7 +381,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
   __nv_bfloat16* logits = reinterpret_cast<__nv_bfloat16*>(ws + pl.off_logits);
   float2* partial = reinterpret_cast<float2*>(ws + pl.off_partial);
   float* tgt_logit = reinterpret_cast<float*>(ws + pl.off_tgt);
-  float* lse = reinterpret_cast<float*>(ws + pl.off_lse);
+  int2* info = reinterpret_cast<int2*>(ws + pl.off_info);
   float* bsum = reinterpret_cast<float*>(ws + pl.off_bsum);
   LmStats* stats = reinterpret_cast<LmStats*>(ws + pl.off_stats);
   float* dw_acc = reinterpret_cast<float*>(ws + pl.off_dw);
@@ -384,17 +423,18 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       ep.targets = tc;
       ep.V = static_cast<int>(V);
       ep.rows = rows;
-      const int rc = launch_gemm_sm100<kLmBN, kLmStages, false, false, EpiLogitsLSE>(
+      const int rc = launch_gemm_sm100<kLmBN, kLmStages, false, false, EpiLogitsLSE, kLmEpiWarps>(
           map_h, map_h, map_h, map_w_k, p, ep, s, HLM_KERNEL_LM_LOGITS);
       if (rc != HLM_OK) return rc;
     }
     // 2. lse + loss
     {
-      const int nb = (rows + 255) / 256;
+      const int info_rows = static_cast<int>(lm_info_rows(rows));
+      const int nb = (info_rows + 255) / 256;
       {
         LaunchScope scope(0, s);
-        lm_finalize_kernel<<<nb, 256, 0, s>>>(partial, pl.n_parts, tgt_logit, tc, rows, V,
-                                              ignore_index, lse, bsum);
+        lm_finalize_kernel<<<nb, 256, 0, s>>>(partial, pl.n_parts, tgt_logit, tc, rows, info_rows,
+                                              V, ignore_index, info, bsum);
       }
       {
         LaunchScope scope(0, s);
@@ -410,8 +450,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
       if (blocks > cap) blocks = cap;
       LaunchScope scope(HLM_KERNEL_LM_DLOGITS, s);
-      lm_dlogits_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(logits, lse, tc, rows, V,
-                                                                 ignore_index, stats);
+      lm_dlogits_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(logits, info, rows, V);
       if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
     }
     // 4. grad_hidden[chunk] = P @ W

@@ -24,6 +24,7 @@ namespace hlm {
 constexpr int kQkvD = 128;
 constexpr int kQkvBN = 2 * kQkvD;  // two heads per output tile
 constexpr int kQkvStages = 4;
+constexpr int kQkvEpiWarps = 4;  // 8 (one warp per lane quadrant and head) spills registers
 constexpr int kDwBN = 256;
 constexpr int kDwStages = 4;
 constexpr int kDwTargetUnits = 2 * 148;
@@ -49,18 +50,26 @@ struct EpiQKV {
     float eps;
   };
   static constexpr int kBoxBytes = 32 * 128;
-  static constexpr int kSmemBytes = 4 * 2 * kBoxBytes;  // per warp: one head = 2 boxes
+  // per epilogue warp: one head = 2 boxes
+  template <int EPI_WARPS>
+  static constexpr int smem_bytes() {
+    return EPI_WARPS * 2 * kBoxBytes;
+  }
 
-  template <int BN>
+  // With two warps per lane quadrant (kParts = 2) warp `part` takes head
+  // `part` of the tile; with one it takes both in turn.
+  template <int BN, int kParts>
   static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t* smem, uint32_t taddr,
-                             int m_tile, int n_tile, int, int quad, int lane) {
+                             int m_tile, int n_tile, int, int quad, int part, int lane) {
     static_assert(BN == 2 * kQkvD, "two heads per tile");
+    static_assert(kParts == 1 || kParts == 2, "one or two warps per lane quadrant");
     const int row = m_tile * kBM + quad * 32 + lane;
     const bool row_ok = row < p.M;
     const int Hq = ep.Hq, Hk = ep.Hk, nqk = Hq + Hk, nh = Hq + 2 * Hk;
     const float eps = ep.eps;
     float* const rstd = ep.rstd;
-    const uint32_t buf = smem_u32(smem) + static_cast<uint32_t>(quad * 2 * kBoxBytes);
+    const uint32_t buf =
+        smem_u32(smem) + static_cast<uint32_t>((part * 4 + quad) * 2 * kBoxBytes);
     // cos/sin of this row's position, first RD/2 entries (shared by both heads)
     float cv[RD > 0 ? RD / 2 : 1], sv[RD > 0 ? RD / 2 : 1];
     if constexpr (RD > 0) {
@@ -95,7 +104,7 @@ struct EpiQKV {
       }
     }
 #pragma unroll 1
-    for (int hs = 0; hs < 2; ++hs) {
+    for (int hs = kParts == 2 ? part : 0; hs < 2; hs += kParts) {
       const int head = n_tile * 2 + hs;
       uint32_t r0[32], r1[32], r2[32], r3[32];
       const uint32_t ta = taddr + static_cast<uint32_t>(hs * kQkvD);
@@ -131,7 +140,7 @@ struct EpiQKV {
         if (row_ok) rstd[static_cast<int64_t>(row) * nqk + head] = inv;
       }
       // stage the bf16 row as two 32x64 boxes (128B swizzle) and store with TMA
-      if (hs > 0) {
+      if (kParts == 1 && hs > 0) {
         if (lane == 0) bulk_wait_group_read<0>();
         __syncwarp();
       }
@@ -222,8 +231,8 @@ static QkvBwdPlan qkv_bwd_plan(int64_t M, int64_t C, int64_t Hq, int64_t Hk) {
 template <int RD>
 static int qkv_fwd_launch(const CUtensorMap& mx, const CUtensorMap& mw, const GemmParams& p,
                           const typename EpiQKV<RD>::Params& ep, cudaStream_t s) {
-  return launch_gemm_sm100<kQkvBN, kQkvStages, false, false, EpiQKV<RD>>(mx, mx, mx, mw, p, ep, s,
-                                                                          HLM_KERNEL_QKV_FWD);
+  return launch_gemm_sm100<kQkvBN, kQkvStages, false, false, EpiQKV<RD>, kQkvEpiWarps>(
+      mx, mx, mx, mw, p, ep, s, HLM_KERNEL_QKV_FWD);
 }
 
 }  // namespace hlm
