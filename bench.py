@@ -38,6 +38,9 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+# stdout carries exactly one JSON line: NCCL's own log lines (e.g. its version
+# banner) go to stderr unless the caller chose a log file
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
@@ -494,7 +497,10 @@ def cpu_baseline_d12(reps: int = 2) -> dict:
 # ---------------------------------------------------------------------------
 # per-operator roofline measurements (rank 0, after the headline)
 # ---------------------------------------------------------------------------
-def bench_ops(device, iters: int = 20) -> dict:
+def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
+    """Per-operator rooflines at the BASELINE operator configs.  `only`: run just
+    the operators whose name starts with it (small, known launch sequences for
+    ncu captures: 3 untimed + `iters` timed calls each)."""
     from hackable_lm_b200 import kernels, ops
 
     import oracle
@@ -520,13 +526,20 @@ def bench_ops(device, iters: int = 20) -> dict:
 
     res = {}
 
+    def want(name):
+        return only is None or name.startswith(only)
+
     def hbm(name, fn, nbytes):
+        if not want(name):
+            return
         ms = timed(fn)
         gbs = nbytes / (ms / 1e3) / 1e9
         res[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "bytes": nbytes,
                      "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4)}
 
     def tensor(name, fn, flop):
+        if not want(name):
+            return
         ms = timed(fn)
         tf = flop / (ms / 1e3) / 1e12
         res[name] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1), "flop": flop,
@@ -561,6 +574,9 @@ def bench_ops(device, iters: int = 20) -> dict:
     c1, s1 = c1.to(device), s1.to(device)
     tensor("qkv_rope_fwd X[16384,768] W[2304,768]", lambda: ops.qkv_rope(xq, wq, c1, s1, 6, 6, 1e-6),
            57_982_058_496)
+    if not want("qkv_rope_bwd"):
+        del flush_buf
+        return res
     qo, ko, vo, rs = ops.qkv_rope(xq, wq, c1, s1, 6, 6, 1e-6)
     gv = torch.randn_like(vo)
     tensor("qkv_rope_bwd (dX+dW)", lambda: ops.qkv_rope_backward(xq, wq, qo, ko, rs, c1, s1, dq, dk, gv, 6, 6,
@@ -620,6 +636,10 @@ def main() -> None:
     ap.add_argument("--ref-tokens", type=int, default=1024, help="tokens per reference-arm step")
     ap.add_argument("--tokens", type=int, default=None,
                     help="override the LM-head token count (smaller cases for ncu captures)")
+    ap.add_argument("--op", default=None,
+                    help="run only the per-operator section for operators starting with this name "
+                         "('all' for every operator) and print {\"ops\": ...}; for ncu captures")
+    ap.add_argument("--op-iters", type=int, default=1, help="timed calls per operator with --op")
     args = ap.parse_args()
     if args.tokens is not None:
         LM["M"] = args.tokens
@@ -638,6 +658,12 @@ def main() -> None:
     d.init()
     device = torch.device("cuda", d.local_rank)
     torch.cuda.set_device(device)
+    if args.op is not None:
+        if d.rank == 0:
+            res = bench_ops(device, iters=args.op_iters, only=None if args.op == "all" else args.op)
+            print(json.dumps({"ops": res}), flush=True)
+        d.close()
+        return
     if args.workload == "lm_head":
         out = bench_lm_head(args, d, device)
     else:

@@ -68,6 +68,32 @@ static int plain_gemm(const void* A, const void* B, void* D, int64_t M, int64_t 
                                                               HLM_KERNEL_GEMM);
 }
 
+// CTA-pair version (M >= 256): 256 x BN tiles, each CTA loads half of B.
+template <int BN, bool A_MN, bool B_MN>
+static int plain_gemm_pair(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K,
+                           int64_t lda, int64_t ldb, int64_t ldd, int d_dtype, int accumulate,
+                           cudaStream_t s) {
+  constexpr int STAGES = BN == 256 ? 6 : 8;
+  CUtensorMap ma, mb;
+  bool ok = A_MN ? encode_bf16_map(&ma, A, M, K, lda, 64) : encode_bf16_map(&ma, A, K, M, lda, kBM);
+  ok = ok && (B_MN ? encode_bf16_map(&mb, B, N, K, ldb, 64) : encode_bf16_map(&mb, B, K, N, ldb, BN / 2));
+  if (!ok) return HLM_ERR_DRIVER;
+  GemmParams p;
+  gemm_tiling_pair(p, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), BN, 1);
+  p.err = device_error_ptr();
+  if (p.err == nullptr) return HLM_ERR_LAUNCH;
+  EpiStore::Params ep;
+  ep.d = D;
+  ep.ldd = ldd;
+  ep.split_stride = 0;
+  ep.dtype = d_dtype;
+  ep.accumulate = accumulate;
+  const int esz = d_dtype == HLM_F32 ? 4 : 2;
+  ep.vec_ok = host_aligned16(D) && ((ldd * esz) % 16 == 0);
+  ep.alpha = nullptr;
+  return launch_gemm_pair<BN, STAGES, A_MN, B_MN, EpiStore>(ma, ma, ma, mb, p, ep, s, HLM_KERNEL_GEMM);
+}
+
 }  // namespace hlm
 
 using namespace hlm;
@@ -86,6 +112,22 @@ extern "C" int hlm_gemm_bf16(const void* A, const void* B, void* D, int64_t M, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool wide = N > 128;
   const int am = a_mn_major ? 1 : 0, bm = b_mn_major ? 1 : 0;
+#define HLM_PAIR(BNV, AM, BM)                                                                  \
+  return plain_gemm_pair<BNV, AM, BM>(A, B, D, M, N, K, lda, ldb, ldd, d_dtype, accumulate, s)
+  if (M >= 2 * kBM) {
+    if (wide) {
+      if (!am && !bm) HLM_PAIR(256, false, false);
+      if (!am && bm) HLM_PAIR(256, false, true);
+      if (am && !bm) HLM_PAIR(256, true, false);
+      HLM_PAIR(256, true, true);
+    } else {
+      if (!am && !bm) HLM_PAIR(128, false, false);
+      if (!am && bm) HLM_PAIR(128, false, true);
+      if (am && !bm) HLM_PAIR(128, true, false);
+      HLM_PAIR(128, true, true);
+    }
+  }
+#undef HLM_PAIR
 #define HLM_PLAIN(BNV, AM, BM)                                                                 \
   return plain_gemm<BNV, AM, BM>(A, B, D, M, N, K, lda, ldb, ldd, d_dtype, accumulate, s)
   if (wide) {

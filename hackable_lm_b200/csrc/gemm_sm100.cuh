@@ -295,6 +295,233 @@ __global__ void __launch_bounds__(gemm_threads<EPI_WARPS>(), 1)
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2).  A cluster of two CTAs owns a
+// 256 x BN output tile: CTA r loads A rows 128r..128r+127 of the pair tile and
+// B columns (BN/2) r..(BN/2) r + BN/2 - 1 into its own shared memory (each
+// load counted on the even CTA's stage barrier), one thread of the even CTA
+// issues M = 256 MMAs that read both CTAs' stages, and each CTA's epilogue
+// drains its own 128 accumulator rows from its own TMEM.  Per SM this halves
+// the B traffic into shared memory for the same MMA rate.
+// ---------------------------------------------------------------------------
+template <int BN, int STAGES>
+struct PairSmem {
+  static constexpr int kABytes = kBM * kBK * 2;       // this CTA's 128 A rows
+  static constexpr int kBBytes = (BN / 2) * kBK * 2;  // this CTA's half of B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kNumBars = 2 * STAGES + 4;
+  static constexpr int kTmemSlotOffset = kBarOffset + kNumBars * 8;
+  static constexpr int kEpiOffset = ((kTmemSlotOffset + 16 + 1023) / 1024) * 1024;
+  static constexpr int kTmemCols = 2 * BN;
+  static_assert(BN == 128 || BN == 256, "pair tile N");
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS = 4>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads<EPI_WARPS>(), 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA0,
+                     const __grid_constant__ CUtensorMap tmA1,
+                     const __grid_constant__ CUtensorMap tmA2,
+                     const __grid_constant__ CUtensorMap tmB, const GemmParams p,
+                     const __grid_constant__ typename Epi::Params ep) {
+  using L = PairSmem<BN, STAGES>;
+  static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t bar0 = base + L::kBarOffset;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + L::kTmemSlotOffset);
+  int* err = p.err;
+  // Dynamic shared memory starts at the same offset in both CTAs, so barrier
+  // and stage offsets match across the pair.
+#define FULL_BAR(s) (bar0 + 8u * (s))                    // even CTA: both halves landed
+#define EMPTY_BAR(s) (bar0 + 8u * (STAGES + (s)))        // pair MMAs done with the stage
+#define TFULL_BAR(a) (bar0 + 8u * (2 * STAGES + (a)))
+#define TEMPTY_BAR(a) (bar0 + 8u * (2 * STAGES + 2 + (a)))  // even CTA: both epilogues
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(FULL_BAR(s), 1);
+      mbar_init(EMPTY_BAR(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(TFULL_BAR(a), 1);
+      mbar_init(TEMPTY_BAR(a), 2 * EPI_WARPS);
+    }
+    fence_mbar_init();
+    prefetch_tensormap(&tmA0);
+    if (p.a_seg1 > 0) {
+      prefetch_tensormap(&tmA1);
+      prefetch_tensormap(&tmA2);
+    }
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), L::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // both CTAs' barriers initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  const int total = p.m_tiles * p.n_tiles * p.splits;  // m_tiles counts 256-row pair tiles
+  const int w_first = static_cast<int>(cluster_id_x());
+  const int w_step = static_cast<int>(num_clusters_x());
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_mask = 0, armed_par = 0;
+      bool ok = true;
+      for (int w = w_first; w < total && ok; w += w_step) {
+        int m_pair, n_tile, split;
+        decode_work(w, p, m_pair, n_tile, split);
+        const int m0 = (2 * m_pair + static_cast<int>(rank)) * kBM;
+        const int n0 = n_tile * BN + static_cast<int>(rank) * (BN / 2);
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(EMPTY_BAR(stage), phase ^ 1u, err, kDevErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) {
+            mbar_arrive_expect_tx(FULL_BAR(stage), 2 * L::kStageBytes);
+            armed_mask |= 1u << stage;
+            armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+          }
+          const uint32_t full = mapa_shared(FULL_BAR(stage), 0);
+          const uint32_t sa = base + stage * L::kStageBytes;
+          const uint32_t sb = sa + L::kABytes;
+          const int k0 = kb * kBK;
+          if constexpr (!A_MN) {
+            const CUtensorMap* mp = &tmA0;
+            int kc = k0;
+            if (p.a_seg1 > 0) select_segment(p, kc, mp, &tmA0, &tmA1, &tmA2);
+            tma_load_2d_pair(sa, mp, kc, m0, full);
+          } else {
+#pragma unroll
+            for (int i = 0; i < kBM / 64; ++i) {
+              const CUtensorMap* mp = &tmA0;
+              int mc = m0 + 64 * i;
+              if (p.a_seg1 > 0) select_segment(p, mc, mp, &tmA0, &tmA1, &tmA2);
+              tma_load_2d_pair(sa + i * 8192u, mp, mc, k0, full);
+            }
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(sb, &tmB, k0, n0, full);
+          } else {
+#pragma unroll
+            for (int i = 0; i < BN / 128; ++i) tma_load_2d_pair(sb + i * 8192u, &tmB, n0 + 64 * i, k0, full);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain (even CTA): every armed stage, including the peer's half, has
+      // landed before either CTA releases its shared memory.
+      for (int s = 0; s < STAGES; ++s)
+        if (armed_mask & (1u << s)) mbar_wait_drain(FULL_BAR(s), (armed_par >> s) & 1u, err);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ pair MMA issuer (even CTA)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(2 * kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int w = w_first; w < total && ok; w += w_step, ++it) {
+        int m_pair, n_tile, split;
+        decode_work(w, p, m_pair, n_tile, split);
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+        const int acc = it & 1;
+        const uint32_t acc_par = static_cast<uint32_t>((it >> 1) & 1);
+        if (!mbar_wait_cluster(TEMPTY_BAR(acc), acc_par ^ 1u, err, kDevErrTimeoutTmemEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_cluster(FULL_BAR(stage), phase, err, kDevErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + stage * L::kStageBytes;
+          const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+            const uint64_t adesc = A_MN ? make_sw128_desc(sa + kk * 2048u, 8192u, 1024u)
+                                        : make_sw128_desc(sa + kk * 32u, 16u, 1024u);
+            const uint64_t bdesc = B_MN ? make_sw128_desc(sb + kk * 2048u, 8192u, 1024u)
+                                        : make_sw128_desc(sb + kk * 32u, 16u, 1024u);
+            tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit_pair(EMPTY_BAR(stage));
+          tc_commit_pair(mapa_shared(EMPTY_BAR(stage), 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(TFULL_BAR(acc));
+        tc_commit_pair(mapa_shared(TFULL_BAR(acc), 1));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    constexpr int kParts = EPI_WARPS / 4;
+    const int quad = warp & 3;
+    const int part = (warp - kEpiWarp0) >> 2;
+    int it = 0;
+    for (int w = w_first; w < total; w += w_step, ++it) {
+      int m_pair, n_tile, split;
+      decode_work(w, p, m_pair, n_tile, split);
+      const int acc = it & 1;
+      const uint32_t acc_par = static_cast<uint32_t>((it >> 1) & 1);
+      if (!warp_wait(TFULL_BAR(acc), acc_par, err, kDevErrTimeoutTmemFull, lane)) break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      Epi::template run<BN, kParts>(ep, p, base_ptr + L::kEpiOffset, taddr,
+                                    2 * m_pair + static_cast<int>(rank), n_tile, split, quad, part,
+                                    lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(TEMPTY_BAR(acc), 0));
+    }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
+  }
+
+  // Neither CTA may leave while the other can still signal its barriers or the
+  // pair MMAs can still read its shared memory.
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, L::kTmemCols);
+  }
+#undef FULL_BAR
+#undef EMPTY_BAR
+#undef TFULL_BAR
+#undef TEMPTY_BAR
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -326,6 +553,31 @@ int launch_gemm_sm100(const CUtensorMap& a0, const CUtensorMap& a1, const CUtens
   return launch_status();
 }
 
+// Pair launch: one cluster of two CTAs per two SMs, persistent over the
+// 256 x BN pair tiles (p.m_tiles counts pair tiles: gemm_tiling_pair).
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS = 4>
+int launch_gemm_pair(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& a2,
+                     const CUtensorMap& b, const GemmParams& p, const typename Epi::Params& ep,
+                     cudaStream_t stream, int kernel_id) {
+  using L = PairSmem<BN, STAGES>;
+  auto kern = gemm_pair_kernel<BN, STAGES, A_MN, B_MN, Epi, EPI_WARPS>;
+  const int smem = L::kEpiOffset + Epi::template smem_bytes<EPI_WARPS>() + 1024;
+  static_assert(L::kEpiOffset + Epi::template smem_bytes<EPI_WARPS>() + 1024 <= 232448,
+                "shared memory budget exceeded");
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return HLM_ERR_LAUNCH;
+  const int total = p.m_tiles * p.n_tiles * p.splits;
+  if (total <= 0) return HLM_OK;
+  int pairs = num_sms_of_current_device() / 2;
+  if (pairs > total) pairs = total;
+  if (pairs < 1) pairs = 1;
+  {
+    LaunchScope scope(kernel_id, stream);
+    kern<<<2 * pairs, gemm_threads<EPI_WARPS>(), smem, stream>>>(a0, a1, a2, b, p, ep);
+  }
+  return launch_status();
+}
+
 // Fill the tiling fields of GemmParams.
 inline void gemm_tiling(GemmParams& p, int M, int N, int K, int BN, int splits) {
   p.M = M;
@@ -340,6 +592,12 @@ inline void gemm_tiling(GemmParams& p, int M, int N, int K, int BN, int splits) 
   p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
   p.a_seg1 = 0;
   p.a_seg2 = 0;
+}
+
+// Same for the pair kernel: m_tiles counts 256-row pair tiles.
+inline void gemm_tiling_pair(GemmParams& p, int M, int N, int K, int BN, int splits) {
+  gemm_tiling(p, M, N, K, BN, splits);
+  p.m_tiles = (M + 2 * kBM - 1) / (2 * kBM);
 }
 
 // ---------------------------------------------------------------------------

@@ -192,12 +192,39 @@ HLM_DEVICE void tma_load_2d(uint32_t dst_smem, const CUtensorMap* map, int c0, i
       : "memory");
 }
 
+// TMA load into this CTA's shared memory whose completion is counted on an
+// mbarrier given by cluster address -- the even CTA's barrier of a CTA pair
+// (.cta_group::2).  The source is global memory of this GPU.
+HLM_DEVICE void tma_load_2d_pair(uint32_t dst_smem, const CUtensorMap* map, int c0, int c1,
+                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst_smem),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster)
+      : "memory");
+}
+
 // TMA store of a 2-D box from shared memory (bulk async group of the issuing thread).
 HLM_DEVICE void tma_store_2d(const CUtensorMap* map, int c0, int c1, uint32_t src_smem) {
   asm volatile(
       "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
           reinterpret_cast<uint64_t>(map)),
       "r"(c0), "r"(c1), "r"(src_smem)
+      : "memory");
+}
+// L2 policy that marks written lines first in line for eviction (streamed
+// outputs that should not push reused operands out of L2).
+HLM_DEVICE uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+HLM_DEVICE void tma_store_2d_hint(const CUtensorMap* map, int c0, int c1, uint32_t src_smem,
+                                  uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(src_smem), "l"(policy)
       : "memory");
 }
 HLM_DEVICE void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }

@@ -23,7 +23,8 @@
 namespace hlm {
 
 constexpr int kLmBN = 256;
-constexpr int kLmStages = 4;
+constexpr int kLmStages = 4;      // single-CTA GEMMs (grad_weight)
+constexpr int kLmPairStages = 6;  // CTA-pair GEMMs (logits, grad_hidden)
 constexpr int kLmEpiWarps = 8;
 constexpr int kLmEpiParts = kLmEpiWarps / 4;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -142,7 +143,8 @@ struct EpiLogitsLSE {
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&ep.store_map, col0, m_tile * kBM + quad * 32, buf);
+          // the logits stream must not evict W (re-read by every row tile) from L2
+          tma_store_2d_hint(&ep.store_map, col0, m_tile * kBM + quad * 32, buf, l2_policy_evict_first());
           bulk_commit_group();
         }
       }
@@ -190,44 +192,62 @@ __global__ void __launch_bounds__(1024) lm_count_valid_kernel(const int64_t* __r
   }
 }
 
-// One thread per row: lse, per-row loss, per-block loss sums, and the row's
-// softmax data for the backward: {bits of lse*log2(e), target} for a valid
-// row, {+inf, -1} for an ignored row (its gradient row is then exactly zero).
-__global__ void __launch_bounds__(256) lm_finalize_kernel(
+// Merge of two (max, sum 2^((x - max) log2 e)) pairs; empty pairs have sum 0.
+HLM_DEVICE float2 lse_merge(float2 a, float2 b) {
+  if (!(b.y > 0.0f)) return a;
+  if (!(a.y > 0.0f)) return b;
+  const float m = fmaxf(a.x, b.x);
+  return make_float2(m, a.y * ex2_ftz((a.x - m) * kLog2e) + b.y * ex2_ftz((b.x - m) * kLog2e));
+}
+
+constexpr int kFinRows = 32;    // rows per block (one per lane)
+constexpr int kFinGroups = 8;   // warps per block, each merging every 8th part
+
+// Per row: lse from the per-(tile, part) pairs, the row loss, per-block loss
+// sums, and the row's softmax data for the backward: {bits of lse*log2(e),
+// target} for a valid row, {+inf, -1} for an ignored or padding row (its
+// gradient row is then exactly zero).  Warp g of a block merges parts
+// g, g + 8, ... of the block's 32 rows (lane = row: 256-byte coalesced loads);
+// the eight partial merges are combined in a fixed order.
+__global__ void __launch_bounds__(kFinRows * kFinGroups) lm_finalize_kernel(
     const float2* __restrict__ partial, int n_parts, const float* __restrict__ tgt_logit,
     const int64_t* __restrict__ targets, int rows, int info_rows, int64_t V, int64_t ignore_index,
     int2* __restrict__ info_out, float* __restrict__ block_sums) {
-  __shared__ float s_sum[8];
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  float loss = 0.0f;
-  if (row >= rows && row < info_rows) info_out[row] = make_int2(__float_as_int(INFINITY), -1);
+  __shared__ float2 s_part[kFinGroups][kFinRows];
+  const int lane = threadIdx.x & 31;
+  const int g = threadIdx.x >> 5;
+  const int row = blockIdx.x * kFinRows + lane;
+  float2 acc = make_float2(-INFINITY, 0.0f);
   if (row < rows) {
-    // one pass: online combine of the per-(tile, part) (max, sum) pairs
-    float m = -INFINITY, s = 0.0f;
-    for (int t = 0; t < n_parts; ++t) {
-      const float2 pr = partial[static_cast<int64_t>(t) * rows + row];
-      if (!(pr.y > 0.0f)) continue;
-      if (pr.x > m) {
-        s = s * exp2f((m - pr.x) * kLog2e) + pr.y;
-        m = pr.x;
-      } else {
-        s += pr.y * exp2f((pr.x - m) * kLog2e);
-      }
+    int t = g;
+    for (; t + 3 * kFinGroups < n_parts; t += 4 * kFinGroups) {
+      const float2 p0 = partial[static_cast<int64_t>(t) * rows + row];
+      const float2 p1 = partial[static_cast<int64_t>(t + kFinGroups) * rows + row];
+      const float2 p2 = partial[static_cast<int64_t>(t + 2 * kFinGroups) * rows + row];
+      const float2 p3 = partial[static_cast<int64_t>(t + 3 * kFinGroups) * rows + row];
+      acc = lse_merge(acc, lse_merge(lse_merge(p0, p1), lse_merge(p2, p3)));
     }
-    const float lse = m + log2f(s) * kLn2;
-    const int64_t t = targets[row];
-    const bool valid = t != ignore_index && t >= 0 && t < V;
-    if (valid) loss = lse - tgt_logit[row];
-    info_out[row] = valid ? make_int2(__float_as_int(lse * kLog2e), static_cast<int>(t))
-                          : make_int2(__float_as_int(INFINITY), -1);
+    for (; t < n_parts; t += kFinGroups) acc = lse_merge(acc, partial[static_cast<int64_t>(t) * rows + row]);
   }
-  loss = warp_sum(loss);
-  if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = loss;
+  s_part[g][lane] = acc;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float b = 0.0f;
-    for (int w = 0; w < 8; ++w) b += s_sum[w];
-    block_sums[blockIdx.x] = b;
+  if (g == 0) {
+    float loss = 0.0f;
+    if (row < rows) {
+      float2 m = s_part[0][lane];
+#pragma unroll
+      for (int k = 1; k < kFinGroups; ++k) m = lse_merge(m, s_part[k][lane]);
+      const float lse = m.x + log2f(m.y) * kLn2;
+      const int64_t t = targets[row];
+      const bool valid = t != ignore_index && t >= 0 && t < V;
+      if (valid) loss = lse - tgt_logit[row];
+      info_out[row] = valid ? make_int2(__float_as_int(lse * kLog2e), static_cast<int>(t))
+                            : make_int2(__float_as_int(INFINITY), -1);
+    } else if (row < info_rows) {
+      info_out[row] = make_int2(__float_as_int(INFINITY), -1);
+    }
+    loss = warp_sum(loss);
+    if (lane == 0) block_sums[blockIdx.x] = loss;
   }
 }
 
@@ -338,7 +358,7 @@ static LmPlan lm_plan(int64_t n_tokens, int64_t C, int64_t V, int64_t chunk_toke
   pl.off_info = off;
   off = align256(off + static_cast<size_t>(lm_info_rows(chunk)) * 8);
   pl.off_bsum = off;
-  off = align256(off + static_cast<size_t>((lm_info_rows(chunk) + 255) / 256) * 4);
+  off = align256(off + static_cast<size_t>((lm_info_rows(chunk) + kFinRows - 1) / kFinRows) * 4);
   pl.off_stats = off;
   off = align256(off + sizeof(LmStats));
   pl.off_dw = off;
@@ -399,7 +419,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
 
   // Tensor maps that do not depend on the chunk.
   CUtensorMap map_w_k, map_w_n;
-  if (!encode_bf16_map(&map_w_k, W, C, V, C, kLmBN)) return HLM_ERR_DRIVER;  // B of logits GEMM
+  if (!encode_bf16_map(&map_w_k, W, C, V, C, kLmBN / 2)) return HLM_ERR_DRIVER;  // B half, logits GEMM
   if (!encode_bf16_map(&map_w_n, W, C, V, C, 64)) return HLM_ERR_DRIVER;     // B of dX GEMM
 
   for (int ci = 0; ci < pl.n_chunks; ++ci) {
@@ -414,7 +434,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       CUtensorMap map_h;
       if (!encode_bf16_map(&map_h, Hc, C, rows, C, kBM)) return HLM_ERR_DRIVER;
       GemmParams p;
-      gemm_tiling(p, rows, static_cast<int>(V), static_cast<int>(C), kLmBN, 1);
+      gemm_tiling_pair(p, rows, static_cast<int>(V), static_cast<int>(C), kLmBN, 1);
       p.err = err;
       EpiLogitsLSE::Params ep;
       if (!encode_bf16_map(&ep.store_map, logits, V, rows, V, 32)) return HLM_ERR_DRIVER;
@@ -423,17 +443,17 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       ep.targets = tc;
       ep.V = static_cast<int>(V);
       ep.rows = rows;
-      const int rc = launch_gemm_sm100<kLmBN, kLmStages, false, false, EpiLogitsLSE, kLmEpiWarps>(
+      const int rc = launch_gemm_pair<kLmBN, kLmPairStages, false, false, EpiLogitsLSE, kLmEpiWarps>(
           map_h, map_h, map_h, map_w_k, p, ep, s, HLM_KERNEL_LM_LOGITS);
       if (rc != HLM_OK) return rc;
     }
     // 2. lse + loss
     {
       const int info_rows = static_cast<int>(lm_info_rows(rows));
-      const int nb = (info_rows + 255) / 256;
+      const int nb = (info_rows + kFinRows - 1) / kFinRows;
       {
         LaunchScope scope(0, s);
-        lm_finalize_kernel<<<nb, 256, 0, s>>>(partial, pl.n_parts, tgt_logit, tc, rows, info_rows,
+        lm_finalize_kernel<<<nb, kFinRows * kFinGroups, 0, s>>>(partial, pl.n_parts, tgt_logit, tc, rows, info_rows,
                                               V, ignore_index, info, bsum);
       }
       {
@@ -458,7 +478,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       CUtensorMap map_p;
       if (!encode_bf16_map(&map_p, logits, V, rows, V, kBM)) return HLM_ERR_DRIVER;
       GemmParams p;
-      gemm_tiling(p, rows, static_cast<int>(C), static_cast<int>(V), kLmBN, 1);
+      gemm_tiling_pair(p, rows, static_cast<int>(C), static_cast<int>(V), kLmBN, 1);
       p.err = err;
       EpiStore::Params ep;
       ep.d = static_cast<__nv_bfloat16*>(grad_hidden) + r0 * C;
@@ -468,7 +488,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       ep.accumulate = 0;
       ep.vec_ok = 1;
       ep.alpha = &stats->inv_n;
-      const int rc = launch_gemm_sm100<kLmBN, kLmStages, false, true, EpiStore>(
+      const int rc = launch_gemm_pair<kLmBN, kLmPairStages, false, true, EpiStore>(
           map_p, map_p, map_p, map_w_n, p, ep, s, HLM_KERNEL_LM_DX);
       if (rc != HLM_OK) return rc;
     }

@@ -23,11 +23,10 @@ namespace hlm {
 
 constexpr int kQkvD = 128;
 constexpr int kQkvBN = 2 * kQkvD;  // two heads per output tile
-constexpr int kQkvStages = 4;
+constexpr int kQkvStages = 6;     // CTA-pair stages: 16 KB of A + 16 KB (half) of B
 constexpr int kQkvEpiWarps = 4;  // 8 (one warp per lane quadrant and head) spills registers
 constexpr int kDwBN = 256;
 constexpr int kDwStages = 4;
-constexpr int kDwTargetUnits = 2 * 148;
 
 // Forward epilogue: the tile holds 128 token rows x 2 heads (BN = 256).  Each
 // thread owns one row.  Per head: 4 x tcgen05.ld (128 fp32), then for q/k
@@ -195,15 +194,29 @@ __global__ void __launch_bounds__(256) splitk_reduce_bf16_kernel(const float* __
   }
 }
 
+// Split-K count for the dW GEMM (few output tiles, long K): the smallest split
+// whose work units fill the SM waves to >= 90% (each split adds an fp32 slab
+// to write and reduce), else the best fill found up to 16 splits; every split
+// keeps at least 8 K blocks.
 static inline int qkv_dw_splits(int64_t tokens, int64_t nqkv, int64_t C) {
   const int64_t tiles = ((nqkv + kBM - 1) / kBM) * ((C + kDwBN - 1) / kDwBN);
   const int64_t kblocks = (tokens + kBK - 1) / kBK;
-  int64_t s = (kDwTargetUnits + tiles - 1) / tiles;
-  if (s > kblocks / 4) s = kblocks / 4;
-  if (s < 1) s = 1;
-  // gemm_tiling may merge splits; compute the effective count the same way
-  const int64_t kb_per = (kblocks + s - 1) / s;
-  return static_cast<int>((kblocks + kb_per - 1) / kb_per);
+  const int64_t sms = num_sms_of_current_device();
+  int best = 1;
+  double best_fill = 0.0;
+  for (int64_t s = 1; s <= 16 && s <= kblocks / 8; ++s) {
+    // gemm_tiling may merge splits; evaluate the effective count
+    const int64_t kb_per = (kblocks + s - 1) / s;
+    const int64_t eff = (kblocks + kb_per - 1) / kb_per;
+    const int64_t units = tiles * eff;
+    const double fill = static_cast<double>(units) / (((units + sms - 1) / sms) * sms);
+    if (fill > best_fill + 1e-9) {
+      best_fill = fill;
+      best = static_cast<int>(eff);
+    }
+    if (fill >= 0.9) break;
+  }
+  return best;
 }
 
 static inline size_t a256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -231,7 +244,7 @@ static QkvBwdPlan qkv_bwd_plan(int64_t M, int64_t C, int64_t Hq, int64_t Hk) {
 template <int RD>
 static int qkv_fwd_launch(const CUtensorMap& mx, const CUtensorMap& mw, const GemmParams& p,
                           const typename EpiQKV<RD>::Params& ep, cudaStream_t s) {
-  return launch_gemm_sm100<kQkvBN, kQkvStages, false, false, EpiQKV<RD>, kQkvEpiWarps>(
+  return launch_gemm_pair<kQkvBN, kQkvStages, false, false, EpiQKV<RD>, kQkvEpiWarps>(
       mx, mx, mx, mw, p, ep, s, HLM_KERNEL_QKV_FWD);
 }
 
@@ -260,13 +273,13 @@ extern "C" int hlm_qkv_rope_fwd(const void* x, const void* w_qkv, const void* co
   const int64_t nqkv = (Hq + 2 * Hk) * kQkvD;
   CUtensorMap mx, mw;
   if (!encode_bf16_map(&mx, x, C, M, C, kBM)) return HLM_ERR_DRIVER;
-  if (!encode_bf16_map(&mw, w_qkv, C, nqkv, C, kQkvBN)) return HLM_ERR_DRIVER;
+  if (!encode_bf16_map(&mw, w_qkv, C, nqkv, C, kQkvBN / 2)) return HLM_ERR_DRIVER;  // pair: half of B
   if (rotary_dim > 0 && (!host_aligned16(cos) || !host_aligned16(sin) ||
                          (cs_stride_t * (cs_dtype == HLM_F32 ? 4 : 2)) % 16 != 0))
     return HLM_ERR_UNSUPPORTED;
   if (cs_dtype == HLM_F16) return HLM_ERR_UNSUPPORTED;
   GemmParams p;
-  gemm_tiling(p, static_cast<int>(M), static_cast<int>(nqkv), static_cast<int>(C), kQkvBN, 1);
+  gemm_tiling_pair(p, static_cast<int>(M), static_cast<int>(nqkv), static_cast<int>(C), kQkvBN, 1);
   p.err = device_error_ptr();
   if (p.err == nullptr) return HLM_ERR_LAUNCH;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -387,7 +400,7 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
         !encode_bf16_map(&mb, w_qkv, C, nqkv, C, 64))
       return HLM_ERR_DRIVER;
     GemmParams p;
-    gemm_tiling(p, static_cast<int>(M), static_cast<int>(C), static_cast<int>(nqkv), kDwBN, 1);
+    gemm_tiling_pair(p, static_cast<int>(M), static_cast<int>(C), static_cast<int>(nqkv), kDwBN, 1);
     p.a_seg1 = seg1;
     p.a_seg2 = seg2;
     p.err = err;
@@ -399,8 +412,8 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
     ep.accumulate = 0;
     ep.vec_ok = 1;
     ep.alpha = nullptr;
-    const int rc = launch_gemm_sm100<kDwBN, kDwStages, false, true, EpiStore>(a0, a1, a2, mb, p, ep,
-                                                                              s, HLM_KERNEL_QKV_DX);
+    const int rc = launch_gemm_pair<kDwBN, kQkvStages, false, true, EpiStore>(a0, a1, a2, mb, p, ep, s,
+                                                                             HLM_KERNEL_QKV_DX);
     if (rc != HLM_OK) return rc;
   }
   // 3. grad_w = [dq|dk|dv]^T @ X   (split-K over tokens)
