@@ -503,49 +503,62 @@ def cpu_baseline_d12(reps: int = 2) -> dict:
 # per-operator roofline measurements (rank 0, after the headline)
 # ---------------------------------------------------------------------------
 def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
-    """Per-operator rooflines at the BASELINE operator configs.  `only`: run just
-    the operators whose name starts with it (small, known launch sequences for
-    ncu captures: 3 untimed + `iters` timed calls each)."""
-    from hackable_lm_b200 import kernels, ops
+    """Per-operator rooflines at the BASELINE operator configs.
+
+    L2 policy: inputs larger than L2.  Each operator cycles through enough
+    private copies of its inputs that one cycle reads more than twice the L2
+    size of distinct input bytes, so no call finds its inputs in L2; the time
+    per call is the CUDA-event time of the whole timed loop divided by the
+    number of calls (each call also pays the write-back of the previous call's
+    outputs, as inside a training step).  `only`: run just the operators whose
+    name starts with it (small, known launch sequences for ncu captures: one
+    untimed pass over the copies, then `iters` timed calls)."""
+    from hackable_lm_b200 import ops
 
     import oracle
 
     peaks, _ = load_peaks()
-    flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
 
-    def timed(fn, n=iters):
-        for _ in range(3):
-            fn()
+    def timed(fn, inputs, in_bytes, n=iters):
+        copies = max(2, -(-2 * L2_BYTES // max(1, in_bytes)))
+        sets = [inputs] + [tuple(t.clone() if isinstance(t, torch.Tensor) else t for t in inputs)
+                           for _ in range(copies - 1)]
+        for st in sets:  # untimed pass (allocations, first-launch work)
+            fn(*st)
         torch.cuda.synchronize()
-        total = 0.0
-        for _ in range(n):
-            flush_buf.zero_()
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record()
-            fn()
-            b.record()
-            torch.cuda.synchronize()
-            total += a.elapsed_time(b)
-        return total / n
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        # a spin kernel ahead of the timed loop keeps the GPU busy while the host
+        # queues the calls, so host-side call overhead cannot open gaps between them
+        torch.cuda._sleep(int(n * 400_000))
+        a.record()
+        for i in range(n):
+            fn(*sets[i % copies])
+        b.record()
+        torch.cuda.synchronize()
+        del sets
+        return a.elapsed_time(b) / n
 
     res = {}
 
     def want(name):
         return only is None or name.startswith(only)
 
-    def hbm(name, fn, nbytes):
+    def nbytes_of(inputs):
+        return sum(t.numel() * t.element_size() for t in inputs if isinstance(t, torch.Tensor))
+
+    def hbm(name, fn, inputs, nbytes):
         if not want(name):
             return
-        ms = timed(fn)
+        ms = timed(fn, inputs, nbytes_of(inputs))
         gbs = nbytes / (ms / 1e3) / 1e9
         res[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "bytes": nbytes,
                      "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4)}
 
-    def tensor(name, fn, flop):
+    def tensor(name, fn, inputs, flop):
         if not want(name):
             return
-        ms = timed(fn)
+        ms = timed(fn, inputs, nbytes_of(inputs))
         tf = flop / (ms / 1e3) / 1e12
         res[name] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1), "flop": flop,
                      "frac_of_bf16": round(tf / peaks["bf16_tflops"], 4)}
@@ -553,14 +566,16 @@ def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
     g = torch.Generator().manual_seed(0)
     gu = torch.randn(16384, 4096, generator=g).to(torch.bfloat16).to(device)
     go = torch.randn(16384, 2048, generator=g).to(torch.bfloat16).to(device)
-    hbm("swiglu_fwd [16384,4096]", lambda: ops.swiglu(gu), 201_326_592)
-    hbm("swiglu_bwd [16384,4096]", lambda: ops.swiglu_backward(gu, go), 335_544_320)
+    hbm("swiglu_fwd [16384,4096]", lambda a: ops.swiglu(a), (gu,), 201_326_592)
+    hbm("swiglu_bwd [16384,4096]", lambda a, b: ops.swiglu_backward(a, b), (gu, go), 335_544_320)
     del gu, go
     x = torch.randn(32768, 768, generator=g).to(torch.bfloat16).to(device)
     r = torch.randn(32768, 768, generator=g).to(torch.bfloat16).to(device)
     gn = torch.randn(32768, 768, generator=g).to(torch.bfloat16).to(device)
-    hbm("residual_rmsnorm_fwd [32768,768]", lambda: ops.residual_rms_norm(r, x, None, 1e-6), 201_326_592)
-    hbm("rmsnorm_bwd [32768,768]", lambda: ops.rms_norm_backward(x, None, r, gn, 1e-6), 201_326_592)
+    hbm("residual_rmsnorm_fwd [32768,768]", lambda a, b: ops.residual_rms_norm(a, b, None, 1e-6), (r, x),
+        201_326_592)
+    hbm("rmsnorm_bwd [32768,768]", lambda a, b, c: ops.rms_norm_backward(a, None, b, c, 1e-6), (x, r, gn),
+        201_326_592)
     del x, r, gn
     B, T, H, D = 8, 2048, 6, 128
     q = torch.randn(B, T, H, D, generator=g).to(torch.bfloat16).to(device)
@@ -570,23 +585,24 @@ def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
     sin = sin.transpose(1, 2).to(device)
     dq = torch.randn_like(q)
     dk = torch.randn_like(k)
-    hbm("qk_norm_rope_fwd [8,2048,6,128]", lambda: ops.qk_norm_rope(q, k, cos, sin, 1e-6), 100_663_296)
-    hbm("qk_norm_rope_bwd [8,2048,6,128]", lambda: ops.qk_norm_rope_backward(q, k, dq, dk, cos, sin, 1e-6),
-        150_994_944)
+    hbm("qk_norm_rope_fwd [8,2048,6,128]", lambda a, b: ops.qk_norm_rope(a, b, cos, sin, 1e-6), (q, k),
+        100_663_296)
+    hbm("qk_norm_rope_bwd [8,2048,6,128]",
+        lambda a, b, c, d: ops.qk_norm_rope_backward(a, b, c, d, cos, sin, 1e-6), (q, k, dq, dk), 150_994_944)
     xq = torch.randn(8, 2048, 768, generator=g).to(torch.bfloat16).to(device)
     wq = (torch.randn(2304, 768, generator=g) * 0.02).to(torch.bfloat16).to(device)
     c1, s1 = oracle.rope_tables(D, T, 10_000.0, 0.25, dtype=torch.bfloat16)
     c1, s1 = c1.to(device), s1.to(device)
-    tensor("qkv_rope_fwd X[16384,768] W[2304,768]", lambda: ops.qkv_rope(xq, wq, c1, s1, 6, 6, 1e-6),
+    tensor("qkv_rope_fwd X[16384,768] W[2304,768]", lambda a: ops.qkv_rope(a, wq, c1, s1, 6, 6, 1e-6), (xq,),
            57_982_058_496)
     if not want("qkv_rope_bwd"):
-        del flush_buf
         return res
     qo, ko, vo, rs = ops.qkv_rope(xq, wq, c1, s1, 6, 6, 1e-6)
     gv = torch.randn_like(vo)
-    tensor("qkv_rope_bwd (dX+dW)", lambda: ops.qkv_rope_backward(xq, wq, qo, ko, rs, c1, s1, dq, dk, gv, 6, 6,
-                                                                 1e-6, True, True), 115_964_116_992)
-    del flush_buf
+    tensor("qkv_rope_bwd (dX+dW)",
+           lambda a, b, c, d, e, f, h: ops.qkv_rope_backward(a, wq, b, c, d, c1, s1, e, f, h, 6, 6, 1e-6, True,
+                                                             True),
+           (xq, qo, ko, rs, dq, dk, gv), 115_964_116_992)
     return res
 
 

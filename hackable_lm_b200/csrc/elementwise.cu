@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(256) swiglu_fwd_vec_kernel(const T* __restrict
         gv.to_float(g);
         uv.to_float(up);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) o[i] = g[i] * sigmoidf_(g[i]) * up[i];
+        for (int i = 0; i < VEC; ++i) o[i] = g[i] * sigmoid_fast(g[i]) * up[i];
         ov.from_float(o);
         st_global_v4(out + (r0 + r) * hidden + static_cast<int64_t>(cv) * VEC, ov.raw);
       }
@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(256) swiglu_bwd_vec_kernel(const T* __restrict
         dv.to_float(d);
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-          const float sg = sigmoidf_(g[i]);
+          const float sg = sigmoid_fast(g[i]);
           const float silu = g[i] * sg;
           const float dsilu = sg * (1.0f + g[i] * (1.0f - sg));
           rg[i] = d[i] * up[i] * dsilu;

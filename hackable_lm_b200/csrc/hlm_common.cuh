@@ -526,6 +526,11 @@ HLM_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 HLM_DEVICE float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// 1 / (1 + 2^(-x log2 e)) with the hardware ex2 and an approximate divide
+// (two MUFU ops, a few ulp of fp32): for kernels whose outputs are bf16.
+HLM_DEVICE float sigmoid_fast(float x) {
+  return __fdividef(1.0f, 1.0f + ex2_ftz(x * -1.4426950408889634f));
+}
 
 HLM_DEVICE float warp_sum(float v) {
 #pragma unroll
