@@ -469,6 +469,15 @@ HLM_DEVICE uint4 ld_global_nc_v4(const void* p) {
                : "l"(p));
   return v;
 }
+// Read-only 16-byte load that allocates in L1 (a second read of the same
+// line from the warp, e.g. a RoPE rotation partner, then hits L1).
+HLM_DEVICE uint4 ld_global_nc_l1_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
 HLM_DEVICE uint4 ld_global_v4(const void* p) {
   uint4 v;
   asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"

@@ -7,10 +7,10 @@
 //   backward: g_n = inverse rotation of g; dx = inv*(g_n - z*mean(g_n*z)).
 //
 // Vector path: one head vector is spread over LPH = D/VEC lanes, each lane
-// holding one 16-byte vector.  The rotation partner of a lane's vector sits
-// `half/VEC` lanes away and is fetched with a shuffle instead of being
-// re-read from memory; the sum of squares and the backward dot product are
-// shuffle-xor reductions inside the LPH-lane group.
+// holding one 16-byte vector; a warp walks the heads of one token at a time.
+// The rotation partner of a lane's vector is re-read (an L1 hit); the sum of
+// squares and the backward dot product are shuffle-xor reductions inside the
+// LPH-lane group.
 #include <type_traits>
 
 #include "rope_vec.cuh"
@@ -48,25 +48,29 @@ HLM_DEVICE void load_cs_vec(const CS* p, float (&out)[VEC]) {
   }
 }
 
-// Item-based vector kernel: one LPH-lane group per head vector (lane = 8
-// consecutive dims), HPW = 32/LPH vectors per warp per step, persistent grid.
-// Every load of a step is issued up front -- the lane's 16 bytes, the 16 bytes
-// of its rotation partner (re-read from memory: an L1 hit, cheaper than
-// shuffles), and its cos/sin vectors -- and the rotation is branch-free:
+// Token-major vector kernel: a warp owns one token at a time and walks its
+// H = Hq + Hk head vectors HPW = 32/LPH at a time (one LPH-lane group per
+// head vector, lane = VEC consecutive dims).  Everything that depends only on
+// the token and the lane -- the batch/position index math and the lane's
+// cos/sin slice with its rotation role folded in -- is computed once per token
+// and reused for every head.  U passes of loads are issued before any of them
+// is used (the lane's 16 bytes, its rotation partner's 16 bytes -- a re-read
+// that hits L1, cheaper than shuffles -- and for the backward the gradient
+// pair), then the rotation is branch-free:
 //   out = inv * (x*c' + sgn*s*px),  c' = cos (rotated dims) or 1 (pass-through),
 //   sgn = -1 for d < rd/2, +1 for rd/2 <= d < rd, 0 beyond.
 // Modes: kRopeFwd (x -> rotated norm), kRopeBwdX (x, g -> dx),
 //        kRopeBwdY (saved output y, saved 1/rms, g -> dx; the normalised
 //        vector z is the inverse rotation of y).
-template <typename T, typename CS, int LPH, int MODE>
+template <typename T, typename CS, int LPH, int MODE, int U>
 __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(const RopeArgs a) {
   constexpr int VEC = 16 / sizeof(T);
   constexpr int HPW = 32 / LPH;
   const int lane = threadIdx.x & 31;
   const int slot = lane / LPH, li = lane % LPH;
-  const uint32_t H = static_cast<uint32_t>(a.Hq + a.Hk);
-  const uint32_t Hq = static_cast<uint32_t>(a.Hq);
-  const uint32_t total = a.tokens * H;
+  const int H = a.Hq + a.Hk;
+  const int Hq = a.Hq;
+  const int D = a.D;
   const int half = a.rd / 2, d0 = li * VEC;
   const int role = d0 < half ? 0 : (d0 < a.rd ? 1 : 2);
   const int pdim = role == 0 ? d0 + half : (role == 1 ? d0 - half : d0);
@@ -75,30 +79,14 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(const RopeArgs a)
   const float cpass = role == 2 ? 1.0f : 0.0f;  // c' = cpass + crot * cos
   const float crot = 1.0f - cpass;
   const bool has_rot = a.rd > 0;
-  const float inv_d = 1.0f / static_cast<float>(a.D);
+  const float inv_d = 1.0f / static_cast<float>(D);
   const T* xq = static_cast<const T*>(a.xq);
   const T* xk = static_cast<const T*>(a.xk);
+  const int passes = (H + HPW - 1) / HPW;
   const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
-  for (uint32_t base = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * HPW; base < total;
-       base += nwarps * HPW) {
-    const uint32_t item = base + slot;
-    const bool ok = item < total;
-    const uint32_t it = ok ? item : 0;
-    const uint32_t tok = it / H, h = it - tok * H;
+  for (uint32_t tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tok < a.tokens;
+       tok += nwarps) {
     const uint32_t b = tok / a.T, t = tok - b * a.T;
-    const bool is_q = h < Hq;
-    const uint32_t hh = is_q ? h : h - Hq;
-    const T* row = is_q ? xq + b * a.qs0 + t * a.qs1 + hh * a.qs2 : xk + b * a.ks0 + t * a.ks1 + hh * a.ks2;
-    const int64_t off = (static_cast<int64_t>(tok) * (is_q ? a.Hq : a.Hk) + hh) * a.D + d0;
-    const uint4 xr = ld_global_nc_v4(row + d0);
-    const uint4 pr = ld_global_nc_v4(row + pdim);
-    uint4 gr = make_uint4(0, 0, 0, 0), pgr = make_uint4(0, 0, 0, 0);
-    if constexpr (MODE != kRopeFwd) {
-      const T* grow = static_cast<const T*>(is_q ? a.gq : a.gk) +
-                      (static_cast<int64_t>(tok) * (is_q ? a.Hq : a.Hk) + hh) * a.D;
-      gr = ld_global_nc_v4(grow + d0);
-      pgr = ld_global_nc_v4(grow + pdim);
-    }
     float c[VEC], s[VEC];
     if (has_rot) {
       load_cs_vec<CS, VEC>(static_cast<const CS*>(a.cosp) + t * a.cs_stride + cb, c);
@@ -107,69 +95,99 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(const RopeArgs a)
 #pragma unroll
       for (int i = 0; i < VEC; ++i) c[i] = s[i] = 0.0f;
     }
-    float rs = 0.0f;
-    if constexpr (MODE == kRopeBwdY) rs = a.rstd[static_cast<int64_t>(tok) * H + h];
-    float x[VEC], px[VEC];
-    {
-      Vec16<T> v, pv;
-      v.raw = xr;
-      pv.raw = pr;
-      v.to_float(x);
-      pv.to_float(px);
-    }
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       c[i] = fmaf(crot, c[i], cpass);
       s[i] *= sgn;
     }
-    float res[VEC];
-    if constexpr (MODE == kRopeFwd) {
-      float ss = 0.0f;
+    const T* qrow = xq + b * a.qs0 + t * a.qs1;
+    const T* krow = xk + b * a.ks0 + t * a.ks1;
+    const int64_t qo = static_cast<int64_t>(tok) * Hq * D;  // outputs / grads: contiguous
+    const int64_t ko = static_cast<int64_t>(tok) * a.Hk * D;
+    for (int p0 = 0; p0 < passes; p0 += U) {
+      uint4 xr[U], pr[U], gr[U], pgr[U];
+      float rs[U];
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) ss = fmaf(x[i], x[i], ss);
-      ss = group_sum<LPH>(ss);
-      const float inv = rsqrtf(ss * inv_d + a.eps);
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) res[i] = inv * fmaf(s[i], px[i], x[i] * c[i]);
-    } else {
-      float g[VEC], pg[VEC];
-      {
-        Vec16<T> v, pv;
-        v.raw = gr;
-        pv.raw = pgr;
-        v.to_float(g);
-        pv.to_float(pg);
+      for (int u = 0; u < U; ++u) {
+        const int h = (p0 + u) * HPW + slot;
+        const int hc = h < H ? h : 0;
+        const bool is_q = hc < Hq;
+        const int hh = is_q ? hc : hc - Hq;
+        const T* row = is_q ? qrow + hh * a.qs2 : krow + hh * a.ks2;
+        xr[u] = ld_global_nc_l1_v4(row + d0);
+        pr[u] = ld_global_nc_l1_v4(row + pdim);
+        if constexpr (MODE != kRopeFwd) {
+          const T* grow = static_cast<const T*>(is_q ? a.gq : a.gk) + (is_q ? qo : ko) +
+                          static_cast<int64_t>(hh) * D;
+          gr[u] = ld_global_nc_l1_v4(grow + d0);
+          pgr[u] = ld_global_nc_l1_v4(grow + pdim);
+        }
+        if constexpr (MODE == kRopeBwdY) rs[u] = a.rstd[static_cast<int64_t>(tok) * H + hc];
       }
-      float inv, z[VEC];
-      if constexpr (MODE == kRopeBwdX) {
-        float ss = 0.0f;
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) ss = fmaf(x[i], x[i], ss);
-        ss = group_sum<LPH>(ss);
-        inv = rsqrtf(ss * inv_d + a.eps);
+      for (int u = 0; u < U; ++u) {
+        const int h = (p0 + u) * HPW + slot;
+        float x[VEC], px[VEC], res[VEC];
+        {
+          Vec16<T> v, pv;
+          v.raw = xr[u];
+          pv.raw = pr[u];
+          v.to_float(x);
+          pv.to_float(px);
+        }
+        if constexpr (MODE == kRopeFwd) {
+          float ss = 0.0f;
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) z[i] = x[i] * inv;
-      } else {
-        inv = rs;
-        // inverse rotation of the saved output y gives the normalised vector
+          for (int i = 0; i < VEC; ++i) ss = fmaf(x[i], x[i], ss);
+          ss = group_sum<LPH>(ss);
+          const float inv = rsqrtf(ss * inv_d + a.eps);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) z[i] = fmaf(-s[i], px[i], x[i] * c[i]);
+          for (int i = 0; i < VEC; ++i) res[i] = inv * fmaf(s[i], px[i], x[i] * c[i]);
+        } else {
+          float g[VEC], pg[VEC];
+          {
+            Vec16<T> v, pv;
+            v.raw = gr[u];
+            pv.raw = pgr[u];
+            v.to_float(g);
+            pv.to_float(pg);
+          }
+          float inv, z[VEC];
+          if constexpr (MODE == kRopeBwdX) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) ss = fmaf(x[i], x[i], ss);
+            ss = group_sum<LPH>(ss);
+            inv = rsqrtf(ss * inv_d + a.eps);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) z[i] = x[i] * inv;
+          } else {
+            inv = rs[u];
+            // inverse rotation of the saved output y gives the normalised vector
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) z[i] = fmaf(-s[i], px[i], x[i] * c[i]);
+          }
+          // inverse rotation of the output gradient
+          float dot = 0.0f, gn[VEC];
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) {
+            gn[i] = fmaf(-s[i], pg[i], g[i] * c[i]);
+            dot = fmaf(gn[i], z[i], dot);
+          }
+          dot = group_sum<LPH>(dot) * inv_d;
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) res[i] = inv * fmaf(-z[i], dot, gn[i]);
+        }
+        if (h < H) {
+          const bool is_q = h < Hq;
+          const int hh = is_q ? h : h - Hq;
+          Vec16<T> o;
+          o.from_float(res);
+          st_global_v4(static_cast<T*>(is_q ? a.oq : a.ok) + (is_q ? qo : ko) +
+                           static_cast<int64_t>(hh) * D + d0,
+                       o.raw);
+        }
       }
-      // inverse rotation of the output gradient
-      float dot = 0.0f, gn[VEC];
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) {
-        gn[i] = fmaf(-s[i], pg[i], g[i] * c[i]);
-        dot = fmaf(gn[i], z[i], dot);
-      }
-      dot = group_sum<LPH>(dot) * inv_d;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) res[i] = inv * fmaf(-z[i], dot, gn[i]);
-    }
-    if (ok) {
-      Vec16<T> o;
-      o.from_float(res);
-      st_global_v4(static_cast<T*>(is_q ? a.oq : a.ok) + off, o.raw);
     }
   }
 }
@@ -254,17 +272,42 @@ __global__ void __launch_bounds__(256) qk_norm_rope_scalar_kernel(
   }
 }
 
+// Loads in flight per lane: U passes of 2 (forward) or 4 (backward) vectors
+// (measured: the backward's extra registers cost more than deeper batching gains).
+template <int MODE>
+constexpr int rope_passes_per_batch() {
+  return MODE == kRopeFwd ? 3 : 1;
+}
+
+template <typename T, typename CS, int LPH, int MODE>
+static void launch_rope_vec_lph(const RopeArgs& a, int64_t warps_needed, cudaStream_t s) {
+  constexpr int U = rope_passes_per_batch<MODE>();
+  auto kern = qk_norm_rope_vec_kernel<T, CS, LPH, MODE, U>;
+  // persistent grid: as many 256-thread blocks as are resident at once
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 256, 0) != cudaSuccess || n < 1) n = 1;
+    per_sm = n;
+  }
+  int64_t blocks = (warps_needed + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * per_sm;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  kern<<<static_cast<int>(blocks), 256, 0, s>>>(a);
+}
+
 template <typename T, typename CS, int MODE>
-static void launch_rope_vec(int lph, const RopeArgs& a, int blocks, cudaStream_t s) {
+static void launch_rope_vec(int lph, const RopeArgs& a, int64_t warps_needed, cudaStream_t s) {
   switch (lph) {
     case 8:
-      qk_norm_rope_vec_kernel<T, CS, 8, MODE><<<blocks, 256, 0, s>>>(a);
+      launch_rope_vec_lph<T, CS, 8, MODE>(a, warps_needed, s);
       break;
     case 16:
-      qk_norm_rope_vec_kernel<T, CS, 16, MODE><<<blocks, 256, 0, s>>>(a);
+      launch_rope_vec_lph<T, CS, 16, MODE>(a, warps_needed, s);
       break;
     default:
-      qk_norm_rope_vec_kernel<T, CS, 32, MODE><<<blocks, 256, 0, s>>>(a);
+      launch_rope_vec_lph<T, CS, 32, MODE>(a, warps_needed, s);
       break;
   }
 }
@@ -292,16 +335,12 @@ int rope_vec_launch(const RopeArgs& a, int cs_dtype, int kernel_id, cudaStream_t
     vec = vec && host_aligned16(a.cosp) && host_aligned16(a.sinp) &&
           (a.cs_stride * (cs_f32 ? 4 : 2)) % 16 == 0;
   if (!vec) return HLM_ERR_UNSUPPORTED;
-  const int64_t warps = (static_cast<int64_t>(a.tokens) * (a.Hq + a.Hk) * lph + 31) / 32;
-  int64_t blocks = (warps + 7) / 8;
-  const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
-  if (blocks > cap) blocks = cap;
-  if (blocks < 1) blocks = 1;
+  const int64_t warps = static_cast<int64_t>(a.tokens);  // one warp per token at a time
   LaunchScope scope(kernel_id, s);
   if (cs_f32)
-    launch_rope_vec<T, float, MODE>(lph, a, static_cast<int>(blocks), s);
+    launch_rope_vec<T, float, MODE>(lph, a, warps, s);
   else
-    launch_rope_vec<T, T, MODE>(lph, a, static_cast<int>(blocks), s);
+    launch_rope_vec<T, T, MODE>(lph, a, warps, s);
   return launch_status();
 }
 
