@@ -73,10 +73,10 @@ template <int BN, bool A_MN, bool B_MN>
 static int plain_gemm_pair(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K,
                            int64_t lda, int64_t ldb, int64_t ldd, int d_dtype, int accumulate,
                            cudaStream_t s) {
-  constexpr int STAGES = BN == 256 ? 6 : 8;
+  constexpr int STAGES = BN == 384 ? 5 : (BN == 256 ? 6 : 8);
   CUtensorMap ma, mb;
   bool ok = A_MN ? encode_bf16_map(&ma, A, M, K, lda, 64) : encode_bf16_map(&ma, A, K, M, lda, kBM);
-  ok = ok && (B_MN ? encode_bf16_map(&mb, B, N, K, ldb, 64) : encode_bf16_map(&mb, B, K, N, ldb, BN / 2));
+  ok = ok && (B_MN ? encode_bf16_map(&mb, B, N, K, ldb, 64) : encode_bf16_map(&mb, B, K, N, ldb, 64));
   if (!ok) return HLM_ERR_DRIVER;
   GemmParams p;
   gemm_tiling_pair(p, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), BN, 1);
@@ -115,6 +115,14 @@ extern "C" int hlm_gemm_bf16(const void* A, const void* B, void* D, int64_t M, i
 #define HLM_PAIR(BNV, AM, BM)                                                                  \
   return plain_gemm_pair<BNV, AM, BM>(A, B, D, M, N, K, lda, ldb, ldd, d_dtype, accumulate, s)
   if (M >= 2 * kBM) {
+    if (N % 384 == 0 && K >= 8192) {
+      // long K: 256 x 384 pair tiles (one accumulator, whose epilogue is then a
+      // small share of the tile), less B traffic per FLOP
+      if (!am && !bm) HLM_PAIR(384, false, false);
+      if (!am && bm) HLM_PAIR(384, false, true);
+      if (am && !bm) HLM_PAIR(384, true, false);
+      HLM_PAIR(384, true, true);
+    }
     if (wide) {
       if (!am && !bm) HLM_PAIR(256, false, false);
       if (!am && bm) HLM_PAIR(256, false, true);

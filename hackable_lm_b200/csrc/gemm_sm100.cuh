@@ -312,8 +312,13 @@ struct PairSmem {
   static constexpr int kNumBars = 2 * STAGES + 4;
   static constexpr int kTmemSlotOffset = kBarOffset + kNumBars * 8;
   static constexpr int kEpiOffset = ((kTmemSlotOffset + 16 + 1023) / 1024) * 1024;
-  static constexpr int kTmemCols = 2 * BN;
-  static_assert(BN == 128 || BN == 256, "pair tile N");
+  // BN <= 256: two accumulators (epilogue overlaps the next tile); BN = 384:
+  // one accumulator and two MMAs per K step (N = 256 + 128), for long-K GEMMs
+  static constexpr int kAccs = BN <= 256 ? 2 : 1;
+  static constexpr int kN0 = BN <= 256 ? BN : 256;  // first MMA of a K step
+  static constexpr int kN1 = BN - kN0;              // second MMA (BN = 384)
+  static constexpr int kTmemCols = kAccs * BN <= 256 ? 256 : 512;
+  static_assert(BN == 128 || BN == 256 || BN == 384, "pair tile N");
 };
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS = 4>
@@ -383,7 +388,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads<EPI_WAR
         int m_pair, n_tile, split;
         decode_work(w, p, m_pair, n_tile, split);
         const int m0 = (2 * m_pair + static_cast<int>(rank)) * kBM;
-        const int n0 = n_tile * BN + static_cast<int>(rank) * (BN / 2);
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -414,11 +418,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads<EPI_WAR
               tma_load_2d_pair(sa + i * 8192u, mp, mc, k0, full);
             }
           }
-          if constexpr (!B_MN) {
-            tma_load_2d_pair(sb, &tmB, k0, n0, full);
-          } else {
+          // This CTA's half of B: columns (N0/2) r.. of the first MMA and, for
+          // BN = 384, N0 + (N1/2) r.. of the second, as 64-column boxes
+          // (K-major: 64-row boxes) stacked 8 KB apart.
+          const int nb0 = n_tile * BN + static_cast<int>(rank) * (L::kN0 / 2);
 #pragma unroll
-            for (int i = 0; i < BN / 128; ++i) tma_load_2d_pair(sb + i * 8192u, &tmB, n0 + 64 * i, k0, full);
+          for (int i = 0; i < L::kN0 / 128; ++i) {
+            if constexpr (!B_MN)
+              tma_load_2d_pair(sb + i * 8192u, &tmB, k0, nb0 + 64 * i, full);
+            else
+              tma_load_2d_pair(sb + i * 8192u, &tmB, nb0 + 64 * i, k0, full);
+          }
+          if constexpr (L::kN1 > 0) {
+            const int nb1 = n_tile * BN + L::kN0 + static_cast<int>(rank) * (L::kN1 / 2);
+#pragma unroll
+            for (int i = 0; i < L::kN1 / 128; ++i) {
+              const uint32_t dst = sb + static_cast<uint32_t>(L::kN0 / 128 + i) * 8192u;
+              if constexpr (!B_MN)
+                tma_load_2d_pair(dst, &tmB, k0, nb1 + 64 * i, full);
+              else
+                tma_load_2d_pair(dst, &tmB, nb1 + 64 * i, k0, full);
+            }
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -434,7 +454,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads<EPI_WAR
   } else if (warp == 1) {
     // ------------------------------------------------------------ pair MMA issuer (even CTA)
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16_f32(2 * kBM, BN, A_MN, B_MN);
+      constexpr uint32_t idesc0 = make_idesc_bf16_f32(2 * kBM, L::kN0, A_MN, B_MN);
+      constexpr uint32_t idesc1 = make_idesc_bf16_f32(2 * kBM, L::kN1 > 0 ? L::kN1 : 16, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -444,8 +465,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads<EPI_WAR
         decode_work(w, p, m_pair, n_tile, split);
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
-        const int acc = it & 1;
-        const uint32_t acc_par = static_cast<uint32_t>((it >> 1) & 1);
+        const int acc = L::kAccs == 2 ? (it & 1) : 0;
+        const uint32_t acc_par = static_cast<uint32_t>(L::kAccs == 2 ? ((it >> 1) & 1) : (it & 1));
         if (!mbar_wait_cluster(TEMPTY_BAR(acc), acc_par ^ 1u, err, kDevErrTimeoutTmemEmpty)) {
           ok = false;
           break;
@@ -466,7 +487,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads<EPI_WAR
                                         : make_sw128_desc(sa + kk * 32u, 16u, 1024u);
             const uint64_t bdesc = B_MN ? make_sw128_desc(sb + kk * 2048u, 8192u, 1024u)
                                         : make_sw128_desc(sb + kk * 32u, 16u, 1024u);
-            tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            const uint32_t accum = (kb > kb0 || kk > 0) ? 1u : 0u;
+            tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc0, accum);
+            if constexpr (L::kN1 > 0) {
+              // second MMA: columns [256, BN); its B half starts after the first's
+              constexpr uint32_t off = static_cast<uint32_t>(L::kN0 / 2) * 128u;
+              const uint64_t bdesc1 = B_MN ? make_sw128_desc(sb + off + kk * 2048u, 8192u, 1024u)
+                                           : make_sw128_desc(sb + off + kk * 32u, 16u, 1024u);
+              tc_mma_f16_pair(d_tmem + static_cast<uint32_t>(L::kN0), adesc, bdesc1, idesc1, accum);
+            }
           }
           tc_commit_pair(EMPTY_BAR(stage));
           tc_commit_pair(mapa_shared(EMPTY_BAR(stage), 1));
@@ -489,8 +518,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads<EPI_WAR
     for (int w = w_first; w < total; w += w_step, ++it) {
       int m_pair, n_tile, split;
       decode_work(w, p, m_pair, n_tile, split);
-      const int acc = it & 1;
-      const uint32_t acc_par = static_cast<uint32_t>((it >> 1) & 1);
+      const int acc = L::kAccs == 2 ? (it & 1) : 0;
+      const uint32_t acc_par = static_cast<uint32_t>(L::kAccs == 2 ? ((it >> 1) & 1) : (it & 1));
       if (!warp_wait(TFULL_BAR(acc), acc_par, err, kDevErrTimeoutTmemFull, lane)) break;
       tc_fence_after();
       const uint32_t taddr =

@@ -23,8 +23,9 @@
 namespace hlm {
 
 constexpr int kLmBN = 256;
-constexpr int kLmStages = 4;      // single-CTA GEMMs (grad_weight)
-constexpr int kLmPairStages = 6;  // CTA-pair GEMMs (logits, grad_hidden)
+constexpr int kLmPairStages = 6;  // CTA-pair logits GEMM (256 x 256 tiles)
+constexpr int kLmBwdBN = 384;     // grad_hidden / grad_weight: 256 x 384 pair tiles (K = V or tokens)
+constexpr int kLmBwdStages = 5;
 constexpr int kLmEpiWarps = 8;
 constexpr int kLmEpiParts = kLmEpiWarps / 4;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -419,7 +420,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
 
   // Tensor maps that do not depend on the chunk.
   CUtensorMap map_w_k, map_w_n;
-  if (!encode_bf16_map(&map_w_k, W, C, V, C, kLmBN / 2)) return HLM_ERR_DRIVER;  // B half, logits GEMM
+  if (!encode_bf16_map(&map_w_k, W, C, V, C, 64)) return HLM_ERR_DRIVER;  // B boxes, logits GEMM
   if (!encode_bf16_map(&map_w_n, W, C, V, C, 64)) return HLM_ERR_DRIVER;     // B of dX GEMM
 
   for (int ci = 0; ci < pl.n_chunks; ++ci) {
@@ -478,7 +479,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       CUtensorMap map_p;
       if (!encode_bf16_map(&map_p, logits, V, rows, V, kBM)) return HLM_ERR_DRIVER;
       GemmParams p;
-      gemm_tiling_pair(p, rows, static_cast<int>(C), static_cast<int>(V), kLmBN, 1);
+      gemm_tiling_pair(p, rows, static_cast<int>(C), static_cast<int>(V), kLmBwdBN, 1);
       p.err = err;
       EpiStore::Params ep;
       ep.d = static_cast<__nv_bfloat16*>(grad_hidden) + r0 * C;
@@ -488,7 +489,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       ep.accumulate = 0;
       ep.vec_ok = 1;
       ep.alpha = &stats->inv_n;
-      const int rc = launch_gemm_pair<kLmBN, kLmPairStages, false, true, EpiStore>(
+      const int rc = launch_gemm_pair<kLmBwdBN, kLmBwdStages, false, true, EpiStore>(
           map_p, map_p, map_p, map_w_n, p, ep, s, HLM_KERNEL_LM_DX);
       if (rc != HLM_OK) return rc;
     }
@@ -498,7 +499,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       if (!encode_bf16_map(&map_pt, logits, V, rows, V, 64)) return HLM_ERR_DRIVER;
       if (!encode_bf16_map(&map_hn, Hc, C, rows, C, 64)) return HLM_ERR_DRIVER;
       GemmParams p;
-      gemm_tiling(p, static_cast<int>(V), static_cast<int>(C), rows, kLmBN, 1);
+      gemm_tiling_pair(p, static_cast<int>(V), static_cast<int>(C), rows, kLmBwdBN, 1);
       p.err = err;
       EpiStore::Params ep;
       ep.ldd = C;
@@ -514,7 +515,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
         ep.dtype = HLM_F32;
         ep.accumulate = ci > 0 ? 1 : 0;
       }
-      const int rc = launch_gemm_sm100<kLmBN, kLmStages, true, true, EpiStore>(
+      const int rc = launch_gemm_pair<kLmBwdBN, kLmBwdStages, true, true, EpiStore>(
           map_pt, map_pt, map_pt, map_hn, p, ep, s, HLM_KERNEL_LM_DW);
       if (rc != HLM_OK) return rc;
     }

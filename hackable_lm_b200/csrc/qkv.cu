@@ -273,7 +273,7 @@ extern "C" int hlm_qkv_rope_fwd(const void* x, const void* w_qkv, const void* co
   const int64_t nqkv = (Hq + 2 * Hk) * kQkvD;
   CUtensorMap mx, mw;
   if (!encode_bf16_map(&mx, x, C, M, C, kBM)) return HLM_ERR_DRIVER;
-  if (!encode_bf16_map(&mw, w_qkv, C, nqkv, C, kQkvBN / 2)) return HLM_ERR_DRIVER;  // pair: half of B
+  if (!encode_bf16_map(&mw, w_qkv, C, nqkv, C, 64)) return HLM_ERR_DRIVER;  // pair: 64-row boxes of B
   if (rotary_dim > 0 && (!host_aligned16(cos) || !host_aligned16(sin) ||
                          (cs_stride_t * (cs_dtype == HLM_F32 ? 4 : 2)) % 16 != 0))
     return HLM_ERR_UNSUPPORTED;

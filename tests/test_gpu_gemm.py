@@ -21,7 +21,7 @@ def _operands(M, N, K, a_mn, b_mn, device, seed=0):
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 768), (200, 136, 136), (1000, 768, 2304),
-                                   (64, 64, 64)])
+                                   (64, 64, 64), (704, 1152, 8192)])
 def test_gemm_layouts(M, N, K, a_mn, b_mn, cuda_device):
     from hackable_lm_b200 import _lib, ops
 
