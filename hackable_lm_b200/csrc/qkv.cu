@@ -26,7 +26,6 @@ constexpr int kQkvBN = 2 * kQkvD;  // two heads per output tile
 constexpr int kQkvStages = 6;     // CTA-pair stages: 16 KB of A + 16 KB (half) of B
 constexpr int kQkvEpiWarps = 4;  // 8 (one warp per lane quadrant and head) spills registers
 constexpr int kDwBN = 256;
-constexpr int kDwStages = 4;
 
 // Forward epilogue: the tile holds 128 token rows x 2 heads (BN = 256).  Each
 // thread owns one row.  Per head: 4 x tcgen05.ld (128 fp32), then for q/k
@@ -195,13 +194,13 @@ __global__ void __launch_bounds__(256) splitk_reduce_bf16_kernel(const float* __
 }
 
 // Split-K count for the dW GEMM (few output tiles, long K): the smallest split
-// whose work units fill the SM waves to >= 90% (each split adds an fp32 slab
-// to write and reduce), else the best fill found up to 16 splits; every split
-// keeps at least 8 K blocks.
+// whose work units (256 x kDwBN pair tiles) fill the CTA-pair waves to >= 90%
+// (each split adds an fp32 slab to write and reduce), else the best fill found
+// up to 16 splits; every split keeps at least 8 K blocks.
 static inline int qkv_dw_splits(int64_t tokens, int64_t nqkv, int64_t C) {
-  const int64_t tiles = ((nqkv + kBM - 1) / kBM) * ((C + kDwBN - 1) / kDwBN);
+  const int64_t tiles = ((nqkv + 2 * kBM - 1) / (2 * kBM)) * ((C + kDwBN - 1) / kDwBN);
   const int64_t kblocks = (tokens + kBK - 1) / kBK;
-  const int64_t sms = num_sms_of_current_device();
+  const int64_t sms = num_sms_of_current_device() / 2;  // CTA pairs
   int best = 1;
   double best_fill = 0.0;
   for (int64_t s = 1; s <= 16 && s <= kblocks / 8; ++s) {
@@ -425,8 +424,8 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
         !encode_bf16_map(&mb, x, C, M, C, 64))
       return HLM_ERR_DRIVER;
     GemmParams p;
-    gemm_tiling(p, static_cast<int>(nqkv), static_cast<int>(C), static_cast<int>(M), kDwBN,
-                pl.splits);
+    gemm_tiling_pair(p, static_cast<int>(nqkv), static_cast<int>(C), static_cast<int>(M), kDwBN,
+                     pl.splits);
     if (p.splits != pl.splits) return HLM_ERR_LAUNCH;
     p.a_seg1 = seg1;
     p.a_seg2 = seg2;
@@ -439,8 +438,8 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
     ep.accumulate = 0;
     ep.vec_ok = 1;
     ep.alpha = nullptr;
-    const int rc = launch_gemm_sm100<kDwBN, kDwStages, true, true, EpiStore>(a0, a1, a2, mb, p, ep,
-                                                                             s, HLM_KERNEL_QKV_DW);
+    const int rc = launch_gemm_pair<kDwBN, kQkvStages, true, true, EpiStore>(a0, a1, a2, mb, p, ep, s,
+                                                                            HLM_KERNEL_QKV_DW);
     if (rc != HLM_OK) return rc;
     const int64_t n = nqkv * C;
     int64_t blocks = (n / 4 + 255) / 256;
