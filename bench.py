@@ -244,7 +244,7 @@ def bench_lm_head(args, d: Dist, device) -> dict:
     # ---- device-timed value, with the library timing its own kernels
     clocks = ClockSampler(device.index)
     kernels_to_time = ("lm_logits", "lm_dlogits", "lm_dx", "lm_dw")
-    timers = {k: _lib.KernelTimer(k, args.steps) for k in kernels_to_time}
+    timers = {k: _lib.KernelTimer(k, 4 * args.steps) for k in kernels_to_time}
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -261,31 +261,34 @@ def bench_lm_head(args, d: Dist, device) -> dict:
     value = M * d.world / (ms_per_step / 1e3)
 
     kt = {k: timers[k].times_ms() for k in kernels_to_time}
+    # per step (= per call): a kernel may launch more than once (the dlogits pass
+    # and grad_hidden GEMM run in two row halves), and the second dlogits half
+    # overlaps the first grad_hidden GEMM on a side stream, so shares can sum
+    # above 1
     flops = {"lm_logits": 2.0 * M * C * V, "lm_dx": 2.0 * M * C * V, "lm_dw": 2.0 * M * C * V}
     bytes_ = {"lm_dlogits": 4.0 * M * V}  # bf16 logits read + dlogits written in place
+    per_step = {k: sum(ts) / args.steps for k, ts in kt.items() if ts}
     breakdown = {}
-    for k, ts in kt.items():
-        if not ts:
-            continue
-        avg = sum(ts) / len(ts)
-        entry = {"ms": round(avg, 4), "share_of_step": round(avg / ms_per_step, 4)}
+    for k, ms in per_step.items():
+        entry = {"ms": round(ms, 4), "launches_per_step": len(kt[k]) // args.steps,
+                 "share_of_step": round(ms / ms_per_step, 4)}
         if k in flops:
-            entry["tflops"] = round(flops[k] / (avg / 1e3) / 1e12, 1)
+            entry["tflops"] = round(flops[k] / (ms / 1e3) / 1e12, 1)
         if k in bytes_:
-            entry["gbs"] = round(bytes_[k] / (avg / 1e3) / 1e9, 1)
+            entry["gbs"] = round(bytes_[k] / (ms / 1e3) / 1e9, 1)
         breakdown[k] = entry
-    dominant = max(kt, key=lambda k: (sum(kt[k]) / max(1, len(kt[k]))) if kt[k] else 0.0)
-    dom_avg = sum(kt[dominant]) / len(kt[dominant])
+    dominant = max(per_step, key=per_step.get)
+    dom_ms = per_step[dominant]
     tr = traffic_table().get(("lm_head", dominant))
     if dominant in flops:
-        achieved = flops[dominant] / (dom_avg / 1e3) / 1e12
+        achieved = flops[dominant] / (dom_ms / 1e3) / 1e12
         peak = peaks["bf16_tflops"]
         roofline = {"kernel": dominant, "bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": tr,
                     "peak_source": f"{peak_src} bf16_tflops (burst: kernel timed inside a ~5 ms step)",
-                    "algorithmic_per_launch": f"2*M*C*V = {flops[dominant]:.4e} FLOP"}
+                    "algorithmic_per_step": f"2*M*C*V = {flops[dominant]:.4e} FLOP"}
     else:
-        achieved = bytes_[dominant] / (dom_avg / 1e3) / 1e9
+        achieved = bytes_[dominant] / (dom_ms / 1e3) / 1e9
         peak = peaks["hbm_gbs"]
         roofline = {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": tr,
@@ -335,7 +338,7 @@ def bench_lm_head(args, d: Dist, device) -> dict:
 # ---------------------------------------------------------------------------
 D12_FLOPS_PER_TOKEN = 887_095_296  # config.estimate_flops_per_token, full causal attention
 
-# per-layer kernels launch once per layer and micro-step; LM-head kernels once per micro-step
+# operator calls per micro-step: per-layer kernels once per layer, LM-head kernels once
 D12_KERNELS = {"lm_logits": 1, "lm_dlogits": 1, "lm_dx": 1, "lm_dw": 1, "qkv_fwd": 12, "qkv_bwd_norm": 12,
                "qkv_dx": 12, "qkv_dw": 12, "swiglu_fwd": 12, "swiglu_bwd": 12, "rmsnorm_fwd": 25,
                "rmsnorm_bwd": 25}
@@ -367,7 +370,8 @@ def bench_d12(args, d: Dist, device) -> dict:
         step()
     torch.cuda.synchronize()
     # per-kernel timing of the library's own launches during the first timed step
-    timers = {k: _lib.KernelTimer(k, n * s.accum) for k, n in D12_KERNELS.items()}
+    # capacity: up to two launches per operator call (LM dlogits / grad_hidden run in row halves)
+    timers = {k: _lib.KernelTimer(k, 2 * n * s.accum) for k, n in D12_KERNELS.items()}
     clocks = ClockSampler(device.index)
     clocks.start()
     d.barrier()
@@ -401,9 +405,9 @@ def bench_d12(args, d: Dist, device) -> dict:
 
     M = s.micro_batch * s.seq_len
     C, V, Hd = s.config.n_embd, s.config.vocab_size, 3 * s.config.n_head * s.config.head_dim
+    # algorithmic FLOPs / HBM bytes per operator call (bf16 = 2 bytes)
     flops = {"lm_logits": 2.0 * M * C * V, "lm_dx": 2.0 * M * C * V, "lm_dw": 2.0 * M * C * V,
              "qkv_fwd": 2.0 * M * C * Hd, "qkv_dx": 2.0 * M * C * Hd, "qkv_dw": 2.0 * M * C * Hd}
-    # algorithmic HBM bytes per launch of the memory-bound kernels (bf16 = 2 bytes)
     Hm, Dq = s.config.mlp_hidden, s.config.n_head * s.config.head_dim
     n_fwd = D12_KERNELS["rmsnorm_fwd"]
     bytes_ = {
@@ -422,8 +426,10 @@ def bench_d12(args, d: Dist, device) -> dict:
         if not ts:
             continue
         totals[k] = sum(ts)
-        avg = sum(ts) / len(ts)
-        e = {"launches_in_step": t.launches, "avg_ms": round(avg, 4), "total_ms": round(sum(ts), 3),
+        # per operator call (D12_KERNELS calls per micro-step; a call may be two launches)
+        avg = sum(ts) / (D12_KERNELS[k] * s.accum)
+        e = {"launches_in_step": t.launches, "calls_in_step": D12_KERNELS[k] * s.accum,
+             "avg_ms_per_call": round(avg, 4), "total_ms": round(sum(ts), 3),
              "share_of_step": round(sum(ts) / step0_ms, 4)}
         if k in flops:
             e["tflops"] = round(flops[k] / (avg / 1e3) / 1e12, 1)
@@ -431,7 +437,7 @@ def bench_d12(args, d: Dist, device) -> dict:
             e["gbs"] = round(bytes_[k] / (avg / 1e3) / 1e9, 1)
         breakdown[k] = e
     dominant = max((k for k in totals if k in flops or k in bytes_), key=totals.get)
-    dom_avg = breakdown[dominant]["avg_ms"]
+    dom_avg = breakdown[dominant]["avg_ms_per_call"]
     roofline = {"kernel": dominant, "traffic": traffic_table().get(("d12", dominant))}
     if dominant in flops:
         achieved = flops[dominant] / (dom_avg / 1e3) / 1e12

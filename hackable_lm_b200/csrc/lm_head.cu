@@ -18,6 +18,10 @@
 //   5. dW GEMM       grad_weight (+)= (P^T @ H_chunk) / n_valid (both MN-major)
 // A pre-pass counts the valid targets of the whole batch so the 1/n_valid
 // scale is known to every chunk on the device, with no host round trip.
+// Within a chunk the dlogits pass of the second row half runs on a side stream
+// alongside the first half's grad_hidden GEMM (see the chunk loop).
+#include <mutex>
+
 #include "gemm_sm100.cuh"
 
 namespace hlm {
@@ -204,15 +208,15 @@ HLM_DEVICE float2 lse_merge(float2 a, float2 b) {
 constexpr int kFinRows = 32;    // rows per block (one per lane)
 constexpr int kFinGroups = 8;   // warps per block, each merging every 8th part
 
-// Per row: lse from the per-(tile, part) pairs, the row loss, per-block loss
-// sums, and the row's softmax data for the backward: {bits of lse*log2(e),
-// target} for a valid row, {+inf, -1} for an ignored or padding row (its
-// gradient row is then exactly zero).  Warp g of a block merges parts
+// Per row: lse from the per-(tile, part) pairs (row stride `stride`), the row
+// loss, per-block loss sums, and the row's softmax data for the backward:
+// {bits of lse*log2(e), target} for a valid row, {+inf, -1} for an ignored row
+// (its gradient row is then exactly zero).  Warp g of a block merges parts
 // g, g + 8, ... of the block's 32 rows (lane = row: 256-byte coalesced loads);
 // the eight partial merges are combined in a fixed order.
 __global__ void __launch_bounds__(kFinRows * kFinGroups) lm_finalize_kernel(
-    const float2* __restrict__ partial, int n_parts, const float* __restrict__ tgt_logit,
-    const int64_t* __restrict__ targets, int rows, int info_rows, int64_t V, int64_t ignore_index,
+    const float2* __restrict__ partial, int n_parts, int stride, const float* __restrict__ tgt_logit,
+    const int64_t* __restrict__ targets, int rows, int64_t V, int64_t ignore_index,
     int2* __restrict__ info_out, float* __restrict__ block_sums) {
   __shared__ float2 s_part[kFinGroups][kFinRows];
   const int lane = threadIdx.x & 31;
@@ -222,13 +226,13 @@ __global__ void __launch_bounds__(kFinRows * kFinGroups) lm_finalize_kernel(
   if (row < rows) {
     int t = g;
     for (; t + 3 * kFinGroups < n_parts; t += 4 * kFinGroups) {
-      const float2 p0 = partial[static_cast<int64_t>(t) * rows + row];
-      const float2 p1 = partial[static_cast<int64_t>(t + kFinGroups) * rows + row];
-      const float2 p2 = partial[static_cast<int64_t>(t + 2 * kFinGroups) * rows + row];
-      const float2 p3 = partial[static_cast<int64_t>(t + 3 * kFinGroups) * rows + row];
+      const float2 p0 = partial[static_cast<int64_t>(t) * stride + row];
+      const float2 p1 = partial[static_cast<int64_t>(t + kFinGroups) * stride + row];
+      const float2 p2 = partial[static_cast<int64_t>(t + 2 * kFinGroups) * stride + row];
+      const float2 p3 = partial[static_cast<int64_t>(t + 3 * kFinGroups) * stride + row];
       acc = lse_merge(acc, lse_merge(lse_merge(p0, p1), lse_merge(p2, p3)));
     }
-    for (; t < n_parts; t += kFinGroups) acc = lse_merge(acc, partial[static_cast<int64_t>(t) * rows + row]);
+    for (; t < n_parts; t += kFinGroups) acc = lse_merge(acc, partial[static_cast<int64_t>(t) * stride + row]);
   }
   s_part[g][lane] = acc;
   __syncthreads();
@@ -244,8 +248,6 @@ __global__ void __launch_bounds__(kFinRows * kFinGroups) lm_finalize_kernel(
       if (valid) loss = lse - tgt_logit[row];
       info_out[row] = valid ? make_int2(__float_as_int(lse * kLog2e), static_cast<int>(t))
                             : make_int2(__float_as_int(INFINITY), -1);
-    } else if (row < info_rows) {
-      info_out[row] = make_int2(__float_as_int(INFINITY), -1);
     }
     loss = warp_sum(loss);
     if (lane == 0) block_sums[blockIdx.x] = loss;
@@ -272,8 +274,6 @@ __global__ void __launch_bounds__(256) lm_loss_reduce_kernel(const float* __rest
   }
 }
 
-// Rows of the per-row softmax data are padded to a multiple of 128.
-static inline int64_t lm_info_rows(int64_t rows) { return (rows + kBM - 1) / kBM * kBM; }
 
 // In place: S -> P = softmax - onehot = 2^(S log2 e - lse log2 e) - [col == target],
 // rounded to bf16 (the reference's in-place gradient overwrite,
@@ -320,6 +320,33 @@ __global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restric
     dst[i] = __float2bfloat16_rn(src[i]);
 }
 
+// One side stream (non-blocking) and its events per device, created on first
+// use and kept for the process; the mutex keeps one call's record/wait
+// sequence from interleaving with another thread's.
+struct SideStream {
+  std::mutex mu;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev_lse[2] = {nullptr, nullptr};  // [1]: second half may start (caller stream)
+  cudaEvent_t ev_p[2] = {nullptr, nullptr};    // [1]: second half's dlogits done (side stream)
+};
+
+static SideStream* side_stream_of_current_device() {
+  static std::mutex init_mu;
+  static SideStream side[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(init_mu);
+  SideStream& ss = side[dev];
+  if (ss.stream == nullptr) {
+    if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    for (int i = 0; i < 2; ++i)
+      if (cudaEventCreateWithFlags(&ss.ev_lse[i], cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventCreateWithFlags(&ss.ev_p[i], cudaEventDisableTiming) != cudaSuccess)
+        return nullptr;
+  }
+  return &ss;
+}
+
 // ---------------------------------------------------------------------------
 // Workspace plan
 // ---------------------------------------------------------------------------
@@ -357,9 +384,9 @@ static LmPlan lm_plan(int64_t n_tokens, int64_t C, int64_t V, int64_t chunk_toke
   pl.off_tgt = off;
   off = align256(off + static_cast<size_t>(chunk) * 4);
   pl.off_info = off;
-  off = align256(off + static_cast<size_t>(lm_info_rows(chunk)) * 8);
+  off = align256(off + static_cast<size_t>(chunk) * 8);
   pl.off_bsum = off;
-  off = align256(off + static_cast<size_t>((lm_info_rows(chunk) + kFinRows - 1) / kFinRows) * 4);
+  off = align256(off + static_cast<size_t>((chunk + kFinRows - 1) / kFinRows) * 4);
   pl.off_stats = off;
   off = align256(off + sizeof(LmStats));
   pl.off_dw = off;
@@ -448,14 +475,13 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
           map_h, map_h, map_h, map_w_k, p, ep, s, HLM_KERNEL_LM_LOGITS);
       if (rc != HLM_OK) return rc;
     }
-    // 2. lse + loss
+    // 2. lse, per-row softmax data and loss
     {
-      const int info_rows = static_cast<int>(lm_info_rows(rows));
-      const int nb = (info_rows + kFinRows - 1) / kFinRows;
+      const int nb = (rows + kFinRows - 1) / kFinRows;
       {
         LaunchScope scope(0, s);
-        lm_finalize_kernel<<<nb, kFinRows * kFinGroups, 0, s>>>(partial, pl.n_parts, tgt_logit, tc, rows, info_rows,
-                                              V, ignore_index, info, bsum);
+        lm_finalize_kernel<<<nb, kFinRows * kFinGroups, 0, s>>>(partial, pl.n_parts, rows, tgt_logit, tc,
+                                                                 rows, V, ignore_index, info, bsum);
       }
       {
         LaunchScope scope(0, s);
@@ -463,35 +489,80 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
       }
       if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
     }
-    if (!want_dx && !want_dw) continue;
-    // 3. dlogits in place
-    {
-      const int64_t vecs = static_cast<int64_t>(rows) * (V / 8);
+    const bool grads = want_dx || want_dw;
+    if (!grads) continue;
+    // 3. dlogits in place.  With at least 512 rows and grad_hidden wanted, the
+    // rows split in two halves (a multiple of 256, the pair tile) and the second
+    // half's pass runs on a side stream x while the first half's grad_hidden
+    // GEMM runs on the caller's stream s:
+    //   s: dlogits(A) | dX(A)      | dX(B) dW
+    //   x:            | dlogits(B) |
+    // The GEMM keeps one CTA per SM busy on the tensor pipe and leaves issue
+    // slots, registers and memory bandwidth that the streaming pass fills.
+    // (Overlapping a pass with the logits GEMM instead slows both: that GEMM's
+    // epilogue needs the issue slots and the bandwidth itself.)
+    const int split = (want_dx && rows >= 512) ? ((rows / 2 + 255) / 256) * 256 : rows;
+    const int n_halves = split < rows ? 2 : 1;
+    const int lo_of[2] = {0, split}, hi_of[2] = {split, rows};
+    SideStream* side = nullptr;
+    std::unique_lock<std::mutex> side_lock;
+    if (n_halves == 2) {
+      side = side_stream_of_current_device();
+      if (side == nullptr) return HLM_ERR_LAUNCH;
+      side_lock = std::unique_lock<std::mutex>(side->mu);
+    }
+    auto dlogits = [&](int r_lo, int r_hi, cudaStream_t st) -> int {
+      const int n = r_hi - r_lo;
+      if (n <= 0) return HLM_OK;
+      const int64_t vecs = static_cast<int64_t>(n) * (V / 8);
       int64_t blocks = (vecs + 255) / 256;
       const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
       if (blocks > cap) blocks = cap;
-      LaunchScope scope(HLM_KERNEL_LM_DLOGITS, s);
-      lm_dlogits_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(logits, info, rows, V);
-      if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
+      LaunchScope scope(HLM_KERNEL_LM_DLOGITS, st);
+      lm_dlogits_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(logits + static_cast<int64_t>(r_lo) * V,
+                                                                 info + r_lo, n, V);
+      return launch_status();
+    };
+    {
+      int rc = dlogits(lo_of[0], hi_of[0], s);
+      if (rc != HLM_OK) return rc;
+      if (n_halves == 2) {
+        if (cudaEventRecord(side->ev_lse[1], s) != cudaSuccess ||
+            cudaStreamWaitEvent(side->stream, side->ev_lse[1], 0) != cudaSuccess)
+          return HLM_ERR_LAUNCH;
+        rc = dlogits(lo_of[1], hi_of[1], side->stream);
+        if (rc != HLM_OK) return rc;
+        if (cudaEventRecord(side->ev_p[1], side->stream) != cudaSuccess) return HLM_ERR_LAUNCH;
+      }
     }
-    // 4. grad_hidden[chunk] = P @ W
-    if (want_dx) {
+    // 4. grad_hidden[chunk] = P @ W, per half once its dlogits pass is done
+    auto grad_hidden_gemm = [&](int r_lo, int r_hi) -> int {
+      const int n = r_hi - r_lo;
+      if (n <= 0) return HLM_OK;
       CUtensorMap map_p;
-      if (!encode_bf16_map(&map_p, logits, V, rows, V, kBM)) return HLM_ERR_DRIVER;
+      if (!encode_bf16_map(&map_p, logits + static_cast<int64_t>(r_lo) * V, V, n, V, kBM))
+        return HLM_ERR_DRIVER;
       GemmParams p;
-      gemm_tiling_pair(p, rows, static_cast<int>(C), static_cast<int>(V), kLmBwdBN, 1);
+      gemm_tiling_pair(p, n, static_cast<int>(C), static_cast<int>(V), kLmBwdBN, 1);
       p.err = err;
       EpiStore::Params ep;
-      ep.d = static_cast<__nv_bfloat16*>(grad_hidden) + r0 * C;
+      ep.d = static_cast<__nv_bfloat16*>(grad_hidden) + (r0 + r_lo) * C;
       ep.ldd = C;
       ep.split_stride = 0;
       ep.dtype = HLM_BF16;
       ep.accumulate = 0;
       ep.vec_ok = 1;
       ep.alpha = &stats->inv_n;
-      const int rc = launch_gemm_pair<kLmBwdBN, kLmBwdStages, false, true, EpiStore>(
+      return launch_gemm_pair<kLmBwdBN, kLmBwdStages, false, true, EpiStore>(
           map_p, map_p, map_p, map_w_n, p, ep, s, HLM_KERNEL_LM_DX);
-      if (rc != HLM_OK) return rc;
+    };
+    for (int h = 0; h < n_halves; ++h) {
+      // the second half's rows are ready once the side stream's pass is done
+      if (h == 1 && cudaStreamWaitEvent(s, side->ev_p[1], 0) != cudaSuccess) return HLM_ERR_LAUNCH;
+      if (want_dx) {
+        const int rc = grad_hidden_gemm(lo_of[h], hi_of[h]);
+        if (rc != HLM_OK) return rc;
+      }
     }
     // 5. grad_weight (+)= P^T @ H_chunk
     if (want_dw) {
