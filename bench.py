@@ -339,7 +339,7 @@ def bench_lm_head(args, d: Dist, device) -> dict:
 D12_FLOPS_PER_TOKEN = 887_095_296  # config.estimate_flops_per_token, full causal attention
 
 # operator calls per micro-step: per-layer kernels once per layer, LM-head kernels once
-D12_KERNELS = {"lm_logits": 1, "lm_dlogits": 1, "lm_dx": 1, "lm_dw": 1, "qkv_fwd": 12, "qkv_bwd_norm": 12,
+D12_KERNELS = {"lm_logits": 1, "lm_dlogits": 1, "lm_dx": 1, "lm_dw": 1, "gate_up": 12, "qkv_fwd": 12, "qkv_bwd_norm": 12,
                "qkv_dx": 12, "qkv_dw": 12, "swiglu_fwd": 12, "swiglu_bwd": 12, "rmsnorm_fwd": 25,
                "rmsnorm_bwd": 25}
 
@@ -407,7 +407,8 @@ def bench_d12(args, d: Dist, device) -> dict:
     C, V, Hd = s.config.n_embd, s.config.vocab_size, 3 * s.config.n_head * s.config.head_dim
     # algorithmic FLOPs / HBM bytes per operator call (bf16 = 2 bytes)
     flops = {"lm_logits": 2.0 * M * C * V, "lm_dx": 2.0 * M * C * V, "lm_dw": 2.0 * M * C * V,
-             "qkv_fwd": 2.0 * M * C * Hd, "qkv_dx": 2.0 * M * C * Hd, "qkv_dw": 2.0 * M * C * Hd}
+             "qkv_fwd": 2.0 * M * C * Hd, "qkv_dx": 2.0 * M * C * Hd, "qkv_dw": 2.0 * M * C * Hd,
+             "gate_up": 2.0 * M * C * 2 * s.config.mlp_hidden}
     Hm, Dq = s.config.mlp_hidden, s.config.n_head * s.config.head_dim
     n_fwd = D12_KERNELS["rmsnorm_fwd"]
     bytes_ = {
@@ -601,6 +602,11 @@ def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
     c1, s1 = c1.to(device), s1.to(device)
     tensor("qkv_rope_fwd X[16384,768] W[2304,768]", lambda a: ops.qkv_rope(a, wq, c1, s1, 6, 6, 1e-6), (xq,),
            57_982_058_496)
+    xg = torch.randn(32768, 768, generator=g).to(torch.bfloat16).to(device)
+    wg = (torch.randn(4096, 768, generator=g) * 0.02).to(torch.bfloat16).to(device)
+    tensor("gate_up_swiglu X[32768,768] W[4096,768]", lambda a: ops.gate_up_swiglu(a, wg), (xg,),
+           2 * 32768 * 768 * 4096)
+    del xg, wg
     if not want("qkv_rope_bwd"):
         return res
     qo, ko, vo, rs = ops.qkv_rope(xq, wq, c1, s1, 6, 6, 1e-6)

@@ -55,6 +55,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
         [_P, _P, _P, _P, _P, _P, _P, c_size_t, _I64, _I64, _I64, _I64, _I64, _P], c_int),
     "hlm_lm_head_ce_workspace_bytes": ([_I64, _I64, _I64, _I64], c_size_t),
     "hlm_scale_by_device_scalar": ([_P, _P, _I64, c_int, _P], c_int),
+    "hlm_gate_up_swiglu_fwd": ([_P, _P, _P, _P, _I64, _I64, _I64, _P], c_int),
     "hlm_gemm_bf16": (
         [_P, _P, _P, _I64, _I64, _I64, c_int, c_int, _I64, _I64, _I64, c_int, c_int, _P], c_int),
 }
@@ -114,7 +115,7 @@ def clear_device_error(stream: int = 0) -> None:
 KERNEL_IDS = {
     "lm_logits": 1, "lm_dlogits": 2, "lm_dx": 3, "lm_dw": 4, "qkv_fwd": 5, "qkv_bwd_norm": 6,
     "qkv_dx": 7, "qkv_dw": 8, "swiglu_fwd": 9, "swiglu_bwd": 10, "rmsnorm_fwd": 11,
-    "rmsnorm_bwd": 12, "qk_rope_fwd": 13, "qk_rope_bwd": 14, "gemm": 15,
+    "rmsnorm_bwd": 12, "qk_rope_fwd": 13, "qk_rope_bwd": 14, "gemm": 15, "gate_up": 16,
 }
 
 

@@ -47,6 +47,11 @@ struct GemmParams {
   // [0, a_seg1) -> map 0, [a_seg1, a_seg2) -> map 1, [a_seg2, ...) -> map 2.
   // a_seg1 == 0 means a single tensor.  Boundaries are multiples of 64.
   int a_seg1, a_seg2;
+  // Pair kernel, BN <= 256 only: when > 0, CTA r of a pair loads its half of B
+  // from rows n_tile * BN/2 + r * b_pair_stride (two separate row ranges of B,
+  // e.g. the gate and up halves of a packed gate/up weight) instead of the
+  // contiguous n_tile * BN + r * BN/2.
+  int b_pair_stride;
   int* err;
 };
 
@@ -421,7 +426,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads<EPI_WAR
           // This CTA's half of B: columns (N0/2) r.. of the first MMA and, for
           // BN = 384, N0 + (N1/2) r.. of the second, as 64-column boxes
           // (K-major: 64-row boxes) stacked 8 KB apart.
-          const int nb0 = n_tile * BN + static_cast<int>(rank) * (L::kN0 / 2);
+          const int nb0 = (L::kN1 == 0 && p.b_pair_stride > 0)
+                              ? n_tile * (BN / 2) + static_cast<int>(rank) * p.b_pair_stride
+                              : n_tile * BN + static_cast<int>(rank) * (L::kN0 / 2);
 #pragma unroll
           for (int i = 0; i < L::kN0 / 128; ++i) {
             if constexpr (!B_MN)
@@ -621,6 +628,7 @@ inline void gemm_tiling(GemmParams& p, int M, int N, int K, int BN, int splits) 
   p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
   p.a_seg1 = 0;
   p.a_seg2 = 0;
+  p.b_pair_stride = 0;
 }
 
 // Same for the pair kernel: m_tiles counts 256-row pair tiles.

@@ -1,0 +1,127 @@
+// gate_up projection with the SwiGLU activation in the GEMM epilogue: the
+// reference's GateUpProjection.fwd_triton (model.py:291-292), i.e. a cuBLAS
+// GEMM x @ W_gate_up^T followed by swiglu_triton (kernels.py:743-753), as one
+// CTA-pair tcgen05 GEMM.
+//
+//   gate_up[M, 2H] = x[M, C] @ W[2H, C]^T   (bf16, kept for the backward)
+//   h[M, H]        = silu(gate) * up        (fp32 math on the bf16-rounded
+//                                            gate/up, like the reference)
+//
+// A pair tile covers 256 rows and 128 hidden units: CTA 0 loads the 128 gate
+// rows of W and CTA 1 the matching 128 up rows (GemmParams::b_pair_stride = H),
+// so every accumulator row holds [gate(128) | up(128)] and the epilogue can
+// form h without another pass over gate_up.
+#include "gemm_sm100.cuh"
+
+namespace hlm {
+
+constexpr int kMlpStages = 4;
+constexpr int kMlpEpiWarps = 8;  // two warps per TMEM lane quadrant, one 64-unit group each
+
+// Epilogue: per warp (32 rows) and 64-unit group: gate and up (2 x 64 fp32
+// columns from TMEM) rounded to bf16 and staged as two 32x64 boxes for the
+// gate_up output, h = silu(gate) * up staged as a third box; one lane issues
+// the three TMA stores.  Eight epilogue warps: two per lane quadrant.
+struct EpiSwiGLU {
+  struct Params {
+    alignas(64) CUtensorMap map_gu;  // gate_up [M][2H] bf16, box {64, 32}
+    alignas(64) CUtensorMap map_h;   // h [M][H] bf16, box {64, 32}
+    int H;
+  };
+  static constexpr int kBoxBytes = 32 * 128;
+  template <int EPI_WARPS>
+  static constexpr int smem_bytes() {
+    return EPI_WARPS * 3 * kBoxBytes;
+  }
+
+  // Warp `part` of kParts (1 or 2) sharing a lane quadrant takes every
+  // kParts-th 64-unit group; each group is processed in two 32-column halves
+  // to keep the register footprint small.
+  template <int BN, int kParts>
+  static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t* smem, uint32_t taddr,
+                             int m_tile, int n_tile, int, int quad, int part, int lane) {
+    static_assert(BN == 256 && (kParts == 1 || kParts == 2), "128 gate + 128 up columns");
+    const uint32_t buf = smem_u32(smem) + static_cast<uint32_t>((part * 4 + quad) * 3 * kBoxBytes);
+    const int row0 = m_tile * kBM + quad * 32;
+#pragma unroll 1
+    for (int g = part; g < 2; g += kParts) {
+      // the stores that last used the staging boxes must have read them
+      if (lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
+#pragma unroll 1
+      for (int hs = 0; hs < 2; ++hs) {
+        uint32_t pg[16], pu[16], ph[16];
+        {
+          uint32_t a[32], b[32];
+          tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(g * 64 + hs * 32), a);
+          tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(128 + g * 64 + hs * 32), b);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            pg[j] = pack_bf16x2(__uint_as_float(a[2 * j]), __uint_as_float(a[2 * j + 1]));
+            pu[j] = pack_bf16x2(__uint_as_float(b[2 * j]), __uint_as_float(b[2 * j + 1]));
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float g0 = bf16_lo(pg[j]), g1 = bf16_hi(pg[j]);
+          const float u0 = bf16_lo(pu[j]), u1 = bf16_hi(pu[j]);
+          ph[j] = pack_bf16x2(g0 * sigmoid_fast(g0) * u0, g1 * sigmoid_fast(g1) * u1);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cc = hs * 4 + c;  // 16-byte chunk of the 128-byte row
+          const uint32_t off = static_cast<uint32_t>(lane * 128 + ((cc ^ (lane & 7)) << 4));
+          st_shared_v4(buf + off, make_uint4(pg[4 * c], pg[4 * c + 1], pg[4 * c + 2], pg[4 * c + 3]));
+          st_shared_v4(buf + kBoxBytes + off,
+                       make_uint4(pu[4 * c], pu[4 * c + 1], pu[4 * c + 2], pu[4 * c + 3]));
+          st_shared_v4(buf + 2 * kBoxBytes + off,
+                       make_uint4(ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]));
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && row0 < p.M) {
+        const int col = n_tile * 128 + g * 64;  // hidden unit of the group's first column
+        tma_store_2d(&ep.map_gu, col, row0, buf);
+        tma_store_2d(&ep.map_gu, ep.H + col, row0, buf + kBoxBytes);
+        tma_store_2d(&ep.map_h, col, row0, buf + 2 * kBoxBytes);
+        bulk_commit_group();
+      }
+    }
+  }
+};
+
+}  // namespace hlm
+
+using namespace hlm;
+
+extern "C" int hlm_gate_up_swiglu_fwd(const void* x, const void* w_gate_up, void* gate_up_out,
+                                      void* h_out, int64_t M, int64_t C, int64_t H, void* stream) {
+  if (M < 0 || C <= 0 || H <= 0) return HLM_ERR_INVALID_ARG;
+  if (M == 0) return HLM_OK;
+  if (x == nullptr || w_gate_up == nullptr || gate_up_out == nullptr || h_out == nullptr)
+    return HLM_ERR_INVALID_ARG;
+  if (C % 64 != 0 || H % 128 != 0 || M > (1ll << 31) - 512 || 2 * H > (1ll << 30))
+    return HLM_ERR_UNSUPPORTED;
+  if (!host_aligned16(x) || !host_aligned16(w_gate_up) || !host_aligned16(gate_up_out) ||
+      !host_aligned16(h_out))
+    return HLM_ERR_UNSUPPORTED;
+  CUtensorMap mx, mw;
+  if (!encode_bf16_map(&mx, x, C, M, C, kBM)) return HLM_ERR_DRIVER;
+  if (!encode_bf16_map(&mw, w_gate_up, C, 2 * H, C, 64)) return HLM_ERR_DRIVER;
+  EpiSwiGLU::Params ep;
+  if (!encode_bf16_map(&ep.map_gu, gate_up_out, 2 * H, M, 2 * H, 32) ||
+      !encode_bf16_map(&ep.map_h, h_out, H, M, H, 32))
+    return HLM_ERR_DRIVER;
+  ep.H = static_cast<int>(H);
+  GemmParams p;
+  // N counted in hidden units: n_tiles = H / 128 tiles of [128 gate | 128 up]
+  gemm_tiling_pair(p, static_cast<int>(M), static_cast<int>(2 * H), static_cast<int>(C), 256, 1);
+  p.n_tiles = static_cast<int>(H / 128);
+  p.b_pair_stride = static_cast<int>(H);
+  p.err = device_error_ptr();
+  if (p.err == nullptr) return HLM_ERR_LAUNCH;
+  return launch_gemm_pair<256, kMlpStages, false, false, EpiSwiGLU, kMlpEpiWarps>(
+      mx, mx, mx, mw, p, ep, static_cast<cudaStream_t>(stream), HLM_KERNEL_GATE_UP);
+}

@@ -25,7 +25,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from . import kernels
+from . import kernels, ops
 from .config import ModelConfig, layer_attention_window
 
 
@@ -200,6 +200,10 @@ class GateUpProjection(AcceleratedModule):
         return F.silu(gate) * up
 
     def fwd_b200(self, x: torch.Tensor) -> torch.Tensor:
+        w = self.gate_up_proj.weight
+        if ops.gate_up_swiglu_supported(x, w):
+            # the GEMM with the SwiGLU activation in its epilogue
+            return ops.gate_up_swiglu(x, w)[0]
         return kernels.swiglu_triton(self.gate_up_proj(x))
 
 

@@ -110,6 +110,66 @@ def _swiglu_bwd(ctx, grad_out):
 swiglu.register_autograd(_swiglu_bwd, setup_context=_swiglu_setup)
 
 
+def gate_up_swiglu_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Shapes and dtypes the fused gate_up + SwiGLU kernel takes."""
+    return (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+            and x.shape[-1] % 64 == 0 and weight.shape[0] % 256 == 0 and weight.shape[1] == x.shape[-1])
+
+
+# gate_up projection + SwiGLU (reference: model.py:285-292 -> kernels.py:743-753; its backward
+# kernels.py:690-700 followed by the two weight-side GEMMs of the linear layer)
+@torch.library.custom_op("hackable_lm_b200::gate_up_swiglu", mutates_args=())
+def gate_up_swiglu(x: torch.Tensor, weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """h = silu(gate) * up with [gate | up] = x @ weight^T, in one tcgen05 GEMM.
+    Returns (h [..., H], gate_up [..., 2H]); gate_up is kept for the backward."""
+    dev = _require_cuda(x, weight)
+    x = x.contiguous()
+    weight = weight.contiguous()
+    C = x.shape[-1]
+    H = weight.shape[0] // 2
+    rows = x.numel() // max(1, C)
+    gate_up = torch.empty((*x.shape[:-1], 2 * H), dtype=x.dtype, device=dev)
+    h = torch.empty((*x.shape[:-1], H), dtype=x.dtype, device=dev)
+    check(_lib_().hlm_gate_up_swiglu_fwd(_ptr(x), _ptr(weight), _ptr(gate_up), _ptr(h), rows, C, H,
+                                          _stream(dev)), "hlm_gate_up_swiglu_fwd")
+    return h, gate_up
+
+
+@gate_up_swiglu.register_fake
+def _gate_up_swiglu_fake(x, weight):
+    H = weight.shape[0] // 2
+    return x.new_empty((*x.shape[:-1], H)), x.new_empty((*x.shape[:-1], 2 * H))
+
+
+def _gate_up_setup(ctx, inputs, output):
+    x, weight = inputs
+    _, gate_up = output
+    ctx.save_for_backward(x, weight, gate_up)
+    # gate_up is a saved activation, not a differentiable output: no zero-filled
+    # [M, 2H] gradient is materialised for it in the backward
+    ctx.mark_non_differentiable(gate_up)
+    ctx.set_materialize_grads(False)
+
+
+def _gate_up_bwd(ctx, grad_h, grad_gate_up):
+    x, weight, gate_up = ctx.saved_tensors
+    dgu = None
+    if grad_h is not None:
+        dgu = swiglu_backward(gate_up, grad_h)
+    if grad_gate_up is not None:
+        dgu = grad_gate_up if dgu is None else dgu + grad_gate_up
+    if dgu is None:
+        return None, None
+    C = x.shape[-1]
+    d2 = dgu.reshape(-1, dgu.shape[-1])
+    grad_x = (d2 @ weight).reshape(x.shape) if ctx.needs_input_grad[0] else None
+    grad_w = (d2.t() @ x.reshape(-1, C)) if ctx.needs_input_grad[1] else None
+    return grad_x, grad_w
+
+
+gate_up_swiglu.register_autograd(_gate_up_bwd, setup_context=_gate_up_setup)
+
+
 # ---------------------------------------------------------------------------
 # RMSNorm / residual-add + RMSNorm  (reference: model.py:14-16, 73-75; kernels.py:245-247)
 # ---------------------------------------------------------------------------

@@ -76,7 +76,8 @@ uint64_t hlm_launch_count(void);
 #define HLM_KERNEL_QK_ROPE_FWD 13
 #define HLM_KERNEL_QK_ROPE_BWD 14
 #define HLM_KERNEL_GEMM 15
-#define HLM_KERNEL_MAX 16
+#define HLM_KERNEL_GATE_UP 16      /* gate_up GEMM + SwiGLU epilogue */
+#define HLM_KERNEL_MAX 17
 
 /* Start timing every launch of kernel `kernel_id`: launch i records
  * start_events[i] immediately before and stop_events[i] immediately after
@@ -245,6 +246,20 @@ size_t hlm_lm_head_ce_workspace_bytes(int64_t n_tokens, int64_t C, int64_t V,
 /* data[i] *= *scale for i < n (scale is a device fp32 scalar).  Backward of
  * the fused LM head, replacing _scale_saved_grad (kernels.py:872-875). */
 int hlm_scale_by_device_scalar(void* data, const float* scale, int64_t n, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * MLP: gate_up projection with the SwiGLU activation in its epilogue
+ * ------------------------------------------------------------------------ */
+
+/* gate_up projection + SwiGLU in one CTA-pair tcgen05 GEMM.  Replaces
+ * GateUpProjection.fwd_triton (model.py:291-292): gate_up = x @ W^T followed by
+ * swiglu_triton (kernels.py:743-753).  x [M, C] bf16 row-major, w_gate_up
+ * [2H, C] bf16 (gate rows first, then up rows, the reference's packed
+ * layout); writes gate_up [M, 2H] bf16 (kept for the backward) and
+ * h = silu(gate) * up [M, H] bf16 (fp32 math on the bf16-rounded gate/up).
+ * Requires C % 64 == 0, H % 128 == 0, 16-byte aligned pointers. */
+int hlm_gate_up_swiglu_fwd(const void* x, const void* w_gate_up, void* gate_up_out, void* h_out,
+                           int64_t M, int64_t C, int64_t H, void* stream);
 
 /* ------------------------------------------------------------------------
  * Plain tcgen05 GEMM (building block; also used by tests)
