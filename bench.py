@@ -38,8 +38,9 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
-# stdout carries exactly one JSON line: NCCL's own log lines (e.g. its version
-# banner) go to stderr unless the caller chose a log file
+# stdout carries exactly one JSON line: NCCL's own log lines go to stderr
+# unless the caller chose a log file (NCCL ignores the file at the VERSION log
+# level, hence also the descriptor switch in main())
 os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 import torch  # noqa: E402
@@ -657,7 +658,24 @@ def run_reference(args, d: Dist) -> dict | None:
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def _claim_stdout():
+    """Keep the process's stdout for the result line alone: file descriptor 1
+    is pointed at stderr for the rest of the run (so a library that prints to
+    stdout, such as NCCL's version banner, lands on stderr) and the returned
+    stream writes to the original stdout."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
 def main() -> None:
+    result_out = _claim_stdout()
+
+    def emit(obj) -> None:
+        result_out.write(json.dumps(obj) + "\n")
+        result_out.flush()
+
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -684,7 +702,7 @@ def main() -> None:
         d.init(backend="gloo")
         out = run_reference(args, d)
         if out is not None:
-            print(json.dumps(out), flush=True)
+            emit(out)
         d.close()
         return
 
@@ -694,7 +712,7 @@ def main() -> None:
     if args.op is not None:
         if d.rank == 0:
             res = bench_ops(device, iters=args.op_iters, only=None if args.op == "all" else args.op)
-            print(json.dumps({"ops": res}), flush=True)
+            emit({"ops": res})
         d.close()
         return
     if args.workload == "lm_head":
@@ -710,7 +728,7 @@ def main() -> None:
             out["ops"] = bench_ops(device)
         if not args.no_cpu_baseline and d.world == 1:
             out["cpu_baseline"] = cpu_baseline_lm() if args.workload == "lm_head" else cpu_baseline_d12()
-        print(json.dumps(out), flush=True)
+        emit(out)
     d.close()
 
 
