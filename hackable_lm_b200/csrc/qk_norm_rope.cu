@@ -6,11 +6,11 @@
 //             z with cos/sin[t, d mod half]; pass-through dims are z.
 //   backward: g_n = inverse rotation of g; dx = inv*(g_n - z*mean(g_n*z)).
 //
-// Vector path: one head vector is spread over LPH = D/VEC lanes, each lane
-// holding one 16-byte vector; a warp walks the heads of one token at a time.
-// The rotation partner of a lane's vector is re-read (an L1 hit); the sum of
-// squares and the backward dot product are shuffle-xor reductions inside the
-// LPH-lane group.
+// Vector path: one head vector is spread over LPH lanes, each lane holding two
+// 16-byte chunks chosen so that it owns whole rotation pairs (no partner
+// loads); a warp walks the heads of one token at a time.  The sum of squares
+// and the backward dot product are shuffle-xor reductions inside the LPH-lane
+// group.
 #include <type_traits>
 
 #include "rope_vec.cuh"
@@ -48,64 +48,124 @@ HLM_DEVICE void load_cs_vec(const CS* p, float (&out)[VEC]) {
   }
 }
 
-// Token-major vector kernel: a warp owns one token at a time and walks its
-// H = Hq + Hk head vectors HPW = 32/LPH at a time (one LPH-lane group per
-// head vector, lane = VEC consecutive dims).  Everything that depends only on
-// the token and the lane -- the batch/position index math and the lane's
-// cos/sin slice with its rotation role folded in -- is computed once per token
-// and reused for every head.  U passes of loads are issued before any of them
-// is used (the lane's 16 bytes, its rotation partner's 16 bytes -- a re-read
-// that hits L1, cheaper than shuffles -- and for the backward the gradient
-// pair), then the rotation is branch-free:
-//   out = inv * (x*c' + sgn*s*px),  c' = cos (rotated dims) or 1 (pass-through),
-//   sgn = -1 for d < rd/2, +1 for rd/2 <= d < rd, 0 beyond.
+// A 16-byte chunk of T as float pairs (element 2j in .x, 2j+1 in .y), for the
+// packed fp32x2 arithmetic of sm_100.
+template <typename T>
+struct Chunk {
+  static constexpr int NP = 8 / sizeof(T);  // float pairs per chunk
+  static HLM_DEVICE void unpack(const uint4& r, float2 (&f)[NP]) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+    if constexpr (std::is_same<T, float>::value) {
+      f[0] = make_float2(__uint_as_float(w[0]), __uint_as_float(w[1]));
+      f[1] = make_float2(__uint_as_float(w[2]), __uint_as_float(w[3]));
+    } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        f[j] = make_float2(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xffff0000u));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) f[j] = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+    }
+  }
+  static HLM_DEVICE uint4 pack(const float2 (&f)[NP]) {
+    uint32_t w[4];
+    if constexpr (std::is_same<T, float>::value) {
+      w[0] = __float_as_uint(f[0].x);
+      w[1] = __float_as_uint(f[0].y);
+      w[2] = __float_as_uint(f[1].x);
+      w[3] = __float_as_uint(f[1].y);
+    } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) w[j] = pack_bf16x2(f[j].x, f[j].y);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __half2 h = __floats2half2_rn(f[j].x, f[j].y);
+        w[j] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+HLM_DEVICE float rsqrt_ftz(float x) {
+  float y;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Token-major vector kernel.  A warp owns one token at a time and walks its
+// H = Hq + Hk head vectors HPW = 32/LPH at a time, LPH = D / (2*CH) lanes per
+// head vector, CH = 16/sizeof(T) elements per 16-byte chunk.  Every lane holds
+// two chunks, laid out so that each lane owns whole rotation pairs:
+//   rotated lane i < rd/(2*CH): dims [i*CH, +CH) and their partners [rd/2 + i*CH, +CH)
+//   pass-through lane j:        dims [rd + j*CH, +CH) and [rd + (D-rd)/2 + j*CH, +CH)
+// so the rotation needs no partner load and one branch-free formula serves
+// every lane:
+//   out0 = inv * (x0*c + s0*x1),  out1 = inv * (x1*c + s1*x0)
+// with (c, s0, s1) = (cos, -sin, +sin) on rotated lanes and (1, 0, 0) on
+// pass-through lanes (the inverse rotation of the backward flips the signs).
+// Each load instruction of the warp covers whole 32-byte sectors.  The token's
+// cos/sin slice and the (batch, position) index are computed once per token;
+// U passes of loads are issued before any of them is used; the fp32 arithmetic
+// runs on float pairs (fma.rn.f32x2 / mul.rn.f32x2, same rounding as scalar).
 // Modes: kRopeFwd (x -> rotated norm), kRopeBwdX (x, g -> dx),
 //        kRopeBwdY (saved output y, saved 1/rms, g -> dx; the normalised
 //        vector z is the inverse rotation of y).
 template <typename T, typename CS, int LPH, int MODE, int U>
-__global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(const RopeArgs a) {
-  constexpr int VEC = 16 / sizeof(T);
+HLM_DEVICE void qk_norm_rope_vec_body(const RopeArgs& a) {
+  using C = Chunk<T>;
+  constexpr int CH = 16 / sizeof(T);
+  constexpr int NP = C::NP;
   constexpr int HPW = 32 / LPH;
   const int lane = threadIdx.x & 31;
   const int slot = lane / LPH, li = lane % LPH;
   const int H = a.Hq + a.Hk;
   const int Hq = a.Hq;
   const int D = a.D;
-  const int half = a.rd / 2, d0 = li * VEC;
-  const int role = d0 < half ? 0 : (d0 < a.rd ? 1 : 2);
-  const int pdim = role == 0 ? d0 + half : (role == 1 ? d0 - half : d0);
-  const int cb = role == 2 ? 0 : (role == 0 ? d0 : d0 - half);
-  const float sgn = role == 0 ? -1.0f : (role == 1 ? 1.0f : 0.0f);
-  const float cpass = role == 2 ? 1.0f : 0.0f;  // c' = cpass + crot * cos
-  const float crot = 1.0f - cpass;
-  const bool has_rot = a.rd > 0;
+  const int half = a.rd >> 1;
+  const int nrot = half / CH;
+  const bool rot = li < nrot;
+  const int off0 = rot ? li * CH : a.rd + (li - nrot) * CH;
+  const int off1 = off0 + (rot ? half : (D - a.rd) >> 1);
+  // sign of sin in the chunk-0 term: -1 forward, +1 for the inverse rotation
+  const float sg = rot ? (MODE == kRopeFwd ? -1.0f : 1.0f) : 0.0f;
+  const float crot = rot ? 1.0f : 0.0f;
   const float inv_d = 1.0f / static_cast<float>(D);
   const T* xq = static_cast<const T*>(a.xq);
   const T* xk = static_cast<const T*>(a.xk);
   const int passes = (H + HPW - 1) / HPW;
   const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
-  for (uint32_t tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tok < a.tokens;
-       tok += nwarps) {
-    const uint32_t b = tok / a.T, t = tok - b * a.T;
-    float c[VEC], s[VEC];
-    if (has_rot) {
-      load_cs_vec<CS, VEC>(static_cast<const CS*>(a.cosp) + t * a.cs_stride + cb, c);
-      load_cs_vec<CS, VEC>(static_cast<const CS*>(a.sinp) + t * a.cs_stride + cb, s);
-    } else {
+  uint32_t tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (tok >= a.tokens) return;
+  // (batch, position) of the token, advanced by nwarps tokens per iteration
+  uint32_t b = tok / a.T, t = tok - b * a.T;
+  const uint32_t db = nwarps / a.T, dt = nwarps - db * a.T;
+  for (; tok < a.tokens; tok += nwarps) {
+    float2 c[NP], s0[NP], s1[NP];
+    {
+      float cf[CH], sf[CH];
+      if (a.rd > 0) {
+        const int64_t ci = static_cast<int64_t>(t) * a.cs_stride + (rot ? li * CH : 0);
+        load_cs_vec<CS, CH>(static_cast<const CS*>(a.cosp) + ci, cf);
+        load_cs_vec<CS, CH>(static_cast<const CS*>(a.sinp) + ci, sf);
+      } else {
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) c[i] = s[i] = 0.0f;
-    }
+        for (int i = 0; i < CH; ++i) cf[i] = sf[i] = 0.0f;
+      }
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      c[i] = fmaf(crot, c[i], cpass);
-      s[i] *= sgn;
+      for (int j = 0; j < NP; ++j) {
+        c[j] = make_float2(fmaf(crot, cf[2 * j], 1.0f - crot), fmaf(crot, cf[2 * j + 1], 1.0f - crot));
+        s0[j] = make_float2(sg * sf[2 * j], sg * sf[2 * j + 1]);
+        s1[j] = make_float2(-s0[j].x, -s0[j].y);
+      }
     }
     const T* qrow = xq + b * a.qs0 + t * a.qs1;
     const T* krow = xk + b * a.ks0 + t * a.ks1;
     const int64_t qo = static_cast<int64_t>(tok) * Hq * D;  // outputs / grads: contiguous
     const int64_t ko = static_cast<int64_t>(tok) * a.Hk * D;
     for (int p0 = 0; p0 < passes; p0 += U) {
-      uint4 xr[U], pr[U], gr[U], pgr[U];
+      uint4 r0[U], r1[U], gr0[U], gr1[U];
       float rs[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -114,82 +174,111 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(const RopeArgs a)
         const bool is_q = hc < Hq;
         const int hh = is_q ? hc : hc - Hq;
         const T* row = is_q ? qrow + hh * a.qs2 : krow + hh * a.ks2;
-        xr[u] = ld_global_nc_l1_v4(row + d0);
-        pr[u] = ld_global_nc_l1_v4(row + pdim);
+        r0[u] = ld_global_nc_v4(row + off0);
+        r1[u] = ld_global_nc_v4(row + off1);
         if constexpr (MODE != kRopeFwd) {
           const T* grow = static_cast<const T*>(is_q ? a.gq : a.gk) + (is_q ? qo : ko) +
                           static_cast<int64_t>(hh) * D;
-          gr[u] = ld_global_nc_l1_v4(grow + d0);
-          pgr[u] = ld_global_nc_l1_v4(grow + pdim);
+          gr0[u] = ld_global_nc_v4(grow + off0);
+          gr1[u] = ld_global_nc_v4(grow + off1);
         }
         if constexpr (MODE == kRopeBwdY) rs[u] = a.rstd[static_cast<int64_t>(tok) * H + hc];
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int h = (p0 + u) * HPW + slot;
-        float x[VEC], px[VEC], res[VEC];
-        {
-          Vec16<T> v, pv;
-          v.raw = xr[u];
-          pv.raw = pr[u];
-          v.to_float(x);
-          pv.to_float(px);
-        }
+        float2 x0[NP], x1[NP], o0[NP], o1[NP];
+        C::unpack(r0[u], x0);
+        C::unpack(r1[u], x1);
         if constexpr (MODE == kRopeFwd) {
-          float ss = 0.0f;
+          float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
-          for (int i = 0; i < VEC; ++i) ss = fmaf(x[i], x[i], ss);
-          ss = group_sum<LPH>(ss);
-          const float inv = rsqrtf(ss * inv_d + a.eps);
+          for (int j = 0; j < NP; ++j) acc = __ffma2_rn(x0[j], x0[j], acc);
 #pragma unroll
-          for (int i = 0; i < VEC; ++i) res[i] = inv * fmaf(s[i], px[i], x[i] * c[i]);
-        } else {
-          float g[VEC], pg[VEC];
-          {
-            Vec16<T> v, pv;
-            v.raw = gr[u];
-            pv.raw = pgr[u];
-            v.to_float(g);
-            pv.to_float(pg);
+          for (int j = 0; j < NP; ++j) acc = __ffma2_rn(x1[j], x1[j], acc);
+          const float ss = group_sum<LPH>(acc.x + acc.y);
+          const float inv = rsqrt_ftz(fmaf(ss, inv_d, a.eps));
+          const float2 inv2 = make_float2(inv, inv);
+#pragma unroll
+          for (int j = 0; j < NP; ++j) {
+            o0[j] = __fmul2_rn(inv2, __ffma2_rn(s0[j], x1[j], __fmul2_rn(x0[j], c[j])));
+            o1[j] = __fmul2_rn(inv2, __ffma2_rn(s1[j], x0[j], __fmul2_rn(x1[j], c[j])));
           }
-          float inv, z[VEC];
+        } else {
+          float2 g0[NP], g1[NP], z0[NP], z1[NP];
+          C::unpack(gr0[u], g0);
+          C::unpack(gr1[u], g1);
+          float inv;
           if constexpr (MODE == kRopeBwdX) {
-            float ss = 0.0f;
+            float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) ss = fmaf(x[i], x[i], ss);
-            ss = group_sum<LPH>(ss);
-            inv = rsqrtf(ss * inv_d + a.eps);
+            for (int j = 0; j < NP; ++j) acc = __ffma2_rn(x0[j], x0[j], acc);
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) z[i] = x[i] * inv;
+            for (int j = 0; j < NP; ++j) acc = __ffma2_rn(x1[j], x1[j], acc);
+            const float ss = group_sum<LPH>(acc.x + acc.y);
+            inv = rsqrt_ftz(fmaf(ss, inv_d, a.eps));
+            const float2 inv2 = make_float2(inv, inv);
+#pragma unroll
+            for (int j = 0; j < NP; ++j) {
+              z0[j] = __fmul2_rn(x0[j], inv2);
+              z1[j] = __fmul2_rn(x1[j], inv2);
+            }
           } else {
             inv = rs[u];
             // inverse rotation of the saved output y gives the normalised vector
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) z[i] = fmaf(-s[i], px[i], x[i] * c[i]);
+            for (int j = 0; j < NP; ++j) {
+              z0[j] = __ffma2_rn(s0[j], x1[j], __fmul2_rn(x0[j], c[j]));
+              z1[j] = __ffma2_rn(s1[j], x0[j], __fmul2_rn(x1[j], c[j]));
+            }
           }
-          // inverse rotation of the output gradient
-          float dot = 0.0f, gn[VEC];
+          // inverse rotation of the output gradient (into g0 / g1), then mean(g_n * z)
+          float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
-          for (int i = 0; i < VEC; ++i) {
-            gn[i] = fmaf(-s[i], pg[i], g[i] * c[i]);
-            dot = fmaf(gn[i], z[i], dot);
+          for (int j = 0; j < NP; ++j) {
+            const float2 n0 = __ffma2_rn(s0[j], g1[j], __fmul2_rn(g0[j], c[j]));
+            const float2 n1 = __ffma2_rn(s1[j], g0[j], __fmul2_rn(g1[j], c[j]));
+            g0[j] = n0;
+            g1[j] = n1;
+            acc = __ffma2_rn(n0, z0[j], acc);
+            acc = __ffma2_rn(n1, z1[j], acc);
           }
-          dot = group_sum<LPH>(dot) * inv_d;
+          const float ndot = -group_sum<LPH>(acc.x + acc.y) * inv_d;
+          const float2 nd2 = make_float2(ndot, ndot), inv2 = make_float2(inv, inv);
 #pragma unroll
-          for (int i = 0; i < VEC; ++i) res[i] = inv * fmaf(-z[i], dot, gn[i]);
+          for (int j = 0; j < NP; ++j) {
+            o0[j] = __fmul2_rn(inv2, __ffma2_rn(z0[j], nd2, g0[j]));
+            o1[j] = __fmul2_rn(inv2, __ffma2_rn(z1[j], nd2, g1[j]));
+          }
         }
         if (h < H) {
           const bool is_q = h < Hq;
           const int hh = is_q ? h : h - Hq;
-          Vec16<T> o;
-          o.from_float(res);
-          st_global_v4(static_cast<T*>(is_q ? a.oq : a.ok) + (is_q ? qo : ko) +
-                           static_cast<int64_t>(hh) * D + d0,
-                       o.raw);
+          T* orow = static_cast<T*>(is_q ? a.oq : a.ok) + (is_q ? qo : ko) +
+                    static_cast<int64_t>(hh) * D;
+          st_global_v4(orow + off0, C::pack(o0));
+          st_global_v4(orow + off1, C::pack(o1));
         }
       }
     }
+    t += dt;
+    b += db;
+    if (t >= a.T) {
+      t -= a.T;
+      ++b;
+    }
   }
+}
+
+// The forward is held to 85 registers (three 256-thread blocks per SM: more
+// loads in flight, measured 10% faster); the backward keeps its registers.
+template <typename T, typename CS, int LPH, int U>
+__global__ void __launch_bounds__(256, 3) qk_norm_rope_fwd_vec_kernel(const RopeArgs a) {
+  qk_norm_rope_vec_body<T, CS, LPH, kRopeFwd, U>(a);
+}
+template <typename T, typename CS, int LPH, int MODE, int U>
+__global__ void __launch_bounds__(256) qk_norm_rope_bwd_vec_kernel(const RopeArgs a) {
+  qk_norm_rope_vec_body<T, CS, LPH, MODE, U>(a);
 }
 
 // Scalar path for any D / rotary_dim / stride: one warp per head vector, the
@@ -282,7 +371,11 @@ constexpr int rope_passes_per_batch() {
 template <typename T, typename CS, int LPH, int MODE>
 static void launch_rope_vec_lph(const RopeArgs& a, int64_t warps_needed, cudaStream_t s) {
   constexpr int U = rope_passes_per_batch<MODE>();
-  auto kern = qk_norm_rope_vec_kernel<T, CS, LPH, MODE, U>;
+  void (*kern)(const RopeArgs);
+  if constexpr (MODE == kRopeFwd)
+    kern = qk_norm_rope_fwd_vec_kernel<T, CS, LPH, U>;
+  else
+    kern = qk_norm_rope_bwd_vec_kernel<T, CS, LPH, MODE, U>;
   // persistent grid: as many 256-thread blocks as are resident at once
   static int per_sm = 0;
   if (per_sm == 0) {
@@ -300,6 +393,9 @@ static void launch_rope_vec_lph(const RopeArgs& a, int64_t warps_needed, cudaStr
 template <typename T, typename CS, int MODE>
 static void launch_rope_vec(int lph, const RopeArgs& a, int64_t warps_needed, cudaStream_t s) {
   switch (lph) {
+    case 4:
+      launch_rope_vec_lph<T, CS, 4, MODE>(a, warps_needed, s);
+      break;
     case 8:
       launch_rope_vec_lph<T, CS, 8, MODE>(a, warps_needed, s);
       break;
@@ -316,12 +412,12 @@ static void launch_rope_vec(int lph, const RopeArgs& a, int64_t warps_needed, cu
 // Returns HLM_ERR_UNSUPPORTED when the layout does not allow 16-byte vectors.
 template <typename T, int MODE>
 int rope_vec_launch(const RopeArgs& a, int cs_dtype, int kernel_id, cudaStream_t s) {
-  constexpr int VEC = 16 / sizeof(T);
-  const int lph = a.D / VEC;
-  bool vec = a.D % VEC == 0 && (lph == 8 || lph == 16 || lph == 32);
-  vec = vec && (a.rd / 2) % VEC == 0 && a.rd <= a.D;
+  constexpr int CH = 16 / sizeof(T);  // elements per 16-byte chunk, two chunks per lane
+  const int lph = a.D / (2 * CH);
+  bool vec = a.D % (2 * CH) == 0 && (lph == 4 || lph == 8 || lph == 16 || lph == 32);
+  vec = vec && (a.rd / 2) % CH == 0 && a.rd <= a.D;
   const int64_t strides[] = {a.qs0, a.qs1, a.qs2, a.ks0, a.ks1, a.ks2};
-  for (int64_t st : strides) vec = vec && st % VEC == 0;
+  for (int64_t st : strides) vec = vec && st % CH == 0;
   vec = vec && host_aligned16(a.xq) && host_aligned16(a.xk) && host_aligned16(a.oq) &&
         host_aligned16(a.ok);
   if (MODE != kRopeFwd) vec = vec && host_aligned16(a.gq) && host_aligned16(a.gk);

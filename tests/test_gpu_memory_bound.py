@@ -160,3 +160,34 @@ def test_qk_norm_rope_c2_strided_bf16(fraction, cuda_device):
     assert_bf16_close(gqkv[..., H * D: 2 * H * D].reshape(B, T, H, D), gk, what="grad k")
     assert torch.count_nonzero(gqkv[..., 2 * H * D:]) == 0
     _dev_err_zero()
+
+
+@pytest.mark.parametrize("B,T,Hq,Hk,D,fraction,cs_dtype", [
+    (3, 1000, 4, 2, 64, 0.25, torch.bfloat16),    # 4 lanes per head vector, rotary_dim 16
+    (2, 1500, 2, 1, 256, 0.5, torch.float32),     # 16 lanes per head vector, fp32 cos/sin
+    (4, 700, 3, 3, 128, 0.125, torch.bfloat16),   # rotary_dim 16: one rotated lane per head
+    (5, 900, 6, 6, 128, 0.0, torch.bfloat16),     # no rotation: norm only
+])
+def test_qk_norm_rope_vec_layouts_bf16(B, T, Hq, Hk, D, fraction, cs_dtype, cuda_device):
+    """Lane layouts of the vector kernel other than the C2 shape (head dims 64 and
+    256, GQA head counts, fp32 tables, rotary_dim 16 and 0), forward and backward,
+    with more tokens than resident warps so that every warp walks several tokens."""
+    from hackable_lm_b200 import kernels
+
+    q = seeded(B, T, Hq, D).to(torch.bfloat16)
+    k = seeded(B, T, Hk, D, seed=3).to(torch.bfloat16)
+    dq = seeded(B, T, Hq, D, seed=1).to(torch.bfloat16)
+    dk = seeded(B, T, Hk, D, seed=2).to(torch.bfloat16)
+    cos, sin = oracle.rope_tables(D, T, 10_000.0, fraction, dtype=cs_dtype)
+    qd = q.to(cuda_device).requires_grad_(True)
+    kd = k.to(cuda_device).requires_grad_(True)
+    qo, ko = kernels.qk_norm_rope_triton(qd, kd, cos.transpose(1, 2).to(cuda_device),
+                                         sin.transpose(1, 2).to(cuda_device), 1e-6)
+    torch.autograd.backward((qo, ko), (dq.to(cuda_device), dk.to(cuda_device)))
+    oq, ok_ = oracle.qk_norm_rope(q, k, cos, sin, 1e-6)
+    assert_bf16_close(qo, oq, what="q_out")
+    assert_bf16_close(ko, ok_, what="k_out")
+    gq, gk = oracle.qk_norm_rope_backward(q, k, dq, dk, cos, sin, 1e-6)
+    assert_bf16_close(qd.grad, gq, what="grad q")
+    assert_bf16_close(kd.grad, gk, what="grad k")
+    _dev_err_zero()
