@@ -27,6 +27,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "hlm_strerror": ([c_int], c_char_p),
     "hlm_device_error_get": ([POINTER(c_int), _P], c_int),
     "hlm_device_error_clear": ([_P], c_int),
+    "hlm_selftest_bounded_wait": ([_I64, c_int, _P], c_int),
     "hlm_launch_count": ([], c_uint64),
     "hlm_profile_begin": ([c_int, POINTER(c_void_p), POINTER(c_void_p), c_int], c_int),
     "hlm_profile_end": ([c_int, POINTER(c_int)], c_int),
@@ -109,6 +110,23 @@ def device_error(stream: int = 0) -> int:
 
 def clear_device_error(stream: int = 0) -> None:
     check(load().hlm_device_error_clear(c_void_p(stream)), "hlm_device_error_clear")
+
+
+# Device error word codes (HLM_DEVERR_* in include/hlm_b200.h).
+DEVERR_NAMES = {
+    0: "none", 1: "timeout: MMA issuer waiting for a TMA stage",
+    2: "timeout: producer waiting for a free stage", 3: "timeout: epilogue waiting for an accumulator",
+    4: "timeout: MMA issuer waiting for the epilogue", 5: "timeout: teardown drain of TMA copies",
+    6: "unexpected tensor-memory address", 7: "self-test wait ran out (expected)",
+}
+DEVERR_SELFTEST_TIMEOUT = 7
+
+
+def selftest_bounded_wait(limit_us: int, scope: int = 0, stream: int = 0) -> None:
+    """Launch the bounded-wait self-test (a wait on an mbarrier nothing arrives at,
+    limited to limit_us); it records DEVERR_SELFTEST_TIMEOUT in the device error word."""
+    check(load().hlm_selftest_bounded_wait(int(limit_us), int(scope), c_void_p(stream)),
+          "hlm_selftest_bounded_wait")
 
 
 # Kernel ids of hlm_profile_begin (include/hlm_b200.h).

@@ -50,7 +50,14 @@ enum DeviceErrorCode : int {
   kDevErrTimeoutTmemEmpty = 4, // MMA warp waited too long for the epilogue
   kDevErrTimeoutDrain = 5,     // teardown drain of in-flight TMA copies ran out
   kDevErrBadTmem = 6,          // tcgen05.alloc returned an unexpected address
+  kDevErrSelftestTimeout = 7,  // hlm_selftest_bounded_wait: the wait ran out (expected)
 };
+static_assert(kDevErrTimeoutFull == HLM_DEVERR_TIMEOUT_FULL && kDevErrTimeoutEmpty == HLM_DEVERR_TIMEOUT_EMPTY &&
+                  kDevErrTimeoutTmemFull == HLM_DEVERR_TIMEOUT_TMEM_FULL &&
+                  kDevErrTimeoutTmemEmpty == HLM_DEVERR_TIMEOUT_TMEM_EMPTY &&
+                  kDevErrTimeoutDrain == HLM_DEVERR_TIMEOUT_DRAIN && kDevErrBadTmem == HLM_DEVERR_BAD_TMEM &&
+                  kDevErrSelftestTimeout == HLM_DEVERR_SELFTEST_TIMEOUT,
+              "device error codes match the public header");
 
 // Upper bound for any single mbarrier wait.  Legitimate waits in these kernels
 // are microseconds; one second means something is broken.
@@ -135,16 +142,20 @@ constexpr uint32_t kWaitSliceNs = 20000;  // suspend slice between timeout check
 // `code` in the error word) if the phase did not complete within the timeout.
 // The error word is sticky across launches, so it is not used to cut waits
 // short: every wait in a failing CTA ends by its own timeout.
-HLM_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+HLM_DEVICE bool mbar_wait_bounded(uint32_t bar, uint32_t parity, unsigned long long limit_ns,
+                                  int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait_sleep(bar, parity, kWaitSliceNs)) {
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_error(err, code);
       return false;
     }
   }
   return true;
+}
+HLM_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_bounded(bar, parity, kWaitTimeoutNs, err, code);
 }
 
 // try_wait with cluster-scope acquire (pairs with mbar_arrive_cluster).
@@ -161,15 +172,19 @@ HLM_DEVICE bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity, uint32_t hi
 }
 // Bounded wait with cluster-scope acquire, for barriers that the peer CTA of a
 // pair arrives on.
-HLM_DEVICE bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* err, int code) {
+HLM_DEVICE bool mbar_wait_cluster_bounded(uint32_t bar, uint32_t parity, unsigned long long limit_ns,
+                                          int* err, int code) {
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait_cluster(bar, parity, kWaitSliceNs)) {
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_error(err, code);
       return false;
     }
   }
   return true;
+}
+HLM_DEVICE bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_cluster_bounded(bar, parity, kWaitTimeoutNs, err, code);
 }
 
 // Wait by lane 0, result broadcast to the warp (keeps .sync.aligned

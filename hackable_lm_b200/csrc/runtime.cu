@@ -99,6 +99,39 @@ extern "C" int hlm_device_error_clear(void* stream) {
   return HLM_OK;
 }
 
+// One warp: lane 0 waits on a fresh mbarrier (phase 0 never completes: no
+// thread arrives) through the bounded wait helpers the GEMM kernels use.
+__global__ void __launch_bounds__(32) selftest_bounded_wait_kernel(unsigned long long limit_ns,
+                                                                   int scope, int* err) {
+  __shared__ alignas(8) uint64_t bar;
+  const uint32_t b = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    if (scope == 0)
+      mbar_wait_bounded(b, 0, limit_ns, err, kDevErrSelftestTimeout);
+    else
+      mbar_wait_cluster_bounded(b, 0, limit_ns, err, kDevErrSelftestTimeout);
+  }
+  __syncwarp();
+}
+
+extern "C" int hlm_selftest_bounded_wait(int64_t limit_us, int scope, void* stream) {
+  if (limit_us < 1 || limit_us > 1000000 || (scope != 0 && scope != 1)) return HLM_ERR_INVALID_ARG;
+  int* err = device_error_ptr();
+  if (err == nullptr) return HLM_ERR_LAUNCH;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  {
+    LaunchScope ls(0, s);
+    selftest_bounded_wait_kernel<<<1, 32, 0, s>>>(static_cast<unsigned long long>(limit_us) * 1000ull,
+                                                  scope, err);
+  }
+  return launch_status();
+}
+
 extern "C" uint64_t hlm_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int hlm_profile_begin(int kernel_id, void* const* start_events, void* const* stop_events,

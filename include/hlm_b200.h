@@ -56,6 +56,27 @@ int hlm_device_error_get(int* out, void* stream);
 /* Reset the device error word to 0 (stream-ordered). */
 int hlm_device_error_clear(void* stream);
 
+/* Codes of the device error word.  A kernel whose bounded wait runs out
+ * records the first code (later ones are dropped), drains its own in-flight
+ * copies, frees its tensor memory and returns; nothing traps. */
+#define HLM_DEVERR_NONE 0
+#define HLM_DEVERR_TIMEOUT_FULL 1       /* MMA issuer waited too long for a TMA stage */
+#define HLM_DEVERR_TIMEOUT_EMPTY 2      /* producer waited too long for a free stage */
+#define HLM_DEVERR_TIMEOUT_TMEM_FULL 3  /* epilogue waited too long for an accumulator */
+#define HLM_DEVERR_TIMEOUT_TMEM_EMPTY 4 /* MMA issuer waited too long for the epilogue */
+#define HLM_DEVERR_TIMEOUT_DRAIN 5      /* teardown drain of in-flight TMA copies ran out */
+#define HLM_DEVERR_BAD_TMEM 6           /* tcgen05.alloc returned an unexpected address */
+#define HLM_DEVERR_SELFTEST_TIMEOUT 7   /* hlm_selftest_bounded_wait ran out, as it should */
+
+/* Self-test of the bounded waits: one warp waits on an mbarrier that nothing
+ * arrives at, with the same wait helper the GEMM roles use (scope 0: CTA-scope
+ * acquire; 1: cluster-scope acquire) and a limit of limit_us microseconds
+ * (1 .. 1000000) instead of the kernels' 1 s.  When the limit runs out the
+ * kernel records HLM_DEVERR_SELFTEST_TIMEOUT and returns, leaving the context
+ * usable.  Asynchronous on `stream`; read the result with
+ * hlm_device_error_get. */
+int hlm_selftest_bounded_wait(int64_t limit_us, int scope, void* stream);
+
 /* Number of kernels this library has launched in this process (all devices).
  * Lets a harness count the library's own launches inside a timed region. */
 uint64_t hlm_launch_count(void);

@@ -66,6 +66,10 @@ def test_invalid_arguments_are_rejected_before_any_launch(lib):
     assert lib.hlm_swiglu_fwd(ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 4, 7, None) == -2
     # fused QKV only supports head_dim 128
     assert lib.hlm_qkv_rope_fwd(*([None] * 8), 1, 8, 64, 1, 1, 64, 32, 32, 1, 1e-6, None) == -2
+    # bounded-wait self-test: limit outside 1 us .. 1 s, or an unknown scope
+    assert lib.hlm_selftest_bounded_wait(0, 0, None) == -1
+    assert lib.hlm_selftest_bounded_wait(2_000_000, 0, None) == -1
+    assert lib.hlm_selftest_bounded_wait(1000, 2, None) == -1
 
 
 def test_workspace_queries(lib):
