@@ -15,13 +15,16 @@
 
 namespace hlm {
 
-constexpr int kMlpStages = 4;
-constexpr int kMlpEpiWarps = 8;  // two warps per TMEM lane quadrant, one 64-unit group each
+// Four epilogue warps (one per TMEM lane quadrant, both 64-unit groups each)
+// leave shared memory for five stages: measured 8% faster than eight warps
+// (two per quadrant) with four stages at X [32768,768], W [4096,768].
+constexpr int kMlpStages = 5;
+constexpr int kMlpEpiWarps = 4;
 
 // Epilogue: per warp (32 rows) and 64-unit group: gate and up (2 x 64 fp32
 // columns from TMEM) rounded to bf16 and staged as two 32x64 boxes for the
 // gate_up output, h = silu(gate) * up staged as a third box; one lane issues
-// the three TMA stores.  Eight epilogue warps: two per lane quadrant.
+// the three TMA stores.
 struct EpiSwiGLU {
   struct Params {
     alignas(64) CUtensorMap map_gu;  // gate_up [M][2H] bf16, box {64, 32}
