@@ -69,10 +69,6 @@ HLM_DEVICE unsigned long long globaltimer_ns() {
   return t;
 }
 
-HLM_DEVICE int load_error_volatile(const int* err) {
-  return *reinterpret_cast<const volatile int*>(err);
-}
-
 HLM_DEVICE void record_error(int* err, int code) { atomicCAS(err, 0, code); }
 
 // ---------------------------------------------------------------------------
@@ -254,30 +250,6 @@ HLM_DEVICE void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0
 HLM_DEVICE void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)
-               : "memory");
-}
-
-HLM_DEVICE void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst_smem),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
-}
-
-HLM_DEVICE uint4 ld_shared_v4(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr));
-  return v;
-}
-
-// L2 prefetch of a 2-D box described by a tensor map (no shared-memory write).
-HLM_DEVICE void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1)
                : "memory");
 }
 
@@ -484,15 +456,6 @@ HLM_DEVICE uint4 ld_global_nc_v4(const void* p) {
                : "l"(p));
   return v;
 }
-// Read-only 16-byte load that allocates in L1 (a second read of the same
-// line from the warp, e.g. a RoPE rotation partner, then hits L1).
-HLM_DEVICE uint4 ld_global_nc_l1_v4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
 HLM_DEVICE uint4 ld_global_v4(const void* p) {
   uint4 v;
   asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -535,15 +498,6 @@ HLM_DEVICE uint32_t max_bf16x2(uint32_t a, uint32_t b) {
   asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
-// Round-to-nearest-even of two finite floats to a bf16 pair on the integer
-// pipe (add 0x7fff plus the lsb of the kept half, keep the high halves), for
-// loops where the conversion unit is already busy with ex2.  Not for NaN/inf.
-HLM_DEVICE uint32_t pack_bf16x2_alu(float lo, float hi) {
-  uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
-  a += 0x7fffu + ((a >> 16) & 1u);
-  b += 0x7fffu + ((b >> 16) & 1u);
-  return __byte_perm(a, b, 0x7632);
-}
 HLM_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h2);
@@ -561,8 +515,6 @@ HLM_DEVICE float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
-
-HLM_DEVICE bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Host helper: 16-byte alignment of a device pointer.
 inline bool host_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
