@@ -81,3 +81,11 @@ def test_workspace_queries(lib):
     assert 4096 * v * 2 <= small < full
     assert lib.hlm_rms_norm_bwd_workspace_bytes(1024, 384) > 0
     assert lib.hlm_qkv_rope_bwd_workspace_bytes(16, 2048, 768, 6, 6, 128) >= 2 * 16 * 2048 * 768 * 2
+
+
+def test_device_error_codes_match_header():
+    """The Python names of the device error codes cover exactly HLM_DEVERR_* of the header."""
+    text = HEADER.read_text()
+    codes = {int(v) for v in re.findall(r"#define HLM_DEVERR_[A-Z_]+ (\d+)", text)}
+    assert codes == set(_lib.DEVERR_NAMES)
+    assert _lib.DEVERR_SELFTEST_TIMEOUT == int(re.search(r"#define HLM_DEVERR_SELFTEST_TIMEOUT (\d+)", text).group(1))
