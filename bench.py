@@ -341,8 +341,8 @@ D12_FLOPS_PER_TOKEN = 887_095_296  # config.estimate_flops_per_token, full causa
 
 # operator calls per micro-step: per-layer kernels once per layer, LM-head kernels once
 D12_KERNELS = {"lm_logits": 1, "lm_dlogits": 1, "lm_dx": 1, "lm_dw": 1, "gate_up": 12, "qkv_fwd": 12, "qkv_bwd_norm": 12,
-               "qkv_dx": 12, "qkv_dw": 12, "swiglu_fwd": 12, "swiglu_bwd": 12, "rmsnorm_fwd": 25,
-               "rmsnorm_bwd": 25}
+               "qkv_dx": 12, "qkv_dw": 12, "swiglu_fwd": 12, "swiglu_bwd": 12, "swiglu_down_bwd": 12,
+               "rmsnorm_fwd": 25, "rmsnorm_bwd": 25}
 
 
 def d12_config(world: int, accum: int) -> dict:
@@ -421,6 +421,9 @@ def bench_d12(args, d: Dist, device) -> dict:
         "rmsnorm_bwd": 2.0 * M * C * (3 + 4 * (n_fwd - 1)) / n_fwd,
         "qkv_bwd_norm": 2.0 * M * Dq * 6,         # read q, k, dq, dk; write dq_in, dk_in
         "lm_dlogits": 4.0 * M * V,                # bf16 logits read + dlogits written in place
+        # down grad_h GEMM + SwiGLU backward: read grad_y [M,C], gate_up [M,2H], W_down [C,H];
+        # write grad_gate_up [M,2H] (HBM-bound: 2*M*C*H FLOP over these bytes is below the ridge)
+        "swiglu_down_bwd": 2.0 * (M * C + 4 * M * Hm + C * Hm),
     }
     breakdown, totals = {}, {}
     for k, t in timers.items():
@@ -608,6 +611,17 @@ def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
     tensor("gate_up_swiglu X[32768,768] W[4096,768]", lambda a: ops.gate_up_swiglu(a, wg), (xg,),
            2 * 32768 * 768 * 4096)
     del xg, wg
+    # down projection backward with the SwiGLU backward in its epilogue (d12 shape): HBM-bound,
+    # 2*M*C*H = 103 GFLOP against 590 MB (read grad_y, gate_up, W_down; write grad_gate_up)
+    if want("swiglu_down_bwd"):
+        gyd = torch.randn(32768, 768, generator=g).to(torch.bfloat16).to(device)
+        gud = torch.randn(32768, 4096, generator=g).to(torch.bfloat16).to(device)
+        wdn = (torch.randn(768, 2048, generator=g) * 0.02).to(torch.bfloat16).to(device)
+        outd = torch.empty_like(gud)
+        hbm("swiglu_down_bwd dY[32768,768] W[768,2048] gate_up[32768,4096]",
+            lambda a, b: ops.swiglu_down_grad(a, wdn, b, out=outd), (gyd, gud),
+            2 * (32768 * 768 + 2 * 32768 * 4096 + 768 * 2048))
+        del gyd, gud, wdn, outd
     if not want("qkv_rope_bwd"):
         return res
     qo, ko, vo, rs = ops.qkv_rope(xq, wq, c1, s1, 6, 6, 1e-6)

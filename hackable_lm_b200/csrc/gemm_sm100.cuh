@@ -25,9 +25,20 @@
 // returns.
 #pragma once
 
+#include <type_traits>
+
 #include "hlm_common.cuh"
 
 namespace hlm {
+
+// Epilogues may declare `static HLM_DEVICE void init(uint8_t* epi_smem)`: the
+// kernel calls it from the thread that initialises the pipeline barriers,
+// before the fence and the CTA/cluster barrier that publish them (for an
+// epilogue's own mbarriers and counters in its shared-memory region).
+template <class E, class = void>
+struct epi_has_init : std::false_type {};
+template <class E>
+struct epi_has_init<E, std::void_t<decltype(E::init(static_cast<uint8_t*>(nullptr)))>> : std::true_type {};
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
@@ -361,6 +372,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads<EPI_WAR
       mbar_init(TFULL_BAR(a), 1);
       mbar_init(TEMPTY_BAR(a), 2 * EPI_WARPS);
     }
+    if constexpr (epi_has_init<Epi>::value) Epi::init(base_ptr + L::kEpiOffset);
     fence_mbar_init();
     prefetch_tensormap(&tmA0);
     if (p.a_seg1 > 0) {

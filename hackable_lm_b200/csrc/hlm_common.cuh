@@ -51,12 +51,14 @@ enum DeviceErrorCode : int {
   kDevErrTimeoutDrain = 5,     // teardown drain of in-flight TMA copies ran out
   kDevErrBadTmem = 6,          // tcgen05.alloc returned an unexpected address
   kDevErrSelftestTimeout = 7,  // hlm_selftest_bounded_wait: the wait ran out (expected)
+  kDevErrTimeoutEpiLoad = 8,   // an epilogue waited too long for its own TMA input load
 };
 static_assert(kDevErrTimeoutFull == HLM_DEVERR_TIMEOUT_FULL && kDevErrTimeoutEmpty == HLM_DEVERR_TIMEOUT_EMPTY &&
                   kDevErrTimeoutTmemFull == HLM_DEVERR_TIMEOUT_TMEM_FULL &&
                   kDevErrTimeoutTmemEmpty == HLM_DEVERR_TIMEOUT_TMEM_EMPTY &&
                   kDevErrTimeoutDrain == HLM_DEVERR_TIMEOUT_DRAIN && kDevErrBadTmem == HLM_DEVERR_BAD_TMEM &&
-                  kDevErrSelftestTimeout == HLM_DEVERR_SELFTEST_TIMEOUT,
+                  kDevErrSelftestTimeout == HLM_DEVERR_SELFTEST_TIMEOUT &&
+                  kDevErrTimeoutEpiLoad == HLM_DEVERR_TIMEOUT_EPI_LOAD,
               "device error codes match the public header");
 
 // Upper bound for any single mbarrier wait.  Legitimate waits in these kernels
@@ -247,6 +249,14 @@ HLM_DEVICE void bulk_wait_group_read() {
 // Wait until every committed bulk group has fully completed.
 HLM_DEVICE void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+HLM_DEVICE uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
 HLM_DEVICE void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)

@@ -20,6 +20,7 @@ namespace hlm {
 // (two per quadrant) with four stages at X [32768,768], W [4096,768].
 constexpr int kMlpStages = 5;
 constexpr int kMlpEpiWarps = 4;
+constexpr int kMlpBwdStages = 4;  // 4 x 32 KB stages + 96 KB of epilogue boxes
 
 // Epilogue: per warp (32 rows) and 64-unit group: gate and up (2 x 64 fp32
 // columns from TMEM) rounded to bf16 and staged as two 32x64 boxes for the
@@ -95,6 +96,128 @@ struct EpiSwiGLU {
   }
 };
 
+// Backward of the MLP's SwiGLU fused into the down projection's grad_h GEMM:
+//   grad_h[M, H]    = grad_y[M, C] @ W_down[C, H]        (rounded to bf16, as
+//                                                         the reference's GEMM output)
+//   grad_gate_up    = swiglu_backward(gate_up, grad_h)  (kernels.py:690-700,
+//                                                         same fp32 arithmetic as
+//                                                         swiglu_bwd_vec_kernel)
+// grad_h never goes to memory.  Epilogue (4 warps, one per TMEM lane
+// quadrant, 32 rows each; a 256-column tile is four 64-unit groups): per group
+// the warp's gate and up boxes (32 x 64 bf16 each) arrive by TMA into one of
+// two input buffers, each with its own mbarrier, the next group's boxes being
+// requested while this one is computed; dgate / dup are staged as two boxes
+// and written with TMA stores.  The buffers' barrier phases continue across
+// tiles through a per-warp use counter kept in shared memory.
+struct EpiSwiGLUBwd {
+  struct Params {
+    alignas(64) CUtensorMap map_gu;   // gate_up [M][2H] bf16, box {64, 32}
+    alignas(64) CUtensorMap map_out;  // grad_gate_up [M][2H] bf16, box {64, 32}
+    int H;
+  };
+  static constexpr int kBoxBytes = 32 * 128;
+  static constexpr int kWarpBytes = 6 * kBoxBytes;  // 2 input buffers x (gate, up) + (dgate, dup)
+  static constexpr int kBarOffset = 4 * kWarpBytes;
+  static constexpr int kCtrOffset = kBarOffset + 4 * 2 * 8;
+  template <int EPI_WARPS>
+  static constexpr int smem_bytes() {
+    static_assert(EPI_WARPS == 4, "one epilogue warp per lane quadrant");
+    return kCtrOffset + 4 * 4;
+  }
+  static HLM_DEVICE void init(uint8_t* smem) {
+    const uint32_t b = smem_u32(smem);
+    for (int w = 0; w < 4; ++w) {
+      mbar_init(b + kBarOffset + 16 * w, 1);
+      mbar_init(b + kBarOffset + 16 * w + 8, 1);
+      reinterpret_cast<volatile uint32_t*>(smem + kCtrOffset)[w] = 0u;
+    }
+  }
+
+  template <int BN, int kParts>
+  static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t* smem, uint32_t taddr,
+                             int m_tile, int n_tile, int, int quad, int, int lane) {
+    static_assert(BN == 256 && kParts == 1, "four 64-unit groups per tile, one warp per quadrant");
+    const int row0 = m_tile * kBM + quad * 32;
+    if (row0 >= p.M) return;  // no rows of this warp in the tile: no loads, barrier phases unchanged
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t in0 = sbase + static_cast<uint32_t>(quad * kWarpBytes);  // buffer b, tensor t: + (2b + t) boxes
+    const uint32_t outb = in0 + 4u * kBoxBytes;                               // dgate, then dup
+    const uint32_t bar0 = sbase + static_cast<uint32_t>(kBarOffset + 16 * quad);
+    volatile uint32_t* ctr = reinterpret_cast<volatile uint32_t*>(smem + kCtrOffset) + quad;
+    const int h0 = n_tile * BN;  // hidden unit of the tile's first column
+    uint32_t n = 0;
+    if (lane == 0) n = *ctr;
+    n = __shfl_sync(0xffffffffu, n, 0);
+    auto request = [&](int g) {  // lane 0: group g's gate and up boxes into buffer g & 1
+      const uint32_t b = static_cast<uint32_t>(g & 1);
+      const uint32_t bar = bar0 + 8u * b;
+      mbar_arrive_expect_tx(bar, 2 * kBoxBytes);
+      tma_load_2d(in0 + (2u * b) * kBoxBytes, &ep.map_gu, h0 + g * 64, row0, bar);
+      tma_load_2d(in0 + (2u * b + 1u) * kBoxBytes, &ep.map_gu, ep.H + h0 + g * 64, row0, bar);
+    };
+    if (lane == 0) request(0);
+#pragma unroll 1
+    for (int g = 0; g < BN / 64; ++g) {
+      // buffer (g + 1) & 1 was last read by group g - 1 (or the previous tile's
+      // last group), whose reads completed before the warp's last __syncwarp
+      if (lane == 0 && g + 1 < BN / 64) request(g + 1);
+      const uint32_t b = static_cast<uint32_t>(g & 1);
+      const uint32_t par = ((n + static_cast<uint32_t>(g)) >> 1) & 1u;
+      if (!warp_wait(bar0 + 8u * b, par, p.err, kDevErrTimeoutEpiLoad, lane)) return;
+      // the stores that last read the output boxes must be done with them
+      if (lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
+      const uint32_t gate_box = in0 + (2u * b) * kBoxBytes;
+      const uint32_t up_box = gate_box + kBoxBytes;
+#pragma unroll 1
+      for (int hs = 0; hs < 2; ++hs) {
+        uint32_t d[32];
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(g * 64 + hs * 32), d);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cc = hs * 4 + c;  // 16-byte chunk of the row's 128 bytes
+          const uint32_t off = static_cast<uint32_t>(lane * 128 + ((cc ^ (lane & 7)) << 4));
+          const uint4 gr = ld_shared_v4(gate_box + off);
+          const uint4 ur = ld_shared_v4(up_box + off);
+          const uint32_t gw[4] = {gr.x, gr.y, gr.z, gr.w};
+          const uint32_t uw[4] = {ur.x, ur.y, ur.z, ur.w};
+          uint32_t og[4], ou[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            // grad_h rounded to bf16 first, like the reference's GEMM output
+            const uint32_t dh = pack_bf16x2(__uint_as_float(d[8 * c + 2 * j]), __uint_as_float(d[8 * c + 2 * j + 1]));
+            float rg[2], ru[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float gv = e ? bf16_hi(gw[j]) : bf16_lo(gw[j]);
+              const float uv = e ? bf16_hi(uw[j]) : bf16_lo(uw[j]);
+              const float dv = e ? bf16_hi(dh) : bf16_lo(dh);
+              const float sg = sigmoid_fast(gv);
+              const float silu = gv * sg;
+              const float dsilu = sg * (1.0f + gv * (1.0f - sg));
+              rg[e] = dv * uv * dsilu;
+              ru[e] = dv * silu;
+            }
+            og[j] = pack_bf16x2(rg[0], rg[1]);
+            ou[j] = pack_bf16x2(ru[0], ru[1]);
+          }
+          st_shared_v4(outb + off, make_uint4(og[0], og[1], og[2], og[3]));
+          st_shared_v4(outb + kBoxBytes + off, make_uint4(ou[0], ou[1], ou[2], ou[3]));
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&ep.map_out, h0 + g * 64, row0, outb);
+        tma_store_2d(&ep.map_out, ep.H + h0 + g * 64, row0, outb + kBoxBytes);
+        bulk_commit_group();
+      }
+    }
+    if (lane == 0) *ctr = n + static_cast<uint32_t>(BN / 64);
+  }
+};
+
 }  // namespace hlm
 
 using namespace hlm;
@@ -127,4 +250,31 @@ extern "C" int hlm_gate_up_swiglu_fwd(const void* x, const void* w_gate_up, void
   if (p.err == nullptr) return HLM_ERR_LAUNCH;
   return launch_gemm_pair<256, kMlpStages, false, false, EpiSwiGLU, kMlpEpiWarps>(
       mx, mx, mx, mw, p, ep, static_cast<cudaStream_t>(stream), HLM_KERNEL_GATE_UP);
+}
+
+extern "C" int hlm_swiglu_down_bwd(const void* grad_y, const void* w_down, const void* gate_up,
+                                   void* grad_gate_up, int64_t M, int64_t C, int64_t H, void* stream) {
+  if (M < 0 || C <= 0 || H <= 0) return HLM_ERR_INVALID_ARG;
+  if (M == 0) return HLM_OK;
+  if (grad_y == nullptr || w_down == nullptr || gate_up == nullptr || grad_gate_up == nullptr)
+    return HLM_ERR_INVALID_ARG;
+  if (C % 64 != 0 || H % 256 != 0 || M > (1ll << 31) - 512 || 2 * H > (1ll << 30))
+    return HLM_ERR_UNSUPPORTED;
+  if (!host_aligned16(grad_y) || !host_aligned16(w_down) || !host_aligned16(gate_up) ||
+      !host_aligned16(grad_gate_up))
+    return HLM_ERR_UNSUPPORTED;
+  CUtensorMap ma, mb;
+  if (!encode_bf16_map(&ma, grad_y, C, M, C, kBM)) return HLM_ERR_DRIVER;  // A [M][C], K-major
+  if (!encode_bf16_map(&mb, w_down, H, C, H, 64)) return HLM_ERR_DRIVER;   // B = W_down [C][H], N-major
+  EpiSwiGLUBwd::Params ep;
+  if (!encode_bf16_map(&ep.map_gu, gate_up, 2 * H, M, 2 * H, 32) ||
+      !encode_bf16_map(&ep.map_out, grad_gate_up, 2 * H, M, 2 * H, 32))
+    return HLM_ERR_DRIVER;
+  ep.H = static_cast<int>(H);
+  GemmParams p;
+  gemm_tiling_pair(p, static_cast<int>(M), static_cast<int>(H), static_cast<int>(C), 256, 1);
+  p.err = device_error_ptr();
+  if (p.err == nullptr) return HLM_ERR_LAUNCH;
+  return launch_gemm_pair<256, kMlpBwdStages, false, true, EpiSwiGLUBwd, 4>(
+      ma, ma, ma, mb, p, ep, static_cast<cudaStream_t>(stream), HLM_KERNEL_SWIGLU_DOWN_BWD);
 }

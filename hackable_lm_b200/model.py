@@ -10,8 +10,10 @@ CPU), ``"b200"`` the hand-written sm_100a kernels:
 
 * QKVProjection.fwd_b200     -> fused tcgen05 GEMM + QK-norm + RoPE (qkv_rope)
 * OutputProjection.fwd_b200  -> o_proj GEMM + fused residual-add + RMSNorm
-* GateUpProjection.fwd_b200  -> gate_up GEMM + SwiGLU kernel
+* GateUpProjection.fwd_b200  -> gate_up GEMM with the SwiGLU in its epilogue
 * DownProjection.fwd_b200    -> down GEMM + fused residual-add + RMSNorm
+* MLP (both of the above on b200) -> gate_up_swiglu + swiglu_down: the down
+  GEMM's backward computes grad_h and the SwiGLU backward in one kernel
 * LMHeadProjection.fwd_b200  -> fused LM head + cross-entropy
 * input norm                 -> RMSNorm kernel
 
@@ -229,6 +231,15 @@ class MLP(nn.Module):
         self.down = DownProjection(config)
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor):
+        if self.gate_up.selected_backend() == "b200" and self.down.selected_backend() == "b200":
+            w_gu = self.gate_up.gate_up_proj.weight
+            w_dn = self.down.down_proj.weight
+            if ops.gate_up_swiglu_supported(x, w_gu) and ops.swiglu_down_supported(w_gu, w_dn):
+                # gate_up GEMM with the SwiGLU in its epilogue, then the down GEMM whose
+                # backward computes grad_h and the SwiGLU backward in one kernel
+                h, gate_up = ops.gate_up_swiglu(x, w_gu)
+                y = ops.swiglu_down(h, gate_up, w_dn)
+                return kernels.residual_rms_norm(residual, y, self.down.norm_eps)
         return self.down(self.gate_up(x), residual)
 
 

@@ -145,9 +145,9 @@ def _gate_up_setup(ctx, inputs, output):
     x, weight = inputs
     _, gate_up = output
     ctx.save_for_backward(x, weight, gate_up)
-    # gate_up is a saved activation, not a differentiable output: no zero-filled
-    # [M, 2H] gradient is materialised for it in the backward
-    ctx.mark_non_differentiable(gate_up)
+    # gate_up is differentiable so that swiglu_down can hand its gradient
+    # straight to it; an output that receives no gradient arrives as None (no
+    # zero-filled [M, 2H] tensor is materialised)
     ctx.set_materialize_grads(False)
 
 
@@ -168,6 +168,71 @@ def _gate_up_bwd(ctx, grad_h, grad_gate_up):
 
 
 gate_up_swiglu.register_autograd(_gate_up_bwd, setup_context=_gate_up_setup)
+
+
+def swiglu_down_supported(w_gate_up: torch.Tensor, w_down: torch.Tensor) -> bool:
+    """Shapes and dtypes of the fused down-projection backward (grad_h GEMM + SwiGLU backward)."""
+    C, H = w_down.shape
+    return (w_down.is_cuda and w_down.dtype == torch.bfloat16 and w_gate_up.dtype == torch.bfloat16
+            and C % 64 == 0 and H % 256 == 0 and w_gate_up.shape[0] == 2 * H)
+
+
+# Down projection of h = swiglu(gate_up) (reference: model.py:295-304, the F.linear of
+# DownProjection; its backward composed with _swiglu_backward, kernels.py:690-700)
+@torch.library.custom_op("hackable_lm_b200::swiglu_down", mutates_args=())
+def swiglu_down(h: torch.Tensor, gate_up: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """y = h @ weight^T, where h must be swiglu(gate_up) (the h and gate_up returned
+    together by gate_up_swiglu).  The backward does not return a gradient for h:
+    it sends the gradient through the SwiGLU to gate_up directly, computing
+    grad_h = grad_y @ weight and the SwiGLU backward in one tcgen05 GEMM
+    (grad_h never goes to memory); the weight gradient is grad_y^T @ h."""
+    _require_cuda(h, gate_up, weight)
+    return torch.nn.functional.linear(h, weight)
+
+
+@swiglu_down.register_fake
+def _swiglu_down_fake(h, gate_up, weight):
+    return h.new_empty((*h.shape[:-1], weight.shape[0]))
+
+
+def _swiglu_down_setup(ctx, inputs, output):
+    h, gate_up, weight = inputs
+    ctx.save_for_backward(h, gate_up, weight)
+    ctx.set_materialize_grads(False)
+
+
+def swiglu_down_grad(grad_y: torch.Tensor, weight: torch.Tensor, gate_up: torch.Tensor,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """grad_gate_up = swiglu_backward(gate_up, grad_y @ weight) in one kernel (no autograd):
+    grad_y [..., C], weight [C, H] (the down projection's nn.Linear weight), gate_up [..., 2H]."""
+    dev = _require_cuda(grad_y, weight, gate_up)
+    C, H = weight.shape
+    gy = grad_y.contiguous()
+    g = gate_up.contiguous()
+    w = weight.contiguous()
+    if out is None:
+        out = torch.empty_like(g)
+    check(_lib_().hlm_swiglu_down_bwd(_ptr(gy), _ptr(w), _ptr(g), _ptr(out), gy.numel() // C, C, H,
+                                       _stream(dev)), "hlm_swiglu_down_bwd")
+    return out
+
+
+def _swiglu_down_bwd(ctx, grad_y):
+    h, gate_up, weight = ctx.saved_tensors
+    if grad_y is None:
+        return None, None, None
+    C, H = weight.shape
+    gy = grad_y.contiguous()
+    grad_gate_up = None
+    if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
+        grad_gate_up = swiglu_down_grad(gy, weight, gate_up)
+    grad_w = None
+    if ctx.needs_input_grad[2]:
+        grad_w = gy.reshape(-1, C).t() @ h.reshape(-1, H)
+    return None, grad_gate_up, grad_w
+
+
+swiglu_down.register_autograd(_swiglu_down_bwd, setup_context=_swiglu_down_setup)
 
 
 # ---------------------------------------------------------------------------

@@ -67,6 +67,7 @@ int hlm_device_error_clear(void* stream);
 #define HLM_DEVERR_TIMEOUT_DRAIN 5      /* teardown drain of in-flight TMA copies ran out */
 #define HLM_DEVERR_BAD_TMEM 6           /* tcgen05.alloc returned an unexpected address */
 #define HLM_DEVERR_SELFTEST_TIMEOUT 7   /* hlm_selftest_bounded_wait ran out, as it should */
+#define HLM_DEVERR_TIMEOUT_EPI_LOAD 8   /* an epilogue waited too long for its own TMA input load */
 
 /* Self-test of the bounded waits: one warp waits on an mbarrier that nothing
  * arrives at, with the same wait helper the GEMM roles use (scope 0: CTA-scope
@@ -98,7 +99,8 @@ uint64_t hlm_launch_count(void);
 #define HLM_KERNEL_QK_ROPE_BWD 14
 #define HLM_KERNEL_GEMM 15
 #define HLM_KERNEL_GATE_UP 16      /* gate_up GEMM + SwiGLU epilogue */
-#define HLM_KERNEL_MAX 17
+#define HLM_KERNEL_SWIGLU_DOWN_BWD 17 /* down grad_h GEMM + SwiGLU backward epilogue */
+#define HLM_KERNEL_MAX 18
 
 /* Start timing every launch of kernel `kernel_id`: launch i records
  * start_events[i] immediately before and stop_events[i] immediately after
@@ -281,6 +283,18 @@ int hlm_scale_by_device_scalar(void* data, const float* scale, int64_t n, int dt
  * Requires C % 64 == 0, H % 128 == 0, 16-byte aligned pointers. */
 int hlm_gate_up_swiglu_fwd(const void* x, const void* w_gate_up, void* gate_up_out, void* h_out,
                            int64_t M, int64_t C, int64_t H, void* stream);
+
+/* Backward through the down projection and the SwiGLU in one CTA-pair tcgen05
+ * GEMM: grad_h = grad_y @ W_down (rounded to bf16, the dtype of the reference's
+ * F.linear backward output, model.py:301-304), then the SwiGLU backward of
+ * _swiglu_backward (kernels.py:690-700) on the saved gate_up, written as
+ * grad_gate_up [M, 2H] bf16; grad_h itself never goes to memory.  grad_y
+ * [M, C], w_down [C, H] (the nn.Linear weight of the down projection),
+ * gate_up [M, 2H], all bf16 row-major.  Requires C % 64 == 0, H % 256 == 0,
+ * 16-byte aligned pointers.  (The down projection's weight gradient and the
+ * gate_up GEMM's input gradients are separate GEMMs.) */
+int hlm_swiglu_down_bwd(const void* grad_y, const void* w_down, const void* gate_up,
+                        void* grad_gate_up, int64_t M, int64_t C, int64_t H, void* stream);
 
 /* ------------------------------------------------------------------------
  * Plain tcgen05 GEMM (building block; also used by tests)

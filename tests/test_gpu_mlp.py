@@ -65,3 +65,63 @@ def test_gate_up_swiglu_rejects_cpu():
     x, w, _ = _operands(256, 128, 128)
     with pytest.raises(Exception):
         ops.gate_up_swiglu(x, w)
+
+
+@pytest.mark.parametrize("M,C,H", [(256, 256, 256), (300, 768, 512), (4096, 768, 2048), (1000, 128, 256)])
+def test_mlp_down_backward_fused_vs_oracle(M, C, H, cuda_device):
+    """gate_up_swiglu -> swiglu_down: forward y and the gradients of x, W_gate_up and W_down,
+    with the down projection's backward computing grad_h and the SwiGLU backward in one
+    kernel, against fp32 autograd of the same bf16 operands."""
+    from hackable_lm_b200 import _lib, ops
+
+    _lib.clear_device_error()
+    x, w, _ = _operands(M, C, H, seed=2)
+    g = torch.Generator().manual_seed(3)
+    wd = (torch.randn(C, H, generator=g) * 0.02).to(torch.bfloat16)
+    gy = torch.randn(M, C, generator=g).to(torch.bfloat16)
+    xd = x.to(cuda_device).requires_grad_(True)
+    wgd = w.to(cuda_device).requires_grad_(True)
+    wdd = wd.to(cuda_device).requires_grad_(True)
+    h, gate_up = ops.gate_up_swiglu(xd, wgd)
+    y = ops.swiglu_down(h, gate_up, wdd)
+    y.backward(gy.to(cuda_device))
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+
+    xr = x.float().requires_grad_(True)
+    wr = w.float().requires_grad_(True)
+    wdr = wd.float().requires_grad_(True)
+    gate, up = (xr @ wr.t()).chunk(2, dim=-1)
+    yr = (torch.nn.functional.silu(gate) * up) @ wdr.t()
+    yr.backward(gy.float())
+    assert_bf16_close(y, yr, what="y")
+    assert_bf16_close(xd.grad, xr.grad, what="grad_x")
+    assert_bf16_close(wgd.grad, wr.grad, what="grad_w_gate_up")
+    assert_bf16_close(wdd.grad, wdr.grad, what="grad_w_down")
+
+
+def test_swiglu_down_bwd_kernel_matches_unfused(cuda_device):
+    """The fused kernel's grad_gate_up equals the unfused composition (cuBLAS grad_h in bf16,
+    then the standalone SwiGLU backward kernel) up to the GEMM's accumulation order."""
+    from hackable_lm_b200 import _lib, ops
+
+    M, C, H = 2048, 768, 2048
+    g = torch.Generator().manual_seed(4)
+    gate_up = torch.randn(M, 2 * H, generator=g).to(torch.bfloat16).to(cuda_device)
+    wd = (torch.randn(C, H, generator=g) * 0.02).to(torch.bfloat16).to(cuda_device)
+    gy = torch.randn(M, C, generator=g).to(torch.bfloat16).to(cuda_device)
+    out = torch.empty_like(gate_up)
+    _lib.check(_lib.load().hlm_swiglu_down_bwd(gy.data_ptr(), wd.data_ptr(), gate_up.data_ptr(),
+                                                out.data_ptr(), M, C, H, 0), "hlm_swiglu_down_bwd")
+    ref = ops.swiglu_backward(gate_up, gy @ wd)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert_bf16_close(out, ref.float(), what="grad_gate_up")
+
+
+def test_swiglu_down_rejects_cpu():
+    from hackable_lm_b200 import ops
+
+    h = torch.zeros(4, 256, dtype=torch.bfloat16)
+    with pytest.raises(Exception):
+        ops.swiglu_down(h, torch.zeros(4, 512, dtype=torch.bfloat16), torch.zeros(64, 256, dtype=torch.bfloat16))
