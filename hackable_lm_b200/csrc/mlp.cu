@@ -20,7 +20,7 @@ namespace hlm {
 // (two per quadrant) with four stages at X [32768,768], W [4096,768].
 constexpr int kMlpStages = 5;
 constexpr int kMlpEpiWarps = 4;
-constexpr int kMlpBwdStages = 4;  // 4 x 32 KB stages + 96 KB of epilogue boxes
+constexpr int kMlpBwdStages = 5;  // 5 x 32 KB stages + 64 KB of epilogue boxes
 
 // Epilogue: per warp (32 rows) and 64-unit group: gate and up (2 x 64 fp32
 // columns from TMEM) rounded to bf16 and staged as two 32x64 boxes for the
@@ -102,13 +102,15 @@ struct EpiSwiGLU {
 //   grad_gate_up    = swiglu_backward(gate_up, grad_h)  (kernels.py:690-700,
 //                                                         same fp32 arithmetic as
 //                                                         swiglu_bwd_vec_kernel)
-// grad_h never goes to memory.  Epilogue (4 warps, one per TMEM lane
-// quadrant, 32 rows each; a 256-column tile is four 64-unit groups): per group
-// the warp's gate and up boxes (32 x 64 bf16 each) arrive by TMA into one of
-// two input buffers, each with its own mbarrier, the next group's boxes being
-// requested while this one is computed; dgate / dup are staged as two boxes
-// and written with TMA stores.  The buffers' barrier phases continue across
-// tiles through a per-warp use counter kept in shared memory.
+// grad_h never goes to memory.  Epilogue: 8 warps, two per TMEM lane quadrant
+// (32 rows each), each taking every other 64-unit group of the 256-column
+// tile.  Per group a warp's gate and up boxes (32 x 64 bf16 each) arrive by
+// TMA into the warp's 8 KB buffer (one mbarrier per warp), dgate / dup are
+// computed row by row and written back in place, and the same buffer goes out
+// with two TMA stores; the next group's load into it waits until those stores
+// have read it.  With two warps per scheduler one computes while the other
+// waits for its load.  The barrier phase continues across tiles through a
+// per-warp use counter kept in shared memory.
 struct EpiSwiGLUBwd {
   struct Params {
     alignas(64) CUtensorMap map_gu;   // gate_up [M][2H] bf16, box {64, 32}
@@ -116,59 +118,50 @@ struct EpiSwiGLUBwd {
     int H;
   };
   static constexpr int kBoxBytes = 32 * 128;
-  static constexpr int kWarpBytes = 6 * kBoxBytes;  // 2 input buffers x (gate, up) + (dgate, dup)
-  static constexpr int kBarOffset = 4 * kWarpBytes;
-  static constexpr int kCtrOffset = kBarOffset + 4 * 2 * 8;
+  static constexpr int kWarps = 8;
+  static constexpr int kWarpBytes = 2 * kBoxBytes;  // gate box, up box (outputs in place)
+  static constexpr int kBarOffset = kWarps * kWarpBytes;
+  static constexpr int kCtrOffset = kBarOffset + kWarps * 8;
   template <int EPI_WARPS>
   static constexpr int smem_bytes() {
-    static_assert(EPI_WARPS == 4, "one epilogue warp per lane quadrant");
-    return kCtrOffset + 4 * 4;
+    static_assert(EPI_WARPS == kWarps, "two epilogue warps per lane quadrant");
+    return kCtrOffset + kWarps * 4;
   }
   static HLM_DEVICE void init(uint8_t* smem) {
     const uint32_t b = smem_u32(smem);
-    for (int w = 0; w < 4; ++w) {
-      mbar_init(b + kBarOffset + 16 * w, 1);
-      mbar_init(b + kBarOffset + 16 * w + 8, 1);
+    for (int w = 0; w < kWarps; ++w) {
+      mbar_init(b + kBarOffset + 8 * w, 1);
       reinterpret_cast<volatile uint32_t*>(smem + kCtrOffset)[w] = 0u;
     }
   }
 
   template <int BN, int kParts>
   static HLM_DEVICE void run(const Params& ep, const GemmParams& p, uint8_t* smem, uint32_t taddr,
-                             int m_tile, int n_tile, int, int quad, int, int lane) {
-    static_assert(BN == 256 && kParts == 1, "four 64-unit groups per tile, one warp per quadrant");
+                             int m_tile, int n_tile, int, int quad, int part, int lane) {
+    static_assert(BN == 256 && kParts == 2, "two warps per quadrant, two 64-unit groups each");
     const int row0 = m_tile * kBM + quad * 32;
-    if (row0 >= p.M) return;  // no rows of this warp in the tile: no loads, barrier phases unchanged
+    if (row0 >= p.M) return;  // no rows of this warp in the tile: no loads, barrier phase unchanged
+    const int slot = part * 4 + quad;
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t in0 = sbase + static_cast<uint32_t>(quad * kWarpBytes);  // buffer b, tensor t: + (2b + t) boxes
-    const uint32_t outb = in0 + 4u * kBoxBytes;                               // dgate, then dup
-    const uint32_t bar0 = sbase + static_cast<uint32_t>(kBarOffset + 16 * quad);
-    volatile uint32_t* ctr = reinterpret_cast<volatile uint32_t*>(smem + kCtrOffset) + quad;
+    const uint32_t gate_box = sbase + static_cast<uint32_t>(slot * kWarpBytes);
+    const uint32_t up_box = gate_box + kBoxBytes;
+    const uint32_t bar = sbase + static_cast<uint32_t>(kBarOffset + 8 * slot);
+    volatile uint32_t* ctr = reinterpret_cast<volatile uint32_t*>(smem + kCtrOffset) + slot;
     const int h0 = n_tile * BN;  // hidden unit of the tile's first column
     uint32_t n = 0;
     if (lane == 0) n = *ctr;
     n = __shfl_sync(0xffffffffu, n, 0);
-    auto request = [&](int g) {  // lane 0: group g's gate and up boxes into buffer g & 1
-      const uint32_t b = static_cast<uint32_t>(g & 1);
-      const uint32_t bar = bar0 + 8u * b;
-      mbar_arrive_expect_tx(bar, 2 * kBoxBytes);
-      tma_load_2d(in0 + (2u * b) * kBoxBytes, &ep.map_gu, h0 + g * 64, row0, bar);
-      tma_load_2d(in0 + (2u * b + 1u) * kBoxBytes, &ep.map_gu, ep.H + h0 + g * 64, row0, bar);
-    };
-    if (lane == 0) request(0);
+    uint32_t used = 0;
 #pragma unroll 1
-    for (int g = 0; g < BN / 64; ++g) {
-      // buffer (g + 1) & 1 was last read by group g - 1 (or the previous tile's
-      // last group), whose reads completed before the warp's last __syncwarp
-      if (lane == 0 && g + 1 < BN / 64) request(g + 1);
-      const uint32_t b = static_cast<uint32_t>(g & 1);
-      const uint32_t par = ((n + static_cast<uint32_t>(g)) >> 1) & 1u;
-      if (!warp_wait(bar0 + 8u * b, par, p.err, kDevErrTimeoutEpiLoad, lane)) return;
-      // the stores that last read the output boxes must be done with them
-      if (lane == 0) bulk_wait_group_read<0>();
-      __syncwarp();
-      const uint32_t gate_box = in0 + (2u * b) * kBoxBytes;
-      const uint32_t up_box = gate_box + kBoxBytes;
+    for (int g = part; g < BN / 64; g += kParts, ++used) {
+      if (lane == 0) {
+        // the stores that last read this buffer must be done with it
+        bulk_wait_group_read<0>();
+        mbar_arrive_expect_tx(bar, 2 * kBoxBytes);
+        tma_load_2d(gate_box, &ep.map_gu, h0 + g * 64, row0, bar);
+        tma_load_2d(up_box, &ep.map_gu, ep.H + h0 + g * 64, row0, bar);
+      }
+      if (!warp_wait(bar, (n + used) & 1u, p.err, kDevErrTimeoutEpiLoad, lane)) return;
 #pragma unroll 1
       for (int hs = 0; hs < 2; ++hs) {
         uint32_t d[32];
@@ -202,19 +195,20 @@ struct EpiSwiGLUBwd {
             og[j] = pack_bf16x2(rg[0], rg[1]);
             ou[j] = pack_bf16x2(ru[0], ru[1]);
           }
-          st_shared_v4(outb + off, make_uint4(og[0], og[1], og[2], og[3]));
-          st_shared_v4(outb + kBoxBytes + off, make_uint4(ou[0], ou[1], ou[2], ou[3]));
+          // in place: each thread rewrites only the chunks of its own row it just read
+          st_shared_v4(gate_box + off, make_uint4(og[0], og[1], og[2], og[3]));
+          st_shared_v4(up_box + off, make_uint4(ou[0], ou[1], ou[2], ou[3]));
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_2d(&ep.map_out, h0 + g * 64, row0, outb);
-        tma_store_2d(&ep.map_out, ep.H + h0 + g * 64, row0, outb + kBoxBytes);
+        tma_store_2d(&ep.map_out, h0 + g * 64, row0, gate_box);
+        tma_store_2d(&ep.map_out, ep.H + h0 + g * 64, row0, up_box);
         bulk_commit_group();
       }
     }
-    if (lane == 0) *ctr = n + static_cast<uint32_t>(BN / 64);
+    if (lane == 0) *ctr = n + used;
   }
 };
 
@@ -275,6 +269,6 @@ extern "C" int hlm_swiglu_down_bwd(const void* grad_y, const void* w_down, const
   gemm_tiling_pair(p, static_cast<int>(M), static_cast<int>(H), static_cast<int>(C), 256, 1);
   p.err = device_error_ptr();
   if (p.err == nullptr) return HLM_ERR_LAUNCH;
-  return launch_gemm_pair<256, kMlpBwdStages, false, true, EpiSwiGLUBwd, 4>(
+  return launch_gemm_pair<256, kMlpBwdStages, false, true, EpiSwiGLUBwd, EpiSwiGLUBwd::kWarps>(
       ma, ma, ma, mb, p, ep, static_cast<cudaStream_t>(stream), HLM_KERNEL_SWIGLU_DOWN_BWD);
 }
