@@ -66,6 +66,18 @@ def test_invalid_arguments_are_rejected_before_any_launch(lib):
     assert lib.hlm_swiglu_fwd(ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 4, 7, None) == -2
     # fused QKV only supports head_dim 128
     assert lib.hlm_qkv_rope_fwd(*([None] * 8), 1, 8, 64, 1, 1, 64, 32, 32, 1, 1e-6, None) == -2
+    # fused gate_up / down-backward GEMMs: bad sizes, null pointers, unsupported widths
+    V16 = ctypes.c_void_p(16)
+    assert lib.hlm_gate_up_swiglu_fwd(None, None, None, None, -1, 64, 128, None) == -1
+    assert lib.hlm_gate_up_swiglu_fwd(None, None, None, None, 256, 64, 128, None) == -1
+    assert lib.hlm_gate_up_swiglu_fwd(V16, V16, V16, V16, 256, 96, 128, None) == -2   # C % 64
+    assert lib.hlm_gate_up_swiglu_fwd(V16, V16, V16, V16, 256, 64, 96, None) == -2    # H % 128
+    assert lib.hlm_gate_up_swiglu_fwd(None, None, None, None, 0, 64, 128, None) == 0  # empty
+    assert lib.hlm_swiglu_down_bwd(None, None, None, None, -1, 64, 256, None) == -1
+    assert lib.hlm_swiglu_down_bwd(None, None, None, None, 256, 64, 256, None) == -1
+    assert lib.hlm_swiglu_down_bwd(V16, V16, V16, V16, 256, 64, 128, None) == -2      # H % 256
+    assert lib.hlm_swiglu_down_bwd(V16, V16, V16, V16, 256, 100, 256, None) == -2     # C % 64
+    assert lib.hlm_swiglu_down_bwd(None, None, None, None, 0, 64, 256, None) == 0     # empty
     # bounded-wait self-test: limit outside 1 us .. 1 s, or an unknown scope
     assert lib.hlm_selftest_bounded_wait(0, 0, None) == -1
     assert lib.hlm_selftest_bounded_wait(2_000_000, 0, None) == -1
