@@ -11,6 +11,7 @@ then compare the CUDA kernels against the pinned oracle.  Inputs are seeded
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -181,7 +182,9 @@ def make_lm_head(kernels, model, config):
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference", help="path of the hackable-lm checkout")
+    ap.add_argument("--reference", default=os.environ.get("HACKABLE_LM_REFERENCE"),
+                    required="HACKABLE_LM_REFERENCE" not in os.environ,
+                    help="path of the hackable-lm checkout (default: $HACKABLE_LM_REFERENCE)")
     ap.add_argument("--out", default=str(HERE))
     args = ap.parse_args()
     sys.dont_write_bytecode = True
