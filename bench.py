@@ -258,6 +258,24 @@ def bench_lm_head(args, d: Dist, device) -> dict:
         timers[k].__exit__(None, None, None)
     launches = _lib.launch_count() - n0
     clk = clocks.stop()
+    # per-phase breakdown of the first timed step (this rank): micro-steps, the exposed
+    # part of the gradient all-reduce (the last micro-step waits for DDP's final
+    # buckets), gradient clipping and the optimizer step
+    prev, micro = start, []
+    phases = {}
+    for tag, ev in phase_events:
+        ms = prev.elapsed_time(ev)
+        if tag == "micro":
+            micro.append(ms)
+        else:
+            phases[tag] = ms
+        prev = ev
+    plain = micro[:-1] if len(micro) > 1 else micro
+    step_phases = {"micro_step_ms": round(statistics.mean(plain), 3),
+                   "last_micro_step_ms": round(micro[-1], 3),
+                   "exposed_allreduce_ms": round(micro[-1] - statistics.mean(plain), 3) if d.world > 1 else 0.0,
+                   "clip_ms": round(phases.get("clip", 0.0), 3), "optimizer_ms": round(phases.get("opt", 0.0), 3),
+                   "note": "first timed step on rank 0; the optimizer's Muon work is sharded over the ranks"}
     ms_per_step = total_ms / args.steps
     value = M * d.world / (ms_per_step / 1e3)
 
@@ -345,9 +363,10 @@ D12_KERNELS = {"lm_logits": 1, "lm_dlogits": 1, "lm_dx": 1, "lm_dw": 1, "gate_up
                "rmsnorm_fwd": 25, "rmsnorm_bwd": 25}
 
 
-def d12_config(world: int, accum: int) -> dict:
+def d12_config(world: int, accum: int, max_grad_norm: float = 1.0) -> dict:
     return {"workload": "d12 DP training step: depth 12, C=768, 6x128 heads, SwiGLU 2048, vocab 32768, "
-                        "seq 2048, micro-batch 16/GPU, global batch 2^20 tokens, Muon+AdamW step",
+                        "seq 2048, micro-batch 16/GPU, global batch 2^20 tokens, global grad-norm clip "
+                        f"{max_grad_norm}, Muon+AdamW step",
             "model": "hackable-lm d12 (random init)", "global_batch": 2**20, "seq_len": 2048,
             "micro_batch_per_gpu": 16, "grad_accum_per_rank": accum,
             "parallelism": f"dp{world}" + (" (DDP, bf16 25 MB buckets, NCCL)" if world > 1 else ""),
@@ -361,14 +380,26 @@ def bench_d12(args, d: Dist, device) -> dict:
 
     peaks, peak_src = load_peaks()
     s = tr.build(device, world=d.world)
-    batches = tr.synthetic_batches(4, s.micro_batch, s.seq_len, s.config.vocab_size, d.rank, device)
+    # fresh data: one distinct micro-batch for every micro-step of the run (warm-up, timed
+    # steps and the end-to-end pass), cycling only beyond 1024 micro-batches (268 MB)
+    n_micro = min(1024, s.accum * (args.warmup + 2 * args.steps + 1))
+    batches = tr.synthetic_batches(n_micro, s.micro_batch, s.seq_len, s.config.vocab_size, d.rank, device)
     tokens_per_step = s.accum * s.micro_batch * s.seq_len * d.world
+    cursor = [0]
 
-    def step():
-        return tr.train_step(s, batches)
+    def next_batch(i):
+        b = batches[cursor[0] % len(batches)]
+        cursor[0] += 1
+        return b
 
-    for _ in range(args.warmup):
-        step()
+    def step(mark=None):
+        return tr.train_step(s, batches, fetch=next_batch, max_grad_norm=args.max_grad_norm, mark=mark)
+
+    first_loss = None
+    for i in range(args.warmup):
+        l = step()
+        if i == 0:
+            first_loss = float(l.float().item())
     torch.cuda.synchronize()
     # per-kernel timing of the library's own launches during the first timed step
     # capacity: up to two launches per operator call (LM dlogits / grad_hidden run in row halves)
@@ -381,13 +412,20 @@ def bench_d12(args, d: Dist, device) -> dict:
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
     first = torch.cuda.Event(enable_timing=True)
+    phase_events: list[tuple[str, torch.cuda.Event]] = []
+
+    def mark(tag):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        phase_events.append((tag, ev))
+
     start.record()
     torch.cuda.nvtx.range_push("timed")  # ncu --nvtx --nvtx-include "timed/" selects these launches
     for i in range(args.steps):
         if i == 0:
             for t in timers.values():
                 t.__enter__()
-        loss = step()
+        loss = step(mark if i == 0 else None)
         if i == 0:
             for t in timers.values():
                 t.__exit__(None, None, None)
@@ -401,6 +439,24 @@ def bench_d12(args, d: Dist, device) -> dict:
     step0_ms = start.elapsed_time(first)
     launches = _lib.launch_count() - n0
     clk = clocks.stop()
+    # per-phase breakdown of the first timed step (this rank): micro-steps, the exposed
+    # part of the gradient all-reduce (the last micro-step waits for DDP's final
+    # buckets), gradient clipping and the optimizer step
+    prev, micro = start, []
+    phases = {}
+    for tag, ev in phase_events:
+        ms = prev.elapsed_time(ev)
+        if tag == "micro":
+            micro.append(ms)
+        else:
+            phases[tag] = ms
+        prev = ev
+    plain = micro[:-1] if len(micro) > 1 else micro
+    step_phases = {"micro_step_ms": round(statistics.mean(plain), 3),
+                   "last_micro_step_ms": round(micro[-1], 3),
+                   "exposed_allreduce_ms": round(micro[-1] - statistics.mean(plain), 3) if d.world > 1 else 0.0,
+                   "clip_ms": round(phases.get("clip", 0.0), 3), "optimizer_ms": round(phases.get("opt", 0.0), 3),
+                   "note": "first timed step on rank 0; the optimizer's Muon work is sharded over the ranks"}
     ms_per_step = total_ms / args.steps
     value = tokens_per_step / (ms_per_step / 1e3)
 
@@ -463,13 +519,14 @@ def bench_d12(args, d: Dist, device) -> dict:
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
 
     def fetch(i):
-        hx, hy = host[i % len(host)]
+        hx, hy = host[cursor[0] % len(host)]
+        cursor[0] += 1
         xd.copy_(hx, non_blocking=True)
         yd.copy_(hy, non_blocking=True)
         return xd, yd
 
     def e2e_step():
-        l = tr.train_step(s, batches, fetch=fetch)
+        l = tr.train_step(s, batches, fetch=fetch, max_grad_norm=args.max_grad_norm)
         loss_host.copy_(l.float(), non_blocking=True)
 
     e2e_ms = cuda_time(e2e_step, args.steps, 1, d, label="e2e") / args.steps
@@ -482,9 +539,12 @@ def bench_d12(args, d: Dist, device) -> dict:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: uniform token ids (seeded per rank), targets = ids shifted by one",
-        "config": d12_config(d.world, s.accum), "roofline": roofline, "kernel_breakdown": breakdown,
+        "config": d12_config(d.world, s.accum, args.max_grad_norm), "roofline": roofline, "kernel_breakdown": breakdown,
         "mfu": round(mfu, 4), "mfu_basis": f"{D12_FLOPS_PER_TOKEN} FLOP/token / measured bf16 burst peak",
-        "loss": float(loss.float().item()), "e2e": e2e, "gpu_launches": launches,
+        "loss_first_step": first_loss, "loss": float(loss.float().item()),
+        "loss_note": f"mean micro-batch loss of the first warm-up step and of the last timed step; "
+                     f"{n_micro} distinct micro-batches over the run; random-init loss is ln(32768) = 10.40",
+        "step_phases": step_phases, "e2e": e2e, "gpu_launches": launches,
         "gpu_launches_per_step": launches / args.steps, "clocks": clk,
     }
 
@@ -506,8 +566,9 @@ def cpu_baseline_d12(reps: int = 2) -> dict:
     times = [d12_cpu_sample() for _ in range(reps)]
     med = statistics.median(times)
     return {"value": 2048 / med, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"oracle d12 model (torch CPU fp32) forward+backward on 1x2048 tokens, median of {reps} "
-                      f"({med:.2f} s each); the optimizer step is excluded"}
+            "sample": f"port: oracle d12 model (torch CPU fp32, a restatement of the reference LanguageModel) "
+                      f"forward+backward on 1x2048 tokens, median of {reps} ({med:.2f} s each); the optimizer "
+                      f"step is excluded"}
 
 
 # ---------------------------------------------------------------------------
@@ -658,8 +719,10 @@ def run_reference(args, d: Dist) -> dict | None:
         times = [d12_cpu_sample() for _ in range(args.steps)]
         total = sum(times)
         value = 2048 * args.steps / total
-        sample = ("oracle d12 model (torch CPU fp32) forward+backward, 1x2048 tokens per step of the "
-                  "2^20-token global batch; optimizer step excluded")
+        sample = ("port: oracle d12 model (torch CPU fp32; a restatement of the reference LanguageModel, "
+                  "which does not travel to the GPU box; the package's torch formulation equals the "
+                  "reference model on its golden fixture to 1e-5) forward+backward, 1x2048 tokens per "
+                  "step of the 2^20-token global batch; optimizer step excluded")
         metric = "d12 step tok/s"
         cfg = d12_config(1, 32)
     ms = total / args.steps * 1e3
@@ -696,6 +759,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--workload", choices=("lm_head", "d12"), default="d12")
+    ap.add_argument("--max-grad-norm", type=float, default=1.0,
+                    help="global gradient-norm clip in the d12 step (the reference's --max-grad-norm; "
+                         "its default 0 skips the clip, this bench includes it so the step does all of "
+                         "the reference's per-step work)")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-operator section")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-tokens", type=int, default=1024, help="tokens per reference-arm step")

@@ -740,10 +740,14 @@ constexpr int kNoAllocPartials = kRmsBwdMaxBlocks * kRmsBwdWarps;
 
 static __device__ __align__(256) float g_noalloc_rms_partial[kNoAllocPartials * kNoAllocMaxCols];
 
-// Device address of g_noalloc_rms_partial, looked up once per device with that
-// device current.  The host-side symbol is only a stand-in and must never be
-// handed to a kernel.
-static float* noalloc_partial_ptr(int* rc) {
+// Device address of g_noalloc_rms_partial on the current device.  The
+// host-side symbol is only a stand-in and must never be handed to a kernel.
+// Outside stream capture the address is looked up again on every call (with
+// the device current), so a context re-created after cudaDeviceReset gets the
+// new address; inside a capture the lookup (which may load the module) is not
+// allowed, so the address cached by an earlier uncaptured call on this device
+// is used, and without one the call is refused with HLM_ERR_UNSUPPORTED.
+static float* noalloc_partial_ptr(cudaStream_t stream, int* rc) {
   static float* ptrs[64] = {nullptr};
   static std::mutex mu;
   int dev = 0;
@@ -751,14 +755,22 @@ static float* noalloc_partial_ptr(int* rc) {
     *rc = HLM_ERR_LAUNCH;
     return nullptr;
   }
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess) {
+    *rc = HLM_ERR_LAUNCH;
+    return nullptr;
+  }
   std::lock_guard<std::mutex> lock(mu);
-  if (ptrs[dev] == nullptr) {
+  if (capture == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_rms_partial) != cudaSuccess || p == nullptr) {
       *rc = HLM_ERR_LAUNCH;
       return nullptr;
     }
     ptrs[dev] = static_cast<float*>(p);
+  } else if (ptrs[dev] == nullptr) {
+    *rc = HLM_ERR_UNSUPPORTED;  // first call on this device made inside a stream capture
+    return nullptr;
   }
   *rc = HLM_OK;
   return ptrs[dev];
@@ -777,10 +789,10 @@ extern "C" int hlm_residual_rms_norm_bwd_noalloc(const void* x, const void* weig
   if (cols == 0) return HLM_OK;
   if (rows > 0 && (x == nullptr || grad_norm == nullptr || grad_in == nullptr))
     return HLM_ERR_INVALID_ARG;
-  int rc = HLM_OK;
-  float* partial = noalloc_partial_ptr(&rc);
-  if (partial == nullptr) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = HLM_OK;
+  float* partial = noalloc_partial_ptr(s, &rc);
+  if (partial == nullptr) return rc;
   const int threads = kRmsBwdThreads;
   const int grid = rms_bwd_weight_blocks(rows);  // <= kRmsBwdMaxBlocks
   HLM_DISPATCH_DTYPE(dtype, T, {

@@ -59,7 +59,9 @@ class KernelInfo:
 
 
 def _cuda_only(t: torch.Tensor, what: str) -> None:
-    if not t.is_cuda:
+    # meta tensors carry shapes only: they reach the operators' fake
+    # implementations (shape propagation, meta-device model construction), never a kernel
+    if not (t.is_cuda or t.is_meta):
         raise RuntimeError(
             f"{what}: the hackable_lm_b200 path runs only on CUDA (sm_100a) tensors; "
             "use the 'torch' module backend for CPU runs"
@@ -248,25 +250,88 @@ def fused_linear_cross_entropy_with_weight(hidden: torch.Tensor, weight: torch.T
     return _B200FusedLinearCrossEntropy.apply(hidden_flat, weight, targets_flat, ignore_index, chunk_size)
 
 
+@dataclass(frozen=True)
+class WindowBlockMask:
+    """What ``flex_attention_block_mask`` returns on this path: the causal
+    (optionally sliding-window) pattern the reference encodes in a FlexAttention
+    BlockMask (kernels.py:850-869), kept as its two parameters so that the
+    attention core can run it on SDPA."""
+
+    seq_len: int
+    window_size: int | None
+
+
+def flex_attention_block_mask(batch_size: int, n_head: int, seq_len: int, device: torch.device,
+                              window_size: int | None = None) -> WindowBlockMask:
+    """Reference signature (kernels.py:850-856): causal mask, plus
+    ``q - kv < window_size`` when a window is given."""
+    del batch_size, n_head, device
+    return WindowBlockMask(int(seq_len), None if window_size is None else int(window_size))
+
+
+def _sdpa_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dropout_p: float, is_causal: bool,
+               attn_mask: torch.Tensor | None, window_size: int | None) -> torch.Tensor:
+    """torch SDPA on [B, H, T, D]; a sliding window becomes the boolean mask
+    ``0 <= q - kv < window`` (the FlashAttention window ``(window - 1, 0)`` of
+    kernels.py:839 and the reference's own mask, model.py:143-153)."""
+    if window_size is not None and attn_mask is None:
+        T = q.shape[-2]
+        pos = torch.arange(T, device=q.device)
+        dist = pos[:, None] - pos[None, :]
+        attn_mask = (dist >= 0) & (dist < window_size)
+        is_causal = False
+    return F.scaled_dot_product_attention(q, k, v, attn_mask=attn_mask, dropout_p=dropout_p,
+                                          is_causal=is_causal and attn_mask is None,
+                                          enable_gqa=q.shape[1] != k.shape[1])
+
+
+_FLASH_BACKENDS = ("flash_attn_2", "flash_attn_3", "flash_attn_4")
+
+
 def scaled_dot_product_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dropout_p: float,
                                  is_causal: bool = True, attn_mask: torch.Tensor | None = None,
-                                 window_size: int | None = None, backend: str = "sdpa") -> torch.Tensor:
-    """Attention core on [B, H, T, D] tensors.
+                                 block_mask: Any | None = None, window_size: int | None = None,
+                                 backend: str = "flash_attn_2") -> torch.Tensor:
+    """Attention core with the reference's signature and backend names (kernels.py:774-847).
 
-    ``"sdpa"`` uses torch.nn.functional.scaled_dot_product_attention (the
-    attention core named by the benchmark configuration); ``"torch"`` is the
-    reference's explicit softmax formulation (kernels.py:785-800).
+    Layouts follow the reference: ``"torch"``, ``"sdpa"`` and
+    ``"flex_attention"`` take and return [B, H, T, D]; the FlashAttention
+    names take and return [B, T, H, D] (the reference's ``fwd_flash_attn_*``
+    pass q, k, v without transposing, model.py:213-251).  Every name except
+    ``"torch"`` runs torch SDPA (the attention core named by the benchmark
+    configuration), so the reference's ``AttentionCore`` runs unmodified on
+    this module.  ``"torch"`` is the reference's explicit softmax
+    (kernels.py:785-800).  The argument checks are the reference's: the
+    FlashAttention names reject an explicit mask and (but for flash_attn_2)
+    dropout, flex_attention rejects dropout.
     """
     if backend == "sdpa":
+        return _sdpa_core(q, k, v, dropout_p, is_causal, attn_mask, window_size)
+    if backend in _FLASH_BACKENDS:
+        if attn_mask is not None:
+            raise RuntimeError(f"{backend} path expects window_size instead of an explicit attention mask")
+        if dropout_p and backend != "flash_attn_2":
+            raise RuntimeError(f"{backend} backend does not support dropout")
+        q, k, v = (t.bfloat16().transpose(1, 2) for t in (q, k, v))
+        return _sdpa_core(q, k, v, dropout_p, is_causal, None, window_size).transpose(1, 2)
+    if backend == "flex_attention":
+        if dropout_p:
+            raise RuntimeError("flex_attention backend does not support dropout")
+        if block_mask is not None:
+            if not isinstance(block_mask, WindowBlockMask):
+                raise RuntimeError("flex_attention on this path takes the mask made by "
+                                   "flex_attention_block_mask (causal, optional sliding window)")
+            if block_mask.seq_len != q.shape[-2]:
+                raise RuntimeError(f"block mask is for seq_len {block_mask.seq_len}, got {q.shape[-2]}")
+            window_size = block_mask.window_size
+        return _sdpa_core(q, k, v, 0.0, True, None, window_size)
+    if backend == "torch":
         if window_size is not None and attn_mask is None:
-            T = q.shape[-2]
-            pos = torch.arange(T, device=q.device)
+            # the reference's caller passes its window as attn_mask (model.py:185-194);
+            # a caller that passes only window_size gets the same mask
+            pos = torch.arange(q.shape[-2], device=q.device)
             dist = pos[:, None] - pos[None, :]
             attn_mask = (dist >= 0) & (dist < window_size)
-            is_causal = False
-        return F.scaled_dot_product_attention(q, k, v, attn_mask=attn_mask, dropout_p=dropout_p,
-                                              is_causal=is_causal and attn_mask is None)
-    if backend == "torch":
         scale = 1.0 / math.sqrt(q.shape[-1])
         attn = torch.matmul(q, k.transpose(-2, -1)) * scale
         if is_causal:

@@ -6,7 +6,8 @@ bf16 (bf16 parameters and gradients), DistributedDataParallel with 25 MB
 bf16 gradient buckets over NCCL, gradient accumulation with ``no_sync`` on all
 but the last micro-step so the global batch is preserved
 (grad_accum = global_tokens / (micro_batch * seq_len * world)), then the
-Muon/AdamW optimizer step on every rank.  Data is synthetic (uniform token
+Muon/AdamW optimizer step (Muon's Newton-Schulz work sharded across the ranks,
+then one all-gather of the updated matrices).  Data is synthetic (uniform token
 ids; targets are the ids shifted by one), so the data loader is not part of
 the step.
 """
@@ -81,12 +82,18 @@ def synthetic_batches(n: int, micro_batch: int, seq_len: int, vocab: int, rank: 
     return out
 
 
-def train_step(s: StepSetup, batches, fetch=None, optimizer_step: bool = True) -> torch.Tensor:
+def train_step(s: StepSetup, batches, fetch=None, optimizer_step: bool = True, max_grad_norm: float = 0.0,
+               mark=None) -> torch.Tensor:
     """One optimizer step over s.accum micro-batches; returns the mean loss (device tensor).
 
     ``fetch(i)`` may supply micro-batch i (e.g. copied from host memory);
     otherwise batches are cycled from the resident list.  With
     ``optimizer_step=False`` the averaged gradients are left in ``.grad``.
+    ``max_grad_norm > 0`` clips the global gradient norm before the optimizer
+    step, as the reference's ``--max-grad-norm`` does (train.py:1004-1005; its
+    default, 0, skips it).  ``mark(tag)``, when given, is called after each
+    micro-step ("micro"), after clipping ("clip") and after the optimizer step
+    ("opt"), so a caller can record CUDA events for a per-phase breakdown.
     """
     s.optimizer.zero_grad()
     total = None
@@ -98,8 +105,16 @@ def train_step(s: StepSetup, batches, fetch=None, optimizer_step: bool = True) -
             _, loss = s.train_model(x, y)
             (loss / s.accum).backward()
         total = loss.detach() if total is None else total + loss.detach()
+        if mark is not None:
+            mark("micro")
+    if max_grad_norm > 0:
+        torch.nn.utils.clip_grad_norm_(s.optimizer.parameters(), max_grad_norm, foreach=True)
+    if mark is not None:
+        mark("clip")
     if optimizer_step:
         s.optimizer.step()
+    if mark is not None:
+        mark("opt")
     return total / s.accum
 
 

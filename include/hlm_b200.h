@@ -167,8 +167,12 @@ size_t hlm_rms_norm_bwd_workspace_bytes(int64_t rows, int64_t cols);
  *   - Scratch (the dweight partial sums) lives in a fixed 4 MiB array inside
  *     the library, held on every GPU that loads it until the process exits.
  *   - cols must be <= HLM_NOALLOC_RMS_MAX_COLS, else HLM_ERR_UNSUPPORTED.
- *   - The first call on each device looks up the array's device address; make
- *     that first call outside any stream capture.
+ *   - Each call made outside stream capture looks up the array's device
+ *     address on the current device (so a context re-created after
+ *     cudaDeviceReset is handled); a call inside a capture reuses the address
+ *     of an earlier uncaptured call on that device, and is refused with
+ *     HLM_ERR_UNSUPPORTED when there was none: make the first call on each
+ *     device outside any stream capture.
  *   - Calls share the array: calls that overlap on the GPU (different streams,
  *     different threads) race and must be serialised by the caller.
  *   - Allocates nothing: no cudaMalloc, cudaFree or allocating library call.

@@ -43,3 +43,16 @@ def cuda_device():
 
     _lib.load()
     return torch.device("cuda", 0)
+
+
+def reference_checkout():
+    """A hackable-lm checkout: $HACKABLE_LM_REFERENCE, else a directory named
+    ``reference`` or ``hackable-lm`` beside this repository; None without one.
+    Only CPU tests read it (the GPU tests use the committed golden fixtures)."""
+    import os
+
+    cands = [os.environ.get("HACKABLE_LM_REFERENCE")] + [str(ROOT.parent / n) for n in ("reference", "hackable-lm")]
+    for c in cands:
+        if c and (Path(c) / "model.py").is_file() and (Path(c) / "kernels.py").is_file():
+            return Path(c)
+    return None

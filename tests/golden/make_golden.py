@@ -6,7 +6,10 @@ model.py imported from a checkout of the reference repository).
 
 The fixtures pin the CPU oracle (oracle/hotpath.py); the GPU parity tests
 then compare the CUDA kernels against the pinned oracle.  Inputs are seeded
-(torch.Generator().manual_seed(0)) and generated on the CPU in fp32.
+(torch.Generator().manual_seed(0)) and generated on the CPU in fp32; the
+fixtures whose GPU tests feed bf16 inputs (qkv, lm_head, the model cases) hold
+bf16-representable values.  The model cases (model_d4_window, model_d12) run
+the reference's whole LanguageModel.
 """
 from __future__ import annotations
 
@@ -26,6 +29,12 @@ def gen(seed: int = 0) -> torch.Generator:
 
 def randn(g, *shape, std=1.0, mean=0.0):
     return torch.randn(*shape, generator=g) * std + mean
+
+
+def bf16_values(t: torch.Tensor) -> torch.Tensor:
+    """fp32 tensor holding bf16-representable values: the fixtures whose GPU tests feed
+    bf16 inputs use them, so both sides start from identical numbers."""
+    return t.to(torch.bfloat16).to(torch.float32)
 
 
 def fingerprint(t: torch.Tensor) -> torch.Tensor:
@@ -133,12 +142,12 @@ def make_qkv(model, config):
     mod = model.QKVProjection(cfg, 0)
     g = gen(0)
     with torch.no_grad():
-        mod.qkv_proj.weight.copy_(randn(g, *mod.qkv_proj.weight.shape, std=0.02))
-    x = randn(g, 2, 16, 256)
+        mod.qkv_proj.weight.copy_(bf16_values(randn(g, *mod.qkv_proj.weight.shape, std=0.02)))
+    x = bf16_values(randn(g, 2, 16, 256))
     xr = x.clone().requires_grad_(True)
     q, k, v = mod.fwd_torch(xr)  # model.py:101-115
     g2 = gen(3)
-    dq, dk, dv = randn(g2, *q.shape), randn(g2, *k.shape), randn(g2, *v.shape)
+    dq, dk, dv = (bf16_values(randn(g2, *t.shape)) for t in (q, k, v))
     ((q * dq).sum() + (k * dk).sum() + (v * dv).sum()).backward()
     cos, sin = mod.rope(16, torch.device("cpu"), torch.float32)
     return {"x": x, "w_qkv": mod.qkv_proj.weight.detach().clone(), "cos": cos.clone(), "sin": sin.clone(),
@@ -167,8 +176,8 @@ def make_lm_head(kernels, model, config):
     # dense CPU branch of fused_linear_cross_entropy_with_weight (kernels.py:955-957) with some
     # targets set to F.cross_entropy's ignore_index: mean over the non-ignored rows.
     g = gen(1)
-    w = randn(g, 96, 64, std=0.02)
-    hidden = randn(g, 40, 64)
+    w = bf16_values(randn(g, 96, 64, std=0.02))
+    hidden = bf16_values(randn(g, 40, 64))
     targets = torch.randint(0, 96, (40,), generator=g)
     targets[torch.randperm(40, generator=g)[:5]] = -100
     hr = hidden.clone().requires_grad_(True)
@@ -180,12 +189,62 @@ def make_lm_head(kernels, model, config):
     return out
 
 
+MODEL_CASES = {
+    # depth 4 with sliding windows (layers 0-2 windowed, layer 3 full: every fourth
+    # and the last layer attend to the whole sequence, config.py:184-191)
+    "model_d4_window": dict(depth=4, vocab=4096, seq=256, batch=2, window=64, seed=0, rows=16),
+    # BASELINE config 5's model: depth 12, vocab 32768, seq 2048, full causal
+    "model_d12": dict(depth=12, vocab=32768, seq=2048, batch=1, window=None, seed=0, rows=6),
+}
+
+
+def make_model(model, config, *, depth, vocab, seq, batch, window, seed, rows):
+    """The reference LanguageModel (model.py:355-391) built by the reference's own
+    resolve_config (config.py:289-488), seeded GPT-style init, then every weight
+    rounded to bf16 (the B200 model trains in bf16, kernels.py:962-972) and one
+    forward + backward on the CPU in fp32 with the torch backends.
+
+    Stored: the init fingerprints (before rounding; a test re-creating the weights
+    from the same seed checks them), the token ids, the loss, every parameter's
+    gradient norm and a seeded subset of gradient rows per parameter (for the token
+    embedding, rows of ids present in the batch)."""
+    resolved = config.resolve_config(depth=depth, vocab_size=vocab, sequence_len=seq, device_batch_size=batch,
+                                     attention_window=window, attention_backend="torch", qkv_backend="torch",
+                                     gate_up_backend="torch", lm_head_backend="torch")
+    cfg = resolved.model
+    torch.manual_seed(seed)
+    m = model.LanguageModel(cfg)
+    fps = {n: fingerprint(p) for n, p in m.named_parameters()}
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(bf16_values(p))
+    ids = torch.randint(0, vocab, (batch, seq + 1), generator=gen(seed + 1))
+    x, y = ids[:, :-1], ids[:, 1:]
+    _, loss = m(x, y)
+    loss.backward()
+    used = torch.unique(x)
+    grad_norms, grad_rows = {}, {}
+    for i, (n, p) in enumerate(m.named_parameters()):
+        grad = p.grad.detach()
+        grad_norms[n] = grad.double().norm()
+        pool = used if n == "tok_emb.weight" else torch.arange(p.shape[0])
+        pick = pool[torch.randperm(pool.numel(), generator=gen(100 + i))[:rows]]
+        grad_rows[n] = (pick.clone(), grad[pick].clone())
+    return {"config": dict(depth=depth, vocab=vocab, seq=seq, batch=batch, window=window,
+                           attention_full_every=cfg.attention_full_every, n_embd=cfg.n_embd,
+                           n_head=cfg.n_head, mlp_hidden=cfg.mlp_hidden, rope_theta=cfg.rope_theta,
+                           rope_fraction=cfg.rope_fraction, loss_chunk_size=cfg.loss_chunk_size),
+            "seed": seed, "init_fingerprint": fps, "ids": ids, "loss": loss.detach().double(),
+            "grad_norm": grad_norms, "grad_rows": grad_rows}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--reference", default=os.environ.get("HACKABLE_LM_REFERENCE"),
                     required="HACKABLE_LM_REFERENCE" not in os.environ,
                     help="path of the hackable-lm checkout (default: $HACKABLE_LM_REFERENCE)")
     ap.add_argument("--out", default=str(HERE))
+    ap.add_argument("--only", nargs="*", help="fixture names to write (default: all)")
     args = ap.parse_args()
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.reference)
@@ -194,19 +253,23 @@ def main() -> None:
     import model  # noqa: E402
 
     torch.set_num_threads(max(1, torch.get_num_threads()))
-    fixtures = {
-        "rmsnorm_c1": make_rmsnorm_c1(model),
-        "residual_rms_norm": make_residual_rms_norm(model),
-        "swiglu": make_swiglu(kernels),
-        "rope_tables": make_rope_tables(model),
-        "qk_norm_rope": make_qk_norm_rope(kernels, model),
-        "qkv": make_qkv(model, config),
-        "lm_head": make_lm_head(kernels, model, config),
+    makers = {
+        "rmsnorm_c1": lambda: make_rmsnorm_c1(model),
+        "residual_rms_norm": lambda: make_residual_rms_norm(model),
+        "swiglu": lambda: make_swiglu(kernels),
+        "rope_tables": lambda: make_rope_tables(model),
+        "qk_norm_rope": lambda: make_qk_norm_rope(kernels, model),
+        "qkv": lambda: make_qkv(model, config),
+        "lm_head": lambda: make_lm_head(kernels, model, config),
     }
+    for name, case in MODEL_CASES.items():
+        makers[name] = lambda case=case: make_model(model, config, **case)
     outdir = Path(args.out)
-    for name, obj in fixtures.items():
+    for name, make in makers.items():
+        if args.only and name not in args.only:
+            continue
         path = outdir / f"{name}.pt"
-        torch.save(obj, path)
+        torch.save(make(), path)
         print(f"wrote {path} ({path.stat().st_size} bytes)")
 
 

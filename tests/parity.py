@@ -14,6 +14,9 @@ the reference GPU test's tolerance (tests/test_kernels.py:78-79 upstream).
 """
 from __future__ import annotations
 
+import json
+import os
+
 import torch
 
 BF16_TOL = 2e-2
@@ -46,16 +49,31 @@ def bf16_err(actual, expected) -> float:
     return ((a - e).abs() / denom).max().item()
 
 
+def record(what: str, **metrics) -> None:
+    """Append one JSON line {test, what, metrics} to $HLM_PARITY_LOG when it is set, so a
+    GPU run leaves a table of every comparison's measured error (not just pass/fail)."""
+    path = os.environ.get("HLM_PARITY_LOG")
+    if not path:
+        return
+    test = os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0]
+    with open(path, "a") as f:
+        f.write(json.dumps({"test": test, "what": what, **metrics}) + "\n")
+
+
 def assert_bf16_close(actual, expected, tol: float = BF16_TOL, what: str = ""):
     err = bf16_err(actual, expected)
+    strict = rms_normalised_max_err(actual, expected)
+    record(what, bf16_err=err, max_err_over_rms=strict, tol=tol)
     assert err <= tol, (f"{what}: max|err|/(rms+|ref|) = {err:.3e} > {tol:.1e} "
-                        f"(max|err|/rms = {rms_normalised_max_err(actual, expected):.3e})")
+                        f"(max|err|/rms = {strict:.3e})")
 
 
 def assert_loss_close(actual, expected, tol: float = LOSS_REL_TOL, what: str = "loss"):
     a = float(actual)
     e = float(expected)
-    assert abs(a - e) <= tol * max(abs(e), 1e-12), f"{what}: {a} vs {e} (rel tol {tol})"
+    rel = abs(a - e) / max(abs(e), 1e-12)
+    record(what, loss_rel_err=rel, tol=tol)
+    assert rel <= tol, f"{what}: {a} vs {e} (rel err {rel:.3e} > tol {tol})"
 
 
 def assert_fp32_close(actual, expected, tol: float = FP32_TOL, what: str = ""):

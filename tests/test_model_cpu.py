@@ -69,3 +69,19 @@ def test_optimizer_updates_every_parameter():
     opt.step()
     for n, p in model.named_parameters():
         assert not torch.equal(before[n], p.detach()), n
+
+
+def test_torch_backend_matches_reference_model_fixture(golden):
+    """This package's model (reference formulation, fp32, CPU) against the reference's
+    own LanguageModel on the same seeded weights and batch (depth 4, windowed
+    attention): init fingerprints, loss and gradients agree to fp32 rounding."""
+    import model_golden as mg
+
+    gd = golden("model_d4_window")
+    model = mg.build(gd, "torch")
+    x, y = mg.batch(gd, "cpu")
+    _, loss = model(x, y)
+    loss.backward()
+    assert abs(loss.item() - gd["loss"].item()) <= 1e-5 * gd["loss"].item()
+    for n, (norm_err, row_err) in mg.grad_errors(model, gd).items():
+        assert norm_err <= 1e-4 and row_err <= 1e-4, (n, norm_err, row_err)

@@ -83,6 +83,30 @@ def test_no_alloc_matches_workspace_entry_point(cuda_device):
     assert _lib.device_error(stream) == 0
 
 
+def test_no_alloc_scalar_path_and_empty_rows(cuda_device):
+    """cols = 383 (not a multiple of the 16-byte vector) takes the scalar kernel;
+    rows = 0 must give grad_weight == 0 even though the shared array still holds the
+    previous call's partial sums."""
+    from hackable_lm_b200 import _lib
+
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    x, w, gout, gnorm = _inputs(500, 383, torch.bfloat16, 4, cuda_device)
+    ref_gin, ref_gw = _with_workspace(lib, x, w, gout, gnorm, stream)
+    gin, gw = _no_alloc(lib, x, w, gout, gnorm, stream)
+    torch.cuda.synchronize()
+    assert_bf16_close(gin, ref_gin, what="grad_in (scalar path)")
+    assert_bf16_close(gw, ref_gw, what="grad_weight (scalar path)")
+    empty = torch.empty(0, 383, dtype=torch.bfloat16, device=cuda_device)
+    gw0 = torch.full((383,), 7.0, dtype=torch.bfloat16, device=cuda_device)
+    rc = lib.hlm_residual_rms_norm_bwd_noalloc(empty.data_ptr(), w.data_ptr(), None, empty.data_ptr(),
+                                               empty.data_ptr(), gw0.data_ptr(), 0, 383, ctypes.c_float(1e-6),
+                                               1, stream)
+    assert rc == 0, rc
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(gw0) == 0
+
+
 def test_no_alloc_rejects_too_many_columns(cuda_device):
     from hackable_lm_b200 import _lib
 
