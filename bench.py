@@ -258,24 +258,6 @@ def bench_lm_head(args, d: Dist, device) -> dict:
         timers[k].__exit__(None, None, None)
     launches = _lib.launch_count() - n0
     clk = clocks.stop()
-    # per-phase breakdown of the first timed step (this rank): micro-steps, the exposed
-    # part of the gradient all-reduce (the last micro-step waits for DDP's final
-    # buckets), gradient clipping and the optimizer step
-    prev, micro = start, []
-    phases = {}
-    for tag, ev in phase_events:
-        ms = prev.elapsed_time(ev)
-        if tag == "micro":
-            micro.append(ms)
-        else:
-            phases[tag] = ms
-        prev = ev
-    plain = micro[:-1] if len(micro) > 1 else micro
-    step_phases = {"micro_step_ms": round(statistics.mean(plain), 3),
-                   "last_micro_step_ms": round(micro[-1], 3),
-                   "exposed_allreduce_ms": round(micro[-1] - statistics.mean(plain), 3) if d.world > 1 else 0.0,
-                   "clip_ms": round(phases.get("clip", 0.0), 3), "optimizer_ms": round(phases.get("opt", 0.0), 3),
-                   "note": "first timed step on rank 0; the optimizer's Muon work is sharded over the ranks"}
     ms_per_step = total_ms / args.steps
     value = M * d.world / (ms_per_step / 1e3)
 

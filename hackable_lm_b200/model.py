@@ -72,7 +72,7 @@ class RMSNorm(nn.Module):
         self.backend = backend
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if self.backend == "b200" and x.is_cuda:
+        if self.backend == "b200" and (x.is_cuda or x.is_meta):
             return kernels.rms_norm(x, self.weight, self.eps)
         return rms_norm_torch(x, self.weight, self.eps)
 

@@ -112,7 +112,7 @@ swiglu.register_autograd(_swiglu_bwd, setup_context=_swiglu_setup)
 
 def gate_up_swiglu_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
     """Shapes and dtypes the fused gate_up + SwiGLU kernel takes."""
-    return (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+    return ((x.is_cuda or x.is_meta) and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
             and x.shape[-1] % 64 == 0 and weight.shape[0] % 256 == 0 and weight.shape[1] == x.shape[-1])
 
 
@@ -173,7 +173,7 @@ gate_up_swiglu.register_autograd(_gate_up_bwd, setup_context=_gate_up_setup)
 def swiglu_down_supported(w_gate_up: torch.Tensor, w_down: torch.Tensor) -> bool:
     """Shapes and dtypes of the fused down-projection backward (grad_h GEMM + SwiGLU backward)."""
     C, H = w_down.shape
-    return (w_down.is_cuda and w_down.dtype == torch.bfloat16 and w_gate_up.dtype == torch.bfloat16
+    return ((w_down.is_cuda or w_down.is_meta) and w_down.dtype == torch.bfloat16 and w_gate_up.dtype == torch.bfloat16
             and C % 64 == 0 and H % 256 == 0 and w_gate_up.shape[0] == 2 * H)
 
 
@@ -201,19 +201,40 @@ def _swiglu_down_setup(ctx, inputs, output):
     ctx.set_materialize_grads(False)
 
 
-def swiglu_down_grad(grad_y: torch.Tensor, weight: torch.Tensor, gate_up: torch.Tensor,
-                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """grad_gate_up = swiglu_backward(gate_up, grad_y @ weight) in one kernel (no autograd):
-    grad_y [..., C], weight [C, H] (the down projection's nn.Linear weight), gate_up [..., 2H]."""
-    dev = _require_cuda(grad_y, weight, gate_up)
+def _swiglu_down_grad_into(grad_y: torch.Tensor, weight: torch.Tensor, gate_up: torch.Tensor,
+                           out: torch.Tensor) -> None:
+    dev = _require_cuda(grad_y, weight, gate_up, out)
     C, H = weight.shape
     gy = grad_y.contiguous()
     g = gate_up.contiguous()
     w = weight.contiguous()
-    if out is None:
-        out = torch.empty_like(g)
+    if not out.is_contiguous() or out.shape != g.shape or out.dtype != g.dtype:
+        raise RuntimeError("swiglu_down_grad: out must be a contiguous tensor like gate_up")
     check(_lib_().hlm_swiglu_down_bwd(_ptr(gy), _ptr(w), _ptr(g), _ptr(out), gy.numel() // C, C, H,
                                        _stream(dev)), "hlm_swiglu_down_bwd")
+
+
+@torch.library.custom_op("hackable_lm_b200::swiglu_down_backward", mutates_args=())
+def swiglu_down_backward(grad_y: torch.Tensor, weight: torch.Tensor, gate_up: torch.Tensor) -> torch.Tensor:
+    """grad_gate_up = swiglu_backward(gate_up, grad_y @ weight) in one kernel:
+    grad_y [..., C], weight [C, H] (the down projection's nn.Linear weight), gate_up [..., 2H]."""
+    out = torch.empty(gate_up.shape, dtype=gate_up.dtype, device=gate_up.device)
+    _swiglu_down_grad_into(grad_y, weight, gate_up, out)
+    return out
+
+
+@swiglu_down_backward.register_fake
+def _swiglu_down_backward_fake(grad_y, weight, gate_up):
+    return torch.empty_like(gate_up, memory_format=torch.contiguous_format)
+
+
+def swiglu_down_grad(grad_y: torch.Tensor, weight: torch.Tensor, gate_up: torch.Tensor,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """grad_gate_up = swiglu_backward(gate_up, grad_y @ weight) in one kernel (no autograd);
+    with ``out`` given, written into it (the benchmark reuses one output buffer)."""
+    if out is None:
+        return swiglu_down_backward(grad_y, weight, gate_up)
+    _swiglu_down_grad_into(grad_y, weight, gate_up, out)
     return out
 
 
@@ -225,7 +246,7 @@ def _swiglu_down_bwd(ctx, grad_y):
     gy = grad_y.contiguous()
     grad_gate_up = None
     if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
-        grad_gate_up = swiglu_down_grad(gy, weight, gate_up)
+        grad_gate_up = swiglu_down_backward(gy, weight, gate_up)
     grad_w = None
     if ctx.needs_input_grad[2]:
         grad_w = gy.reshape(-1, C).t() @ h.reshape(-1, H)

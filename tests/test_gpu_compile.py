@@ -49,6 +49,7 @@ def _op_cases(dev):
         "swiglu_backward": (ops.swiglu_backward, (gate_up.detach(), _bf(g, 128, 256))),
         "gate_up_swiglu": (ops.gate_up_swiglu, (xm, w_gu)),
         "swiglu_down": (ops.swiglu_down, (h.detach().requires_grad_(True), gu.detach().requires_grad_(True), w_dn)),
+        "swiglu_down_backward": (ops.swiglu_down_backward, (_bf(g, 128, 256), w_dn.detach(), gu.detach())),
         "rms_norm": (ops.rms_norm, (r, None, 1e-6)),
         "rms_norm_weighted": (ops.rms_norm, (r, wn, 1e-6)),
         "residual_rms_norm": (ops.residual_rms_norm, (r, b, None, 1e-6)),
@@ -64,7 +65,7 @@ def _op_cases(dev):
     }
 
 
-OP_NAMES = ["swiglu", "swiglu_backward", "gate_up_swiglu", "swiglu_down", "rms_norm", "rms_norm_weighted",
+OP_NAMES = ["swiglu", "swiglu_backward", "gate_up_swiglu", "swiglu_down", "swiglu_down_backward", "rms_norm", "rms_norm_weighted",
             "residual_rms_norm", "rms_norm_backward", "qk_norm_rope", "qk_norm_rope_backward", "qkv_rope",
             "qkv_rope_backward", "lm_head_ce", "scale_"]
 

@@ -85,3 +85,40 @@ def test_torch_backend_matches_reference_model_fixture(golden):
     assert abs(loss.item() - gd["loss"].item()) <= 1e-5 * gd["loss"].item()
     for n, (norm_err, row_err) in mg.grad_errors(model, gd).items():
         assert norm_err <= 1e-4 and row_err <= 1e-4, (n, norm_err, row_err)
+
+
+def test_b200_model_traces_fullgraph_on_meta():
+    """The B200 model compiles the way the reference trains (torch.compile with
+    fullgraph=True, dynamic=False, kernels.py:126-137) with no graph break, forward and
+    backward: traced on meta tensors (the operators' fake implementations) with the
+    aot_eager backend, every B200 operator of the step appears in the graph.  The GPU
+    test runs the compiled model against eager."""
+    from torch.utils._python_dispatch import TorchDispatchMode
+
+    from hackable_lm_b200 import kernels
+
+    class Rec(TorchDispatchMode):
+        def __init__(self):
+            super().__init__()
+            self.ops = set()
+
+        def __torch_dispatch__(self, func, types, args=(), kwargs=None):
+            self.ops.add(str(func.overloadpacket))
+            return func(*args, **(kwargs or {}))
+
+    cfg = hcfg.model_config_for_depth(2, vocab_size=4096, sequence_len=256, attention_window=64, backend="b200")
+    with torch.device("meta"):
+        m = LanguageModel(cfg)
+    kernels.apply_precision_policy(m, "bf16")
+    compiled = torch.compile(m, backend="aot_eager", fullgraph=True, dynamic=False)
+    ids = torch.randint(0, 4096, (2, 256), device="meta")
+    rec = Rec()
+    with rec:
+        _, loss = compiled(ids, ids)
+        loss.backward()
+    want = {f"hackable_lm_b200.{n}" for n in (
+        "qkv_rope", "qkv_rope_backward", "gate_up_swiglu", "swiglu_down", "swiglu_down_backward",
+        "residual_rms_norm", "rms_norm", "rms_norm_backward", "lm_head_ce", "scale_")}
+    assert not want - rec.ops, sorted(want - rec.ops)
+    for n, p in m.named_parameters():
+        assert p.grad is not None and p.grad.shape == p.shape, n
