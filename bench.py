@@ -342,7 +342,7 @@ D12_FLOPS_PER_TOKEN = 887_095_296  # config.estimate_flops_per_token, full causa
 # operator calls per micro-step: per-layer kernels once per layer, LM-head kernels once
 D12_KERNELS = {"lm_logits": 1, "lm_dlogits": 1, "lm_dx": 1, "lm_dw": 1, "gate_up": 12, "qkv_fwd": 12, "qkv_bwd_norm": 12,
                "qkv_dx": 12, "qkv_dw": 12, "swiglu_fwd": 12, "swiglu_bwd": 12, "swiglu_down_bwd": 12,
-               "rmsnorm_fwd": 25, "rmsnorm_bwd": 25}
+               "proj_norm": 24, "rmsnorm_fwd": 1, "rmsnorm_bwd": 25}
 
 
 def d12_config(world: int, accum: int, max_grad_norm: float = 1.0) -> dict:
@@ -444,19 +444,21 @@ def bench_d12(args, d: Dist, device) -> dict:
 
     M = s.micro_batch * s.seq_len
     C, V, Hd = s.config.n_embd, s.config.vocab_size, 3 * s.config.n_head * s.config.head_dim
+    Hm, Dq = s.config.mlp_hidden, s.config.n_head * s.config.head_dim
     # algorithmic FLOPs / HBM bytes per operator call (bf16 = 2 bytes)
     flops = {"lm_logits": 2.0 * M * C * V, "lm_dx": 2.0 * M * C * V, "lm_dw": 2.0 * M * C * V,
              "qkv_fwd": 2.0 * M * C * Hd, "qkv_dx": 2.0 * M * C * Hd, "qkv_dw": 2.0 * M * C * Hd,
-             "gate_up": 2.0 * M * C * 2 * s.config.mlp_hidden}
-    Hm, Dq = s.config.mlp_hidden, s.config.n_head * s.config.head_dim
+             "gate_up": 2.0 * M * C * 2 * s.config.mlp_hidden,
+             # o_proj (K = C) and down (K = H) calls alternate: the mean per call
+             "proj_norm": 2.0 * M * C * (Dq + s.config.mlp_hidden) / 2}
     n_fwd = D12_KERNELS["rmsnorm_fwd"]
     bytes_ = {
         "swiglu_fwd": 2.0 * M * 3 * Hm,           # read gate_up [M,2H], write [M,H]
         "swiglu_bwd": 2.0 * M * 5 * Hm,           # read gate_up + grad [M,H], write [M,2H]
-        # one weightless norm (read x, write norm) + residual variants (read 2, write 2)
+        # the input norm (read x, write norm); the residual variants run inside proj_norm
         "rmsnorm_fwd": 2.0 * M * C * (2 + 4 * (n_fwd - 1)) / n_fwd,
         # input norm: read x + grad_norm, write grad; residual variants also read the residual grad
-        "rmsnorm_bwd": 2.0 * M * C * (3 + 4 * (n_fwd - 1)) / n_fwd,
+        "rmsnorm_bwd": 2.0 * M * C * (3 + 4 * (D12_KERNELS["rmsnorm_bwd"] - 1)) / D12_KERNELS["rmsnorm_bwd"],
         "qkv_bwd_norm": 2.0 * M * Dq * 6,         # read q, k, dq, dk; write dq_in, dk_in
         "lm_dlogits": 4.0 * M * V,                # bf16 logits read + dlogits written in place
         # down grad_h GEMM + SwiGLU backward: read grad_y [M,C], gate_up [M,2H], W_down [C,H];
@@ -654,6 +656,30 @@ def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
     tensor("gate_up_swiglu X[32768,768] W[4096,768]", lambda a: ops.gate_up_swiglu(a, wg), (xg,),
            2 * 32768 * 768 * 4096)
     del xg, wg
+    # o_proj / down projection with the residual add + RMSNorm in the GEMM epilogue (d12 shapes),
+    # beside the unfused chain it replaces (cuBLAS GEMM + residual_rms_norm kernel).  Bound: the
+    # slower of the FLOPs at the bf16 peak and the bytes (read y, W, residual; write out, norm)
+    # at the HBM peak: o_proj is HBM-bound, down is tensor-bound.
+    for name, K in (("o_proj", 768), ("down", 2048)):
+        key = f"proj_norm {name} y[32768,{K}] W[768,{K}]"
+        if not want(key):
+            continue
+        yd = torch.randn(32768, K, generator=g).to(torch.bfloat16).to(device)
+        wd = (torch.randn(768, K, generator=g) * 0.02).to(torch.bfloat16).to(device)
+        rd = torch.randn(32768, 768, generator=g).to(torch.bfloat16).to(device)
+        flop = 2 * 32768 * 768 * K
+        nbytes = 2 * (32768 * K + 768 * K + 3 * 32768 * 768 + 32768 * 768)
+        ms = timed(lambda a, b: ops.proj_residual_norm(a, wd, b, 1e-6), (yd, rd), nbytes_of((yd, rd)))
+        ms_ref = timed(lambda a, b: ops.residual_rms_norm(b, torch.nn.functional.linear(a, wd), None, 1e-6),
+                       (yd, rd), nbytes_of((yd, rd)))
+        t_tensor = flop / (peaks["bf16_tflops"] * 1e12) * 1e3
+        t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9) * 1e3
+        res[key] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(flop / (ms / 1e3) / 1e12, 1),
+                    "GB/s": round(nbytes / (ms / 1e3) / 1e9, 1), "flop": flop, "bytes": nbytes,
+                    "bound": "tensor" if t_tensor >= t_hbm else "hbm",
+                    "frac_of_roofline": round(max(t_tensor, t_hbm) / ms, 4),
+                    "unfused_us": round(ms_ref * 1e3, 2)}
+        del yd, wd, rd
     # down projection backward with the SwiGLU backward in its epilogue (d12 shape): HBM-bound,
     # 2*M*C*H = 103 GFLOP against 590 MB (read grad_y, gate_up, W_down; write grad_gate_up)
     if want("swiglu_down_bwd"):

@@ -58,6 +58,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "hlm_scale_by_device_scalar": ([_P, _P, _I64, c_int, _P], c_int),
     "hlm_gate_up_swiglu_fwd": ([_P, _P, _P, _P, _I64, _I64, _I64, _P], c_int),
     "hlm_swiglu_down_bwd": ([_P, _P, _P, _P, _I64, _I64, _I64, _P], c_int),
+    "hlm_proj_residual_rms_norm_fwd": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, c_float, _P], c_int),
     "hlm_gemm_bf16": (
         [_P, _P, _P, _I64, _I64, _I64, c_int, c_int, _I64, _I64, _I64, c_int, c_int, _P], c_int),
 }
@@ -120,6 +121,7 @@ DEVERR_NAMES = {
     4: "timeout: MMA issuer waiting for the epilogue", 5: "timeout: teardown drain of TMA copies",
     6: "unexpected tensor-memory address", 7: "self-test wait ran out (expected)",
     8: "timeout: epilogue waiting for its input tile",
+    9: "timeout: epilogue waiting for its cluster peers' row sums",
 }
 DEVERR_SELFTEST_TIMEOUT = 7
 
@@ -136,7 +138,7 @@ KERNEL_IDS = {
     "lm_logits": 1, "lm_dlogits": 2, "lm_dx": 3, "lm_dw": 4, "qkv_fwd": 5, "qkv_bwd_norm": 6,
     "qkv_dx": 7, "qkv_dw": 8, "swiglu_fwd": 9, "swiglu_bwd": 10, "rmsnorm_fwd": 11,
     "rmsnorm_bwd": 12, "qk_rope_fwd": 13, "qk_rope_bwd": 14, "gemm": 15, "gate_up": 16,
-    "swiglu_down_bwd": 17,
+    "swiglu_down_bwd": 17, "proj_norm": 18,
 }
 
 

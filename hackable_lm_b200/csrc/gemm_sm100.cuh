@@ -40,6 +40,18 @@ struct epi_has_init : std::false_type {};
 template <class E>
 struct epi_has_init<E, std::void_t<decltype(E::init(static_cast<uint8_t*>(nullptr)))>> : std::true_type {};
 
+// Epilogues of the single-CTA kernel that exchange data with the other CTAs of
+// a thread-block cluster (launch_gemm_cluster) declare
+// `static constexpr bool kClusterExchange = true`: the kernel then adds a
+// cluster barrier after its barrier initialisation (no CTA signals a peer's
+// barrier before the peer initialised it) and before it exits (no CTA leaves
+// while a peer may still write its shared memory).
+template <class E, class = void>
+struct epi_cluster_exchange : std::false_type {};
+template <class E>
+struct epi_cluster_exchange<E, std::void_t<decltype(E::kClusterExchange)>>
+    : std::integral_constant<bool, E::kClusterExchange> {};
+
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int kUmmaK = 16;
@@ -147,6 +159,7 @@ __global__ void __launch_bounds__(gemm_threads<EPI_WARPS>(), 1)
       mbar_init(TFULL_BAR(a), 1);
       mbar_init(TEMPTY_BAR(a), EPI_WARPS);  // one arrival per epilogue warp
     }
+    if constexpr (epi_has_init<Epi>::value) Epi::init(base_ptr + L::kEpiOffset);
     fence_mbar_init();
     prefetch_tensormap(&tmA0);
     if (p.a_seg1 > 0) {
@@ -161,6 +174,7 @@ __global__ void __launch_bounds__(gemm_threads<EPI_WARPS>(), 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (epi_cluster_exchange<Epi>::value) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
@@ -300,6 +314,7 @@ __global__ void __launch_bounds__(gemm_threads<EPI_WARPS>(), 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (epi_cluster_exchange<Epi>::value) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
@@ -597,6 +612,53 @@ int launch_gemm_sm100(const CUtensorMap& a0, const CUtensorMap& a1, const CUtens
   {
     LaunchScope scope(kernel_id, stream);
     kern<<<grid, gemm_threads<EPI_WARPS>(), smem, stream>>>(a0, a1, a2, b, p, ep);
+  }
+  return launch_status();
+}
+
+// Cluster launch of the single-CTA kernel: clusters of `cluster` CTAs (grid a
+// multiple of it), for
+// epilogues that exchange data across the cluster.  With p.n_tiles == cluster
+// and p.splits == 1, the CTAs of a cluster take the n tiles of one m tile
+// together (work index w = m_tile * n_tiles + n_tile, stepped by the grid).
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS = 4>
+int launch_gemm_cluster(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& a2,
+                        const CUtensorMap& b, const GemmParams& p, const typename Epi::Params& ep,
+                        int cluster, cudaStream_t stream, int kernel_id) {
+  using L = GemmSmem<BN, STAGES>;
+  auto kern = gemm_sm100_kernel<BN, STAGES, A_MN, B_MN, Epi, EPI_WARPS>;
+  const int smem = L::kEpiOffset + Epi::template smem_bytes<EPI_WARPS>() + 1024;
+  static_assert(L::kEpiOffset + Epi::template smem_bytes<EPI_WARPS>() + 1024 <= 232448,
+                "shared memory budget exceeded");
+  if (cluster < 1 || cluster > 8 || p.n_tiles != cluster || p.splits != 1) return HLM_ERR_INVALID_ARG;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return HLM_ERR_LAUNCH;
+  if (p.m_tiles <= 0) return HLM_OK;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(gemm_threads<EPI_WARPS>(), 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // As many clusters as fit on the GPU at once (cluster placement within GPCs can
+  // leave SMs unused, e.g. 45 clusters of three CTAs on 148 SMs): a persistent
+  // cluster beyond that would start only when another has finished all its tiles.
+  int clusters = num_sms_of_current_device() / cluster;
+  cfg.gridDim = dim3(static_cast<unsigned>(clusters * cluster), 1, 1);
+  int fit = 0;
+  if (cudaOccupancyMaxActiveClusters(&fit, kern, &cfg) == cudaSuccess && fit > 0 && fit < clusters)
+    clusters = fit;
+  if (clusters > p.m_tiles) clusters = p.m_tiles;
+  if (clusters < 1) clusters = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(clusters * cluster), 1, 1);
+  {
+    LaunchScope scope(kernel_id, stream);
+    if (cudaLaunchKernelEx(&cfg, kern, a0, a1, a2, b, p, ep) != cudaSuccess) return HLM_ERR_LAUNCH;
   }
   return launch_status();
 }

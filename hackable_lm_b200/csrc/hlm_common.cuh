@@ -52,13 +52,15 @@ enum DeviceErrorCode : int {
   kDevErrBadTmem = 6,          // tcgen05.alloc returned an unexpected address
   kDevErrSelftestTimeout = 7,  // hlm_selftest_bounded_wait: the wait ran out (expected)
   kDevErrTimeoutEpiLoad = 8,   // an epilogue waited too long for its own TMA input load
+  kDevErrTimeoutPeer = 9,      // an epilogue waited too long for its cluster peers' row sums
 };
 static_assert(kDevErrTimeoutFull == HLM_DEVERR_TIMEOUT_FULL && kDevErrTimeoutEmpty == HLM_DEVERR_TIMEOUT_EMPTY &&
                   kDevErrTimeoutTmemFull == HLM_DEVERR_TIMEOUT_TMEM_FULL &&
                   kDevErrTimeoutTmemEmpty == HLM_DEVERR_TIMEOUT_TMEM_EMPTY &&
                   kDevErrTimeoutDrain == HLM_DEVERR_TIMEOUT_DRAIN && kDevErrBadTmem == HLM_DEVERR_BAD_TMEM &&
                   kDevErrSelftestTimeout == HLM_DEVERR_SELFTEST_TIMEOUT &&
-                  kDevErrTimeoutEpiLoad == HLM_DEVERR_TIMEOUT_EPI_LOAD,
+                  kDevErrTimeoutEpiLoad == HLM_DEVERR_TIMEOUT_EPI_LOAD &&
+                  kDevErrTimeoutPeer == HLM_DEVERR_TIMEOUT_PEER,
               "device error codes match the public header");
 
 // Upper bound for any single mbarrier wait.  Legitimate waits in these kernels

@@ -9,11 +9,12 @@ Module and parameter names follow the reference ``model.py`` one to one
 CPU), ``"b200"`` the hand-written sm_100a kernels:
 
 * QKVProjection.fwd_b200     -> fused tcgen05 GEMM + QK-norm + RoPE (qkv_rope)
-* OutputProjection.fwd_b200  -> o_proj GEMM + fused residual-add + RMSNorm
+* OutputProjection.fwd_b200  -> o_proj GEMM with the residual add + RMSNorm in
+  its epilogue (one cluster of CTAs per 128-row block exchanges row sums)
 * GateUpProjection.fwd_b200  -> gate_up GEMM with the SwiGLU in its epilogue
-* DownProjection.fwd_b200    -> down GEMM + fused residual-add + RMSNorm
-* MLP (both of the above on b200) -> gate_up_swiglu + swiglu_down: the down
-  GEMM's backward computes grad_h and the SwiGLU backward in one kernel
+* DownProjection.fwd_b200    -> down GEMM with the residual add + RMSNorm in its epilogue
+* MLP (both of the above on b200) -> gate_up_swiglu + swiglu_down_residual_norm:
+  the down GEMM's backward computes grad_h and the SwiGLU backward in one kernel
 * LMHeadProjection.fwd_b200  -> fused LM head + cross-entropy
 * input norm                 -> RMSNorm kernel
 
@@ -175,7 +176,12 @@ class OutputProjection(AcceleratedModule):
 
     def fwd_b200(self, y: torch.Tensor, residual: torch.Tensor):
         b, t, h, d = y.shape
-        return kernels.residual_rms_norm(residual, self.o_proj(y.reshape(b, t, h * d)), self.norm_eps)
+        y2 = y.reshape(b, t, h * d)
+        w = self.o_proj.weight
+        if ops.proj_norm_supported(y2, w) and residual.dtype == y2.dtype:
+            # o_proj GEMM with the residual add and RMSNorm in its epilogue
+            return ops.proj_residual_norm(y2, w, residual, self.norm_eps)
+        return kernels.residual_rms_norm(residual, self.o_proj(y2), self.norm_eps)
 
 
 class CausalSelfAttention(nn.Module):
@@ -221,6 +227,9 @@ class DownProjection(AcceleratedModule):
         return residual_rms_norm_torch(residual, self.down_proj(x), self.norm_eps)
 
     def fwd_b200(self, x: torch.Tensor, residual: torch.Tensor):
+        w = self.down_proj.weight
+        if ops.proj_norm_supported(x, w) and residual.dtype == x.dtype:
+            return ops.proj_residual_norm(x, w, residual, self.norm_eps)
         return kernels.residual_rms_norm(residual, self.down_proj(x), self.norm_eps)
 
 
@@ -235,9 +244,12 @@ class MLP(nn.Module):
             w_gu = self.gate_up.gate_up_proj.weight
             w_dn = self.down.down_proj.weight
             if ops.gate_up_swiglu_supported(x, w_gu) and ops.swiglu_down_supported(w_gu, w_dn):
-                # gate_up GEMM with the SwiGLU in its epilogue, then the down GEMM whose
-                # backward computes grad_h and the SwiGLU backward in one kernel
+                # gate_up GEMM with the SwiGLU in its epilogue, then the down GEMM (residual
+                # add + RMSNorm in its epilogue) whose backward computes grad_h and the
+                # SwiGLU backward in one kernel
                 h, gate_up = ops.gate_up_swiglu(x, w_gu)
+                if ops.proj_norm_supported(h, w_dn) and residual.dtype == h.dtype:
+                    return ops.swiglu_down_residual_norm(h, gate_up, w_dn, residual, self.down.norm_eps)
                 y = ops.swiglu_down(h, gate_up, w_dn)
                 return kernels.residual_rms_norm(residual, y, self.down.norm_eps)
         return self.down(self.gate_up(x), residual)

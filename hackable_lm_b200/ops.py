@@ -257,6 +257,122 @@ swiglu_down.register_autograd(_swiglu_down_bwd, setup_context=_swiglu_down_setup
 
 
 # ---------------------------------------------------------------------------
+# Output / down projection + residual add + RMSNorm in one GEMM
+# (reference: OutputProjection model.py:253-264, DownProjection model.py:295-304,
+# residual_rms_norm model.py:73-75)
+# ---------------------------------------------------------------------------
+def proj_norm_supported(y: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Shapes the fused projection + residual + RMSNorm GEMM takes: bf16, K % 64 == 0,
+    N = 1..4 x 256 or 1..4 x 128 (the row's N columns fit one thread-block cluster)."""
+    N, K = weight.shape
+    return ((y.is_cuda or y.is_meta) and y.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+            and y.shape[-1] == K and K % 64 == 0
+            and ((N % 256 == 0 and N // 256 <= 4) or (N % 128 == 0 and N // 128 <= 4)))
+
+
+def _proj_norm_fwd(y: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor,
+                   eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(y, weight, residual)
+    N, K = weight.shape
+    y2 = y.contiguous()
+    w = weight.contiguous()
+    r = residual.contiguous()
+    if r.shape[-1] != N or r.numel() // max(1, N) != y2.numel() // max(1, K) or r.dtype != y2.dtype:
+        raise RuntimeError("proj_residual_norm: residual must be [..., N] with y's rows and dtype")
+    out = torch.empty(r.shape, dtype=r.dtype, device=dev)
+    norm = torch.empty(r.shape, dtype=r.dtype, device=dev)
+    check(_lib_().hlm_proj_residual_rms_norm_fwd(_ptr(y2), _ptr(w), _ptr(r), _ptr(out), _ptr(norm),
+                                                  y2.numel() // K, K, N, float(eps), _stream(dev)),
+          "hlm_proj_residual_rms_norm_fwd")
+    return out, norm
+
+
+def _residual_norm_grad(out, grad_out, grad_norm, eps):
+    """Gradient reaching residual + branch through out (directly and through the norm)."""
+    if grad_norm is None:
+        return grad_out
+    g, _ = rms_norm_backward(out, None, grad_out, grad_norm, eps)
+    return g
+
+
+@torch.library.custom_op("hackable_lm_b200::proj_residual_norm", mutates_args=())
+def proj_residual_norm(y: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor,
+                       eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(out, norm) with out = residual + y @ weight^T and norm = rms_norm(out), one GEMM."""
+    return _proj_norm_fwd(y, weight, residual, eps)
+
+
+@proj_residual_norm.register_fake
+def _proj_residual_norm_fake(y, weight, residual, eps):
+    return (torch.empty_like(residual, memory_format=torch.contiguous_format),
+            torch.empty_like(residual, memory_format=torch.contiguous_format))
+
+
+def _proj_norm_setup(ctx, inputs, output):
+    y, weight, residual, eps = inputs
+    out, _ = output
+    ctx.save_for_backward(y, weight, out)
+    ctx.eps = eps
+    ctx.set_materialize_grads(False)
+
+
+def _proj_norm_bwd(ctx, grad_out, grad_norm):
+    y, weight, out = ctx.saved_tensors
+    if grad_out is None and grad_norm is None:
+        return None, None, None, None
+    g = _residual_norm_grad(out, grad_out, grad_norm, ctx.eps)
+    N, K = weight.shape
+    g2 = g.reshape(-1, N)
+    grad_y = (g2 @ weight).reshape(y.shape) if ctx.needs_input_grad[0] else None
+    grad_w = (g2.t() @ y.reshape(-1, K)) if ctx.needs_input_grad[1] else None
+    return grad_y, grad_w, (g if ctx.needs_input_grad[2] else None), None
+
+
+proj_residual_norm.register_autograd(_proj_norm_bwd, setup_context=_proj_norm_setup)
+
+
+@torch.library.custom_op("hackable_lm_b200::swiglu_down_residual_norm", mutates_args=())
+def swiglu_down_residual_norm(h: torch.Tensor, gate_up: torch.Tensor, weight: torch.Tensor,
+                              residual: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """The down projection of h = swiglu(gate_up) with the residual add and RMSNorm in its
+    epilogue: (out, norm), out = residual + h @ weight^T.  Its backward sends the gradient
+    of residual + branch through the fused grad_h GEMM + SwiGLU backward to gate_up (no
+    gradient for h, as swiglu_down), and the weight gradient is g^T @ h."""
+    return _proj_norm_fwd(h, weight, residual, eps)
+
+
+@swiglu_down_residual_norm.register_fake
+def _swiglu_down_residual_norm_fake(h, gate_up, weight, residual, eps):
+    return (torch.empty_like(residual, memory_format=torch.contiguous_format),
+            torch.empty_like(residual, memory_format=torch.contiguous_format))
+
+
+def _sdrn_setup(ctx, inputs, output):
+    h, gate_up, weight, residual, eps = inputs
+    out, _ = output
+    ctx.save_for_backward(h, gate_up, weight, out)
+    ctx.eps = eps
+    ctx.set_materialize_grads(False)
+
+
+def _sdrn_bwd(ctx, grad_out, grad_norm):
+    h, gate_up, weight, out = ctx.saved_tensors
+    if grad_out is None and grad_norm is None:
+        return None, None, None, None, None
+    g = _residual_norm_grad(out, grad_out, grad_norm, ctx.eps)
+    C, H = weight.shape
+    gy = g.contiguous()
+    grad_gate_up = None
+    if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
+        grad_gate_up = swiglu_down_backward(gy, weight, gate_up)
+    grad_w = (gy.reshape(-1, C).t() @ h.reshape(-1, H)) if ctx.needs_input_grad[2] else None
+    return None, grad_gate_up, grad_w, (g if ctx.needs_input_grad[3] else None), None
+
+
+swiglu_down_residual_norm.register_autograd(_sdrn_bwd, setup_context=_sdrn_setup)
+
+
+# ---------------------------------------------------------------------------
 # RMSNorm / residual-add + RMSNorm  (reference: model.py:14-16, 73-75; kernels.py:245-247)
 # ---------------------------------------------------------------------------
 def _rows_cols(x: torch.Tensor) -> tuple[int, int]:

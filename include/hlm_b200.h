@@ -68,6 +68,7 @@ int hlm_device_error_clear(void* stream);
 #define HLM_DEVERR_BAD_TMEM 6           /* tcgen05.alloc returned an unexpected address */
 #define HLM_DEVERR_SELFTEST_TIMEOUT 7   /* hlm_selftest_bounded_wait ran out, as it should */
 #define HLM_DEVERR_TIMEOUT_EPI_LOAD 8   /* an epilogue waited too long for its own TMA input load */
+#define HLM_DEVERR_TIMEOUT_PEER 9       /* an epilogue waited too long for its cluster peers' row sums */
 
 /* Self-test of the bounded waits: one warp waits on an mbarrier that nothing
  * arrives at, with the same wait helper the GEMM roles use (scope 0: CTA-scope
@@ -100,7 +101,8 @@ uint64_t hlm_launch_count(void);
 #define HLM_KERNEL_GEMM 15
 #define HLM_KERNEL_GATE_UP 16      /* gate_up GEMM + SwiGLU epilogue */
 #define HLM_KERNEL_SWIGLU_DOWN_BWD 17 /* down grad_h GEMM + SwiGLU backward epilogue */
-#define HLM_KERNEL_MAX 18
+#define HLM_KERNEL_PROJ_NORM 18    /* o_proj / down GEMM + residual add + RMSNorm epilogue */
+#define HLM_KERNEL_MAX 19
 
 /* Start timing every launch of kernel `kernel_id`: launch i records
  * start_events[i] immediately before and stop_events[i] immediately after
@@ -299,6 +301,27 @@ int hlm_gate_up_swiglu_fwd(const void* x, const void* w_gate_up, void* gate_up_o
  * gate_up GEMM's input gradients are separate GEMMs.) */
 int hlm_swiglu_down_bwd(const void* grad_y, const void* w_down, const void* gate_up,
                         void* grad_gate_up, int64_t M, int64_t C, int64_t H, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Output / down projection with the residual add and RMSNorm in its epilogue
+ * ------------------------------------------------------------------------ */
+
+/* branch = y @ w^T (rounded to bf16, the reference's F.linear output),
+ * out = residual + branch (rounded to bf16), norm = out * rsqrt(mean(out^2) +
+ * eps) over each row of N values (fp32 math on the bf16 out), all in one
+ * tcgen05 GEMM whose epilogue sees whole rows: the N columns of a 128-row
+ * block are split over a cluster of N / BN CTAs (BN = 256, or 128 when N is
+ * not a multiple of 256), which exchange their per-row sums of squares
+ * through distributed shared memory.  Replaces OutputProjection.fwd_torch
+ * (model.py:253-264) and DownProjection.fwd_torch (model.py:303-304): the
+ * nn.Linear GEMM followed by residual_rms_norm (model.py:73-75).
+ * y [M, K], w [N, K] (the nn.Linear weight), residual / out / norm [M, N], all
+ * bf16 row-major, 16-byte aligned.  Requires K % 64 == 0 and N a multiple of
+ * 128 with N <= 1024 (N = 1..4 times 256, or 1..4 times 128); other shapes
+ * return HLM_ERR_UNSUPPORTED. */
+int hlm_proj_residual_rms_norm_fwd(const void* y, const void* w, const void* residual, void* out,
+                                   void* norm, int64_t M, int64_t K, int64_t N, float eps,
+                                   void* stream);
 
 /* ------------------------------------------------------------------------
  * Plain tcgen05 GEMM (building block; also used by tests)

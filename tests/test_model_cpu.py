@@ -117,8 +117,8 @@ def test_b200_model_traces_fullgraph_on_meta():
         _, loss = compiled(ids, ids)
         loss.backward()
     want = {f"hackable_lm_b200.{n}" for n in (
-        "qkv_rope", "qkv_rope_backward", "gate_up_swiglu", "swiglu_down", "swiglu_down_backward",
-        "residual_rms_norm", "rms_norm", "rms_norm_backward", "lm_head_ce", "scale_")}
+        "qkv_rope", "qkv_rope_backward", "gate_up_swiglu", "swiglu_down_residual_norm", "swiglu_down_backward",
+        "proj_residual_norm", "rms_norm", "rms_norm_backward", "lm_head_ce", "scale_")}
     assert not want - rec.ops, sorted(want - rec.ops)
     for n, p in m.named_parameters():
         assert p.grad is not None and p.grad.shape == p.shape, n
