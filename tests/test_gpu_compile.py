@@ -62,12 +62,17 @@ def _op_cases(dev):
                                                       gq, gk, gv, H, H, 1e-6, True, True)),
         "lm_head_ce": (ops.lm_head_ce, (hidden, w_head, targets, -1, 0, True, True)),
         "scale_": (ops.scale_, (_bf(g, 1000), torch.tensor(0.25, device=dev))),
+        "proj_residual_norm": (ops.proj_residual_norm, (_bf(g, 256, 256, grad=True), _bf(g, 768, 256, std=0.02, grad=True),
+                                                        _bf(g, 256, 768, grad=True), 1e-6)),
+        "swiglu_down_residual_norm": (ops.swiglu_down_residual_norm,
+                                      (h.detach().requires_grad_(True), gu.detach().requires_grad_(True),
+                                       _bf(g, 256, 256, std=0.02, grad=True), _bf(g, 128, 256, grad=True), 1e-6)),
     }
 
 
 OP_NAMES = ["swiglu", "swiglu_backward", "gate_up_swiglu", "swiglu_down", "swiglu_down_backward", "rms_norm", "rms_norm_weighted",
             "residual_rms_norm", "rms_norm_backward", "qk_norm_rope", "qk_norm_rope_backward", "qkv_rope",
-            "qkv_rope_backward", "lm_head_ce", "scale_"]
+            "qkv_rope_backward", "lm_head_ce", "scale_", "proj_residual_norm", "swiglu_down_residual_norm"]
 
 
 @pytest.mark.parametrize("name", OP_NAMES)
