@@ -18,8 +18,8 @@
 //   5. dW GEMM       grad_weight (+)= (P^T @ H_chunk) / n_valid (both MN-major)
 // A pre-pass counts the valid targets of the whole batch so the 1/n_valid
 // scale is known to every chunk on the device, with no host round trip.
-// Within a chunk the dlogits pass of the second row half runs on a side stream
-// alongside the first half's grad_hidden GEMM (see the chunk loop).
+// Within a chunk the dlogits passes of the later row parts run on a side stream,
+// each alongside the grad_hidden GEMM of the part before it (see the chunk loop).
 #include <mutex>
 
 #include "gemm_sm100.cuh"
@@ -323,11 +323,13 @@ __global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restric
 // One side stream (non-blocking) and its events per device, created on first
 // use and kept for the process; the mutex keeps one call's record/wait
 // sequence from interleaving with another thread's.
+constexpr int kLmMaxParts = 4;  // row parts of a chunk's backward pipeline
+
 struct SideStream {
   std::mutex mu;
   cudaStream_t stream = nullptr;
-  cudaEvent_t ev_lse[2] = {nullptr, nullptr};  // [1]: second half may start (caller stream)
-  cudaEvent_t ev_p[2] = {nullptr, nullptr};    // [1]: second half's dlogits done (side stream)
+  cudaEvent_t ev_start = nullptr;                // the side stream's passes may start (caller stream)
+  cudaEvent_t ev_p[kLmMaxParts] = {};            // [q]: part q's dlogits done (side stream)
 };
 
 static SideStream* side_stream_of_current_device() {
@@ -339,10 +341,9 @@ static SideStream* side_stream_of_current_device() {
   SideStream& ss = side[dev];
   if (ss.stream == nullptr) {
     if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
-    for (int i = 0; i < 2; ++i)
-      if (cudaEventCreateWithFlags(&ss.ev_lse[i], cudaEventDisableTiming) != cudaSuccess ||
-          cudaEventCreateWithFlags(&ss.ev_p[i], cudaEventDisableTiming) != cudaSuccess)
-        return nullptr;
+    if (cudaEventCreateWithFlags(&ss.ev_start, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+    for (int i = 0; i < kLmMaxParts; ++i)
+      if (cudaEventCreateWithFlags(&ss.ev_p[i], cudaEventDisableTiming) != cudaSuccess) return nullptr;
   }
   return &ss;
 }
@@ -491,22 +492,40 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
     }
     const bool grads = want_dx || want_dw;
     if (!grads) continue;
-    // 3. dlogits in place.  With at least 512 rows and grad_hidden wanted, the
-    // rows split in two halves (a multiple of 256, the pair tile) and the second
-    // half's pass runs on a side stream x while the first half's grad_hidden
-    // GEMM runs on the caller's stream s:
-    //   s: dlogits(A) | dX(A)      | dX(B) dW
-    //   x:            | dlogits(B) |
+    // 3. dlogits in place.  With grad_hidden wanted the rows split into up to
+    // four parts (multiples of 256 rows, the pair tile, at least 1024 rows each);
+    // part 0's pass runs alone on the caller's stream s, the others run one after
+    // another on a side stream x, each beside the grad_hidden GEMM of the part
+    // before it:
+    //   s: dlogits(0) | dX(0)      | dX(1)      | dX(2)      | dX(3) dW
+    //   x:            | dlogits(1) | dlogits(2) | dlogits(3) |
     // The GEMM keeps one CTA per SM busy on the tensor pipe and leaves issue
-    // slots, registers and memory bandwidth that the streaming pass fills.
-    // (Overlapping a pass with the logits GEMM instead slows both: that GEMM's
-    // epilogue needs the issue slots and the bandwidth itself.)
-    const int split = (want_dx && rows >= 512) ? ((rows / 2 + 255) / 256) * 256 : rows;
-    const int n_halves = split < rows ? 2 : 1;
-    const int lo_of[2] = {0, split}, hi_of[2] = {split, rows};
+    // slots, registers and memory bandwidth that the streaming pass fills, so
+    // only part 0's pass is exposed.  (Overlapping a pass with the logits GEMM
+    // instead slows both: that GEMM's epilogue needs the issue slots and the
+    // bandwidth itself.)
+    int n_halves = 1;  // number of row parts
+    int lo_of[kLmMaxParts] = {0}, hi_of[kLmMaxParts] = {rows};
+    if (want_dx) {
+      int parts = kLmMaxParts;
+      while (parts > 1 && rows / parts < 1024) --parts;
+      if (parts > 1) {
+        const int step = ((rows / parts + 255) / 256) * 256;
+        n_halves = 0;
+        for (int r = 0; r < rows && n_halves < kLmMaxParts; r += step) {
+          lo_of[n_halves] = r;
+          hi_of[n_halves] = (n_halves == kLmMaxParts - 1 || r + step > rows) ? rows : r + step;
+          if (hi_of[n_halves] == rows) {
+            ++n_halves;
+            break;
+          }
+          ++n_halves;
+        }
+      }
+    }
     SideStream* side = nullptr;
     std::unique_lock<std::mutex> side_lock;
-    if (n_halves == 2) {
+    if (n_halves > 1) {
       side = side_stream_of_current_device();
       if (side == nullptr) return HLM_ERR_LAUNCH;
       side_lock = std::unique_lock<std::mutex>(side->mu);
@@ -526,13 +545,15 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
     {
       int rc = dlogits(lo_of[0], hi_of[0], s);
       if (rc != HLM_OK) return rc;
-      if (n_halves == 2) {
-        if (cudaEventRecord(side->ev_lse[1], s) != cudaSuccess ||
-            cudaStreamWaitEvent(side->stream, side->ev_lse[1], 0) != cudaSuccess)
+      if (n_halves > 1) {
+        if (cudaEventRecord(side->ev_start, s) != cudaSuccess ||
+            cudaStreamWaitEvent(side->stream, side->ev_start, 0) != cudaSuccess)
           return HLM_ERR_LAUNCH;
-        rc = dlogits(lo_of[1], hi_of[1], side->stream);
-        if (rc != HLM_OK) return rc;
-        if (cudaEventRecord(side->ev_p[1], side->stream) != cudaSuccess) return HLM_ERR_LAUNCH;
+        for (int q = 1; q < n_halves; ++q) {
+          rc = dlogits(lo_of[q], hi_of[q], side->stream);
+          if (rc != HLM_OK) return rc;
+          if (cudaEventRecord(side->ev_p[q], side->stream) != cudaSuccess) return HLM_ERR_LAUNCH;
+        }
       }
     }
     // 4. grad_hidden[chunk] = P @ W, per half once its dlogits pass is done
@@ -557,8 +578,8 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
           map_p, map_p, map_p, map_w_n, p, ep, s, HLM_KERNEL_LM_DX);
     };
     for (int h = 0; h < n_halves; ++h) {
-      // the second half's rows are ready once the side stream's pass is done
-      if (h == 1 && cudaStreamWaitEvent(s, side->ev_p[1], 0) != cudaSuccess) return HLM_ERR_LAUNCH;
+      // part h's rows are ready once the side stream's pass over them is done
+      if (h > 0 && cudaStreamWaitEvent(s, side->ev_p[h], 0) != cudaSuccess) return HLM_ERR_LAUNCH;
       if (want_dx) {
         const int rc = grad_hidden_gemm(lo_of[h], hi_of[h]);
         if (rc != HLM_OK) return rc;
