@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "../../include/hlm_b200.h"
 
 #define HLM_DEVICE __device__ __forceinline__
@@ -25,6 +27,22 @@ namespace hlm {
 // device address of the word for the current device (defined in gemm.cu).
 // ---------------------------------------------------------------------------
 int* device_error_ptr();
+
+// One non-blocking side stream per device with a start event and kSideEvents
+// completion events, created on first use and kept for the process (runtime.cu).
+// Operators that run a memory-bound pass beside a GEMM fork it from the
+// caller's stream (record ev_start there, wait on the side stream) and join it
+// back (record ev_done[i] on the side stream, wait on the caller's), so each
+// call stays stream-ordered for the caller.  Hold `mu` for the whole
+// record/wait sequence of one call.
+constexpr int kSideEvents = 4;
+struct SideStream {
+  std::mutex mu;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev_start = nullptr;
+  cudaEvent_t ev_done[kSideEvents] = {};
+};
+SideStream* side_stream_of_current_device();
 
 // RAII scope around one kernel launch: counts the launch (hlm_launch_count)
 // and, while hlm_profile_begin is active for `kernel_id`, records the

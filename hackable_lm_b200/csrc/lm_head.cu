@@ -320,33 +320,8 @@ __global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restric
     dst[i] = __float2bfloat16_rn(src[i]);
 }
 
-// One side stream (non-blocking) and its events per device, created on first
-// use and kept for the process; the mutex keeps one call's record/wait
-// sequence from interleaving with another thread's.
 constexpr int kLmMaxParts = 4;  // row parts of a chunk's backward pipeline
-
-struct SideStream {
-  std::mutex mu;
-  cudaStream_t stream = nullptr;
-  cudaEvent_t ev_start = nullptr;                // the side stream's passes may start (caller stream)
-  cudaEvent_t ev_p[kLmMaxParts] = {};            // [q]: part q's dlogits done (side stream)
-};
-
-static SideStream* side_stream_of_current_device() {
-  static std::mutex init_mu;
-  static SideStream side[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(init_mu);
-  SideStream& ss = side[dev];
-  if (ss.stream == nullptr) {
-    if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
-    if (cudaEventCreateWithFlags(&ss.ev_start, cudaEventDisableTiming) != cudaSuccess) return nullptr;
-    for (int i = 0; i < kLmMaxParts; ++i)
-      if (cudaEventCreateWithFlags(&ss.ev_p[i], cudaEventDisableTiming) != cudaSuccess) return nullptr;
-  }
-  return &ss;
-}
+static_assert(kLmMaxParts <= kSideEvents, "one side-stream event per part");
 
 // ---------------------------------------------------------------------------
 // Workspace plan
@@ -552,7 +527,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
         for (int q = 1; q < n_halves; ++q) {
           rc = dlogits(lo_of[q], hi_of[q], side->stream);
           if (rc != HLM_OK) return rc;
-          if (cudaEventRecord(side->ev_p[q], side->stream) != cudaSuccess) return HLM_ERR_LAUNCH;
+          if (cudaEventRecord(side->ev_done[q], side->stream) != cudaSuccess) return HLM_ERR_LAUNCH;
         }
       }
     }
@@ -579,7 +554,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
     };
     for (int h = 0; h < n_halves; ++h) {
       // part h's rows are ready once the side stream's pass over them is done
-      if (h > 0 && cudaStreamWaitEvent(s, side->ev_p[h], 0) != cudaSuccess) return HLM_ERR_LAUNCH;
+      if (h > 0 && cudaStreamWaitEvent(s, side->ev_done[h], 0) != cudaSuccess) return HLM_ERR_LAUNCH;
       if (want_dx) {
         const int rc = grad_hidden_gemm(lo_of[h], hi_of[h]);
         if (rc != HLM_OK) return rc;

@@ -21,6 +21,22 @@ int* device_error_ptr() {
   return ptr[dev];
 }
 
+SideStream* side_stream_of_current_device() {
+  static std::mutex init_mu;
+  static SideStream side[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(init_mu);
+  SideStream& ss = side[dev];
+  if (ss.stream == nullptr) {
+    if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    if (cudaEventCreateWithFlags(&ss.ev_start, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+    for (int i = 0; i < kSideEvents; ++i)
+      if (cudaEventCreateWithFlags(&ss.ev_done[i], cudaEventDisableTiming) != cudaSuccess) return nullptr;
+  }
+  return &ss;
+}
+
 static std::atomic<uint64_t> g_launches{0};
 
 struct ProfileSlot {
