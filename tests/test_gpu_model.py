@@ -41,7 +41,7 @@ def test_b200_model_matches_torch_backend(cuda_device):
     _, lt = mt(x, y)
     lb.backward()
     lt.backward()
-    assert_loss_close(lb.detach(), lt.detach(), tol=5e-3)
+    assert_loss_close(lb.detach(), lt.detach())
     pt = dict(mt.named_parameters())
     used = torch.unique(x)
     for n, p in mb.named_parameters():
@@ -52,7 +52,9 @@ def test_b200_model_matches_torch_backend(cuda_device):
             # diluted by the empty ones
             assert torch.count_nonzero(got[~torch.isin(torch.arange(got.shape[0], device=got.device), used)]) == 0
             got, ref = got[used], ref[used]
-        # bf16 activations and weights through 2 layers against fp32 math
+        # bf16 activations and weights through 2 layers against fp32 math: elementwise 5e-2
+        # (the reference's own formulation in bf16 sits at the same level; the
+        # whole-model bar against the reference model is in test_gpu_model_reference.py)
         assert_bf16_close(got, ref, tol=5e-2, what=n)
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
