@@ -288,6 +288,18 @@ def _sdpa_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dropout_p: flo
 _FLASH_BACKENDS = ("flash_attn_2", "flash_attn_3", "flash_attn_4")
 
 
+def attention_b200(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, window_size: int | None) -> torch.Tensor:
+    """Causal attention on [B, T, H, 128] bf16 q, k, v (the QKV kernel's layout, no
+    transposes): the tcgen05 forward of hlm_attention_fwd, gradients through cuDNN's
+    SDPA backward.  ``window_size`` keys per query (the FlashAttention window
+    ``(window_size - 1, 0)``, kernels.py:839) or None for full causal."""
+    _cuda_only(q, "attention_b200")
+    if not ops.attention_supported(q, k, v):
+        raise RuntimeError("attention_b200: needs [B, T, H, 128] bf16 q, k, v with T a multiple of 128")
+    out, _ = ops.attention(q, k, v, 0 if window_size is None else int(window_size), 1.0 / math.sqrt(q.shape[-1]))
+    return out
+
+
 def scaled_dot_product_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dropout_p: float,
                                  is_causal: bool = True, attn_mask: torch.Tensor | None = None,
                                  block_mask: Any | None = None, window_size: int | None = None,

@@ -150,6 +150,11 @@ class AttentionCore(nn.Module):
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         seq_len = q.shape[1]
+        if (self.config.attention_backend == "b200" and (q.is_cuda or q.is_meta)
+                and self.config.dropout == 0.0 and ops.attention_supported(q, k, v)):
+            # tcgen05 forward on the [B, T, H, D] layout the QKV kernel wrote
+            window = self.window if self.window is not None and self.window < seq_len else None
+            return kernels.attention_b200(q, k, v, window)
         q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         if self.n_kv_head != self.n_head:
             rep = self.n_head // self.n_kv_head

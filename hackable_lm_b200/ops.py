@@ -737,6 +737,92 @@ def _scale_fake(x, scale):
 
 
 # ---------------------------------------------------------------------------
+# Attention core: tcgen05 forward, cuDNN backward  (reference: kernels.py:774-847)
+# ---------------------------------------------------------------------------
+def attention_supported(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> bool:
+    """[B, T, H, 128] bf16 q with k, v of the same heads, T a multiple of 128."""
+    return ((q.is_cuda or q.is_meta) and q.dtype == torch.bfloat16 and q.dim() == 4 and q.shape[-1] == 128
+            and q.shape[1] % 128 == 0 and k.shape == q.shape and v.shape == q.shape
+            and k.dtype == q.dtype and v.dtype == q.dtype)
+
+
+@torch.library.custom_op("hackable_lm_b200::attention", mutates_args=())
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, window: int,
+              scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """Causal attention on [B, T, H, 128] bf16 (keys with 0 <= t - k < window; window <= 0
+    means full causal).  Returns (out [B, T, H, 128], lse [B, H, T] fp32, natural log)."""
+    dev = _require_cuda(q, k, v)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    B, T, H, D = q.shape
+    Hk = k.shape[2]
+    out = torch.empty_like(q)
+    lse = torch.empty((B, H, T), dtype=torch.float32, device=dev)
+    check(_lib_().hlm_attention_fwd(_ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(lse), B, T, H, Hk, D,
+                                     int(window), float(scale), _stream(dev)), "hlm_attention_fwd")
+    return out, lse
+
+
+@attention.register_fake
+def _attention_fake(q, k, v, window, scale):
+    B, T, H, _ = q.shape
+    return torch.empty_like(q, memory_format=torch.contiguous_format), q.new_empty((B, H, T), dtype=torch.float32)
+
+
+def _window_bias(T: int, window: int, device) -> torch.Tensor:
+    pos = torch.arange(T, device=device)
+    dist = pos[:, None] - pos[None, :]
+    keep = (dist >= 0) & (dist < window)
+    return torch.zeros((T, T), dtype=torch.bfloat16, device=device).masked_fill(~keep, float("-inf"))
+
+
+@torch.library.custom_op("hackable_lm_b200::attention_backward", mutates_args=())
+def attention_backward(grad_out: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                       out: torch.Tensor, lse: torch.Tensor, window: int,
+                       scale: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients of attention() through cuDNN's SDPA backward kernel (library code, as
+    cuBLAS is for the plain GEMMs), fed with this forward's output and log-sum-exp."""
+    _require_cuda(grad_out, q, k, v, out, lse)
+    B, T, H, D = q.shape
+    # [B, H, T, D] views of the [B, T, H, D] tensors: q, k, v, out and grad_out share
+    # one stride pattern, as cuDNN's backward expects of tensors from its own forward;
+    # no dropout (seed / offset zero), dense (no cumulative sequence lengths), the
+    # log-sum-exp as its [B, H, T, 1] statistics
+    tr = lambda t: t.transpose(1, 2)  # noqa: E731
+    zero = torch.zeros((), dtype=torch.int64, device=q.device)
+    full = window <= 0 or window >= T
+    bias = None if full else _window_bias(T, window, q.device)[None, None].expand(B, H, T, T)
+    dq, dk, dv = torch.ops.aten._scaled_dot_product_cudnn_attention_backward(
+        tr(grad_out.contiguous()), tr(q), tr(k), tr(v), tr(out), lse.unsqueeze(-1), zero, zero, bias, None, None,
+        T, T, 0.0, full, scale=scale)
+    return dq.transpose(1, 2).contiguous(), dk.transpose(1, 2).contiguous(), dv.transpose(1, 2).contiguous()
+
+
+@attention_backward.register_fake
+def _attention_backward_fake(grad_out, q, k, v, out, lse, window, scale):
+    return torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+
+def _attention_setup(ctx, inputs, output):
+    q, k, v, window, scale = inputs
+    out, lse = output
+    ctx.save_for_backward(q, k, v, out, lse)
+    ctx.window = window
+    ctx.scale = scale
+    ctx.set_materialize_grads(False)
+
+
+def _attention_bwd(ctx, grad_out, grad_lse):
+    q, k, v, out, lse = ctx.saved_tensors
+    if grad_out is None:
+        return None, None, None, None, None
+    dq, dk, dv = attention_backward(grad_out, q, k, v, out, lse, ctx.window, ctx.scale)
+    return dq, dk, dv, None, None
+
+
+attention.register_autograd(_attention_bwd, setup_context=_attention_setup)
+
+
+# ---------------------------------------------------------------------------
 # Plain tcgen05 GEMM (building block, used by tests and the bench)
 # ---------------------------------------------------------------------------
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn_major: bool = False, b_mn_major: bool = False,

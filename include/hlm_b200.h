@@ -102,7 +102,8 @@ uint64_t hlm_launch_count(void);
 #define HLM_KERNEL_GATE_UP 16      /* gate_up GEMM + SwiGLU epilogue */
 #define HLM_KERNEL_SWIGLU_DOWN_BWD 17 /* down grad_h GEMM + SwiGLU backward epilogue */
 #define HLM_KERNEL_PROJ_NORM 18    /* o_proj / down GEMM + residual add + RMSNorm epilogue */
-#define HLM_KERNEL_MAX 19
+#define HLM_KERNEL_ATTN_FWD 19     /* attention forward (causal / sliding window) */
+#define HLM_KERNEL_MAX 20
 
 /* Start timing every launch of kernel `kernel_id`: launch i records
  * start_events[i] immediately before and stop_events[i] immediately after
@@ -322,6 +323,23 @@ int hlm_swiglu_down_bwd(const void* grad_y, const void* w_down, const void* gate
 int hlm_proj_residual_rms_norm_fwd(const void* y, const void* w, const void* residual, void* out,
                                    void* norm, int64_t M, int64_t K, int64_t N, float eps,
                                    void* stream);
+
+/* ------------------------------------------------------------------------
+ * Attention forward (causal, optional sliding window), head_dim 128
+ * ------------------------------------------------------------------------ */
+
+/* out[b,t,h,:] = softmax over keys k with 0 <= t - k < window of
+ * (q[b,t,h,:] . k[b,k,hk,:]) * scale, times v[b,k,hk,:]; hk = h / (H / Hk).
+ * lse[b,h,t] = log(sum_k exp(scale * q . k)) (natural log, fp32), the
+ * statistics a FlashAttention-style backward takes.  window <= 0 or >= T means
+ * full causal.  q, out [B, T, H, 128] and k, v [B, T, Hk, 128] bf16 contiguous
+ * (the layout hlm_qkv_rope_fwd writes).  Requires T % 128 == 0, H % Hk == 0,
+ * 16-byte aligned pointers.  Replaces the FlashAttention / SDPA call of
+ * kernels.scaled_dot_product_attention (kernels.py:774-847) with the window
+ * convention (window - 1, 0) of kernels.py:839. */
+int hlm_attention_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int64_t B,
+                      int64_t T, int64_t H, int64_t Hk, int64_t D, int64_t window, float scale,
+                      void* stream);
 
 /* ------------------------------------------------------------------------
  * Plain tcgen05 GEMM (building block; also used by tests)

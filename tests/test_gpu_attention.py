@@ -1,0 +1,117 @@
+"""Attention core: the tcgen05 forward (causal, sliding window) against an fp32
+explicit-softmax reference (the reference's "torch" attention, kernels.py:785-800,
+with the window mask of model.py:143-153), its log-sum-exp, and gradients through the
+cuDNN backward fed with this forward's output and statistics."""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from parity import assert_bf16_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(q, k, v, window):
+    """fp32 attention on [B, T, H, D] (k/v heads repeated for grouped queries)."""
+    B, T, H, D = q.shape
+    rep = H // k.shape[2]
+    qf = q.float().transpose(1, 2)
+    kf = k.float().repeat_interleave(rep, dim=2).transpose(1, 2)
+    vf = v.float().repeat_interleave(rep, dim=2).transpose(1, 2)
+    s = qf @ kf.transpose(-1, -2) / math.sqrt(D)
+    pos = torch.arange(T, device=q.device)
+    dist = pos[:, None] - pos[None, :]
+    keep = (dist >= 0) & (dist < (window if window > 0 else T))
+    s = s.masked_fill(~keep, float("-inf"))
+    lse = torch.logsumexp(s, -1)
+    return (torch.softmax(s, -1) @ vf).transpose(1, 2), lse
+
+
+def _inputs(B, T, H, Hk, seed, dev):
+    g = torch.Generator().manual_seed(seed)
+    mk = lambda h: torch.randn(B, T, h, 128, generator=g).to(torch.bfloat16).to(dev)  # noqa: E731
+    return mk(H), mk(Hk), mk(Hk)
+
+
+@pytest.mark.parametrize("B,T,H,Hk,window", [(2, 256, 2, 2, 0), (1, 512, 3, 3, 128), (2, 384, 2, 2, 200),
+                                             (1, 640, 4, 2, 0), (1, 1024, 1, 1, 512)])
+def test_attention_forward_vs_reference(B, T, H, Hk, window, cuda_device):
+    from hackable_lm_b200 import _lib, ops
+
+    _lib.clear_device_error()
+    q, k, v = _inputs(B, T, H, Hk, 0, cuda_device)
+    out, lse = ops.attention(q, k, v, window, 1.0 / math.sqrt(128))
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    ref, ref_lse = _ref(q, k, v, window)
+    assert_bf16_close(out, ref, what="out")
+    torch.testing.assert_close(lse, ref_lse, atol=2e-2, rtol=0, msg=lambda m: f"lse: {m}")
+
+
+def _sdpa_grads(q, k, v, go, window):
+    """Gradients of torch SDPA (cuDNN on B200) on the same bf16 inputs."""
+    T = q.shape[1]
+    qs, ks, vs = (t.clone().transpose(1, 2).requires_grad_(True) for t in (q, k, v))
+    mask = None
+    if window > 0:
+        pos = torch.arange(T, device=q.device)
+        dist = pos[:, None] - pos[None, :]
+        mask = (dist >= 0) & (dist < window)
+    out = torch.nn.functional.scaled_dot_product_attention(qs, ks, vs, attn_mask=mask, is_causal=mask is None)
+    out.backward(go.transpose(1, 2))
+    return [t.grad.transpose(1, 2) for t in (qs, ks, vs)]
+
+
+def _rel_l2(a, e):
+    a, e = a.double(), e.double()
+    return ((a - e).norm() / e.norm()).item()
+
+
+@pytest.mark.parametrize("T,window", [(256, 0), (512, 160)])
+def test_attention_backward_vs_reference(T, window, cuda_device):
+    """Gradients against fp32 autograd: relative L2 within 1e-2 and no further than 1.5x
+    (+2e-3) the error of torch SDPA's own bf16 gradients on the same inputs (the
+    elementwise bf16 bar does not hold for attention gradients even for SDPA itself)."""
+    from hackable_lm_b200 import ops
+    from parity import record
+
+    q, k, v = _inputs(2, T, 2, 2, 1, cuda_device)
+    g = torch.Generator().manual_seed(2)
+    go = torch.randn(2, T, 2, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    out, _ = ops.attention(qd, kd, vd, window, 1.0 / math.sqrt(128))
+    out.backward(go)
+    qr, kr, vr = (t.float().requires_grad_(True) for t in (q, k, v))
+    ref, _ = _ref(qr, kr, vr, window)
+    ref.backward(go.float())
+    sdpa = _sdpa_grads(q, k, v, go, window)
+    for name, got, exp, other in zip("qkv", (qd.grad, kd.grad, vd.grad), (qr.grad, kr.grad, vr.grad), sdpa):
+        e_ours, e_sdpa = _rel_l2(got, exp), _rel_l2(other, exp)
+        record(f"attention grad_{name}", rel_l2=e_ours, sdpa_rel_l2=e_sdpa)
+        assert e_ours <= 1e-2 and e_ours <= 1.5 * e_sdpa + 2e-3, (name, e_ours, e_sdpa)
+
+
+def test_attention_d12_shape_vs_sdpa(cuda_device):
+    """d12 shape [16, 2048, 6, 128], full causal: output, lse and gradients against
+    torch SDPA (cuDNN) on the same inputs."""
+    from hackable_lm_b200 import _lib, ops
+
+    _lib.clear_device_error()
+    q, k, v = _inputs(16, 2048, 6, 6, 3, cuda_device)
+    g = torch.Generator().manual_seed(4)
+    go = torch.randn(16, 2048, 6, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    out, lse = ops.attention(qd, kd, vd, 0, 1.0 / math.sqrt(128))
+    out.backward(go)
+    qs, ks, vs = (t.clone().transpose(1, 2).requires_grad_(True) for t in (q, k, v))
+    ref = torch.nn.functional.scaled_dot_product_attention(qs, ks, vs, is_causal=True)
+    ref.backward(go.transpose(1, 2))
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert_bf16_close(out, ref.transpose(1, 2).float(), what="out")
+    for name, a, e in zip("qkv", (qd.grad, kd.grad, vd.grad), (qs.grad, ks.grad, vs.grad)):
+        # both bf16; the backward kernel is the same, fed with either forward's statistics
+        assert _rel_l2(a, e.transpose(1, 2)) <= 1e-2, (name, _rel_l2(a, e.transpose(1, 2)))
