@@ -9,21 +9,23 @@
 // q, k, v, out are [B, T, H(k), 128] bf16 (the layout the QKV kernel writes), so
 // no transposes are needed; grouped-query heads map h -> h / (H / Hk).
 //
-// One CTA takes 128 query rows of one (b, h) and walks the key tiles of 128 from
-// the first the window reaches to the diagonal:
-//   warp 0  TMA producer: Q once, then K_j / V_j into a two-stage ring
-//   warp 1  TMEM owner and MMA issuer: S_j = Q K_j^T (M=N=K=128) into one of two
-//           TMEM score buffers, issued one tile ahead; O += P_j V_j into the TMEM
-//           output accumulator once the softmax warps have written P_j
-//   warps 2-5  softmax, one query row per thread: the score row into registers
-//           (one read of the score buffer), row max and exp2 of the scaled, masked
-//           scores against a reference max that moves only when a tile exceeds it
-//           by more than 8, running sum, P_j as bf16 into shared memory (the
-//           128-byte-swizzled K-major layout of the PV MMA's A operand), and, on a
-//           move, the output row rescaled in TMEM (tcgen05.ld / st) before PV_j; at
-//           the end out = O / l through TMA stores and lse = (m + log2 l) ln 2.
-// P_j is written only after PV_{j-1} has finished reading the single P buffer and
-// updating O; S_{j+1} runs on the tensor cores meanwhile.  Every wait is bounded.
+// One CTA takes two query tiles of 128 rows of one (b, h) (K and V are read once
+// for both) and walks the key tiles of 128 from the first the window reaches to
+// the last diagonal:
+//   warp 0  TMA producer: Q of both tiles, then K_t / V_t into two-stage rings
+//   warp 1  TMEM owner and MMA issuer: S_w = Q_w K_t^T (M=N=K=128) into tile w's
+//           score columns; O_w += P_w V_t with P_w read from tensor memory; per key
+//           tile PV_0, S_0(next), PV_1, S_1(next), so that one group's softmax
+//           runs while the tensor cores do the other group's two MMAs
+//   warps 4-7, 8-11  softmax of tile 0 / 1, one query row per thread: the score row
+//           into registers, row max and exp2 of the scaled, masked scores against
+//           a reference max that moves only when a tile exceeds it by more than 8,
+//           running sum, P as bf16 pairs over the first 64 score columns, and, on
+//           a move, the output row rescaled in TMEM (tcgen05.ld / st); at the end
+//           out = O / l through TMA stores and lse = (m + log2 l) ln 2.
+// S_w of the next key tile overwrites P_w, so it is issued after PV_w; MMAs of one
+// thread run in order, so the commit that publishes S_w also covers PV_w (its O
+// may be rescaled and its P overwritten).  Every wait is bounded.
 #include "gemm_sm100.cuh"
 
 namespace hlm {
@@ -41,10 +43,9 @@ HLM_DEVICE void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 HLM_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Waits on the per-tile chain (S -> softmax -> P -> PV -> next P) poll the barrier
-// with mbarrier.test_wait instead of suspending in try_wait: every one of them is
-// on the critical path, and a suspended thread resumes late (measured: 10x slower
-// with suspending waits).  Bounded like every other wait.
+// Waits poll the barrier with mbarrier.test_wait (with `backoff_ns` between polls
+// when given, for the single-thread roles).  Measured against suspending in
+// mbarrier.try_wait: no difference here.  Every wait is bounded.
 HLM_DEVICE bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -56,8 +57,6 @@ HLM_DEVICE bool mbar_test(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// `backoff_ns` > 0: sleep that long between polls, for the single-thread roles
-// (producer, MMA issuer) whose warps share a scheduler with a softmax warp.
 HLM_DEVICE bool mbar_poll(uint32_t bar, uint32_t parity, int* err, int code, uint32_t backoff_ns = 0) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
@@ -76,20 +75,42 @@ HLM_DEVICE bool warp_poll(uint32_t bar, uint32_t parity, int* err, int code, int
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-constexpr int kAttD = 128;         // head dim
-constexpr int kAttBQ = 128;        // query rows per CTA
-constexpr int kAttBK = 128;        // keys per tile
-constexpr int kAttStages = 2;      // K/V ring
-constexpr int kAttAtom = 128 * 128;  // one 128-row x 64-column bf16 swizzle atom (16 KB)
+// D[tmem] (+)= A[tmem] * B[smem]: the A operand (M = 128 rows, K = 16 bf16 per
+// instruction) read from tensor memory, two elements per 32-bit column.
+HLM_DEVICE void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
+constexpr int kAttD = 128;           // head dim
+constexpr int kAttBQ = 128;          // query rows per tile (two tiles per CTA)
+constexpr int kAttBK = 128;          // keys per tile
+constexpr int kAttAtom = 128 * 128;  // one 128-row x 64-column bf16 swizzle atom (16 KB)
+constexpr int kAttTile = 2 * kAttAtom;  // one 128 x 128 bf16 tile (32 KB)
+constexpr int kAttThreads = 384;
+// Register split: launched at kAttLaunchRegs per thread (384 x 168 = 64512, the
+// whole budget of one CTA per SM); the first warpgroup (TMA producer, MMA issuer,
+// two idle warps) gives registers back so that the two softmax warpgroups hold a
+// 128-entry score row and its packed P without spilling.  The shares add up to
+// the launch's total: 128 x 64 + 256 x 216 = 63488 <= 64512.  The host refuses to launch if
+// the compiled kernel's register count differs (a larger share would then wait
+// forever).
+constexpr int kAttLaunchRegs = 168;
+constexpr int kAttIssuerRegs = 64;
+constexpr int kAttSoftmaxRegs = 216;
+static_assert(128 * kAttIssuerRegs + 256 * kAttSoftmaxRegs <= kAttThreads * kAttLaunchRegs, "register split");
 struct AttSmem {
-  static constexpr int kQ = 0;                            // 2 atoms (d 0-63, 64-127)
-  static constexpr int kKV = kQ + 2 * kAttAtom;           // per stage: K 2 atoms, V 2 key blocks x 2 d blocks
-  static constexpr int kStageBytes = 4 * kAttAtom;        // 64 KB
-  static constexpr int kP = kKV + kAttStages * kStageBytes;  // 2 atoms (keys 0-63, 64-127)
-  static constexpr int kBars = kP + 2 * kAttAtom;
-  // barriers: q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full, pv_done
-  static constexpr int kNumBars = 11;
+  static constexpr int kQ = 0;                   // Q of the two query tiles (K-major atoms d 0-63, 64-127)
+  static constexpr int kK = kQ + 2 * kAttTile;   // K ring, two stages (K-major atoms)
+  static constexpr int kV = kK + 2 * kAttTile;   // V ring, two stages (MN-major 64 x 64 blocks)
+  static constexpr int kBars = kV + 2 * kAttTile;
+  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], o_done[2]
+  static constexpr int kNumBars = 15;
   static constexpr int kTmemSlot = kBars + kNumBars * 8;
   static constexpr int kBytes = kTmemSlot + 16;
 };
@@ -98,12 +119,13 @@ struct AttParams {
   int B, T, H, Hk;
   int window;       // keys with t - k < window (window >= T: full causal)
   int q_tiles;      // T / 128
+  int q_pairs;      // ceil(q_tiles / 2): work items per (b, h)
   float scale_log2; // softmax scale * log2(e)
   float* lse;       // [B, H, T]
   int* err;
 };
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kAttThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmVk, const __grid_constant__ CUtensorMap tmO,
                     const AttParams p) {
@@ -115,39 +137,47 @@ __global__ void __launch_bounds__(192, 1)
   const int lane = threadIdx.x & 31;
   int* err = p.err;
 
-  // work item: longest (highest) query tiles first
-  const int per_bh = p.q_tiles;
+  // work item: query tiles 2i and 2i + 1 of one (b, h), longest (highest) first
   const int item = static_cast<int>(blockIdx.x);
-  const int bh = item / per_bh;
-  const int qi = per_bh - 1 - (item - bh * per_bh);
+  const int bh = item / p.q_pairs;
+  const int pair = p.q_pairs - 1 - (item - bh * p.q_pairs);
   const int b = bh / p.H;
   const int h = bh - b * p.H;
   const int hk = h / (p.H / p.Hk);
-  const int q0 = qi * kAttBQ;
-  const int first_key = max(0, q0 - p.window + 1);
-  const int j0 = first_key / kAttBK;
-  const int nt = qi - j0 + 1;  // key tiles j0 .. qi
+  const int qt0 = 2 * pair;
+  const bool has1 = qt0 + 1 < p.q_tiles;
+  auto first_tile = [&](int q) { return max(0, q * kAttBQ - p.window + 1) / kAttBK; };
+  const int j_first = first_tile(qt0);                 // key tiles j_first .. j_last, t = j - j_first
+  const int j_last = has1 ? qt0 + 1 : qt0;
+  const int nkv = j_last - j_first + 1;
+  // query tile w covers key tiles t0(w) .. t1(w)
+  const int t_lo1 = first_tile(qt0 + 1) - j_first;
+  auto t0 = [&](int w) { return w == 0 ? 0 : t_lo1; };
+  auto t1 = [&](int w) { return qt0 + w - j_first; };
+  auto covers = [&](int w, int t) { return (w == 0 || has1) && t >= t0(w) && t <= t1(w); };
 
   const uint32_t bar0 = base + AttSmem::kBars;
   const uint32_t q_full = bar0;
-  auto kv_full = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto kv_empty = [&](int s) { return bar0 + 8u * (3 + s); };
-  auto s_full = [&](int s) { return bar0 + 8u * (5 + s); };
-  auto s_empty = [&](int s) { return bar0 + 8u * (7 + s); };
-  const uint32_t p_full = bar0 + 8u * 9;
-  const uint32_t pv_done = bar0 + 8u * 10;
+  auto k_full = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto k_empty = [&](int s) { return bar0 + 8u * (3 + s); };
+  auto v_full = [&](int s) { return bar0 + 8u * (5 + s); };
+  auto v_empty = [&](int s) { return bar0 + 8u * (7 + s); };
+  auto s_full = [&](int w) { return bar0 + 8u * (9 + w); };
+  auto p_full = [&](int w) { return bar0 + 8u * (11 + w); };
+  auto o_done = [&](int w) { return bar0 + 8u * (13 + w); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + AttSmem::kTmemSlot);
 
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(kv_full(s), 1);
-      mbar_init(kv_empty(s), 1);
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
       mbar_init(s_full(s), 1);
-      mbar_init(s_empty(s), 4);  // the four softmax warps
+      mbar_init(p_full(s), 4);  // the four warps of that tile's softmax group
+      mbar_init(o_done(s), 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
     fence_mbar_init();
     prefetch_tensormap(&tmQ);
     prefetch_tensormap(&tmK);
@@ -162,128 +192,166 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
-  const uint32_t t_s[2] = {tmem_base, tmem_base + 128u};
-  const uint32_t t_o = tmem_base + 256u;
-  const int row_q = b * p.T + q0;         // first query row in the [B*T, H*D] view
-  const int row_k0 = b * p.T;             // first key row of this sequence
+  // TMEM columns: S of tile 0 / 1 (P overwrites its first 64 columns as bf16
+  // pairs), then O of tile 0 / 1
+  auto t_s = [&](int w) { return tmem_base + 128u * static_cast<uint32_t>(w); };
+  auto t_o = [&](int w) { return tmem_base + 256u + 128u * static_cast<uint32_t>(w); };
+  const int row_k0 = b * p.T;  // first key row of this sequence in the [B*T, H*D] view
 
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttIssuerRegs));
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(q_full, 2 * kAttAtom);
-      tma_load_2d(base + AttSmem::kQ, &tmQ, h * kAttD, row_q, q_full);
-      tma_load_2d(base + AttSmem::kQ + kAttAtom, &tmQ, h * kAttD + 64, row_q, q_full);
-      uint32_t armed = 0, armed_par = 0;
-      for (int t = 0; t < nt && ok; ++t) {
+      const int nq = has1 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, static_cast<uint32_t>(nq * kAttTile));
+      for (int w = 0; w < nq; ++w) {
+        const int row_q = row_k0 + (qt0 + w) * kAttBQ;
+        const uint32_t dst = base + AttSmem::kQ + static_cast<uint32_t>(w * kAttTile);
+        tma_load_2d(dst, &tmQ, h * kAttD, row_q, q_full);
+        tma_load_2d(dst + kAttAtom, &tmQ, h * kAttD + 64, row_q, q_full);
+      }
+      int k_issued = 0, v_issued = 0;  // key tiles whose K / V loads were issued
+      for (int t = 0; t < nkv && ok; ++t) {
         const int s = t & 1;
-        if (t >= 2 && !mbar_poll(kv_empty(s), static_cast<uint32_t>(((t >> 1) - 1) & 1), err, kDevErrTimeoutEmpty, 64)) {
+        const uint32_t par = static_cast<uint32_t>(((t >> 1) - 1) & 1);
+        const int key0 = row_k0 + (j_first + t) * kAttBK;
+        if (t >= 2 && !mbar_poll(k_empty(s), par, err, kDevErrTimeoutEmpty, 64)) {
           ok = false;
           break;
         }
-        const uint32_t st = base + AttSmem::kKV + static_cast<uint32_t>(s * AttSmem::kStageBytes);
-        const int key0 = row_k0 + (j0 + t) * kAttBK;
-        mbar_arrive_expect_tx(kv_full(s), AttSmem::kStageBytes);
-        armed |= 1u << s;
-        armed_par = (armed_par & ~(1u << s)) | ((static_cast<uint32_t>(t >> 1) & 1u) << s);
-        // K: two K-major atoms [128 keys][64 d]
-        tma_load_2d(st, &tmK, hk * kAttD, key0, kv_full(s));
-        tma_load_2d(st + kAttAtom, &tmK, hk * kAttD + 64, key0, kv_full(s));
+        const uint32_t kd = base + AttSmem::kK + static_cast<uint32_t>(s * kAttTile);
+        mbar_arrive_expect_tx(k_full(s), kAttTile);
+        tma_load_2d(kd, &tmK, hk * kAttD, key0, k_full(s));
+        tma_load_2d(kd + kAttAtom, &tmK, hk * kAttD + 64, key0, k_full(s));
+        k_issued = t + 1;
+        if (t >= 2 && !mbar_poll(v_empty(s), par, err, kDevErrTimeoutEmpty, 64)) {
+          ok = false;
+          break;
+        }
         // V: MN-major blocks [64 keys][64 d]: key block kb at 16 KB, d block i at 8 KB
+        const uint32_t vd = base + AttSmem::kV + static_cast<uint32_t>(s * kAttTile);
+        mbar_arrive_expect_tx(v_full(s), kAttTile);
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
           for (int i = 0; i < 2; ++i)
-            tma_load_2d(st + 2 * kAttAtom + static_cast<uint32_t>(kb * 16384 + i * 8192), &tmVk, hk * kAttD + 64 * i,
-                        key0 + 64 * kb, kv_full(s));
+            tma_load_2d(vd + static_cast<uint32_t>(kb * 16384 + i * 8192), &tmVk, hk * kAttD + 64 * i,
+                        key0 + 64 * kb, v_full(s));
+        v_issued = t + 1;
       }
-      for (int s = 0; s < 2; ++s)
-        if (armed & (1u << s)) mbar_wait_drain(kv_full(s), (armed_par >> s) & 1u, err);
+      // every load issued has landed before the CTA can exit (after an error too)
       mbar_wait_drain(q_full, 0u, err);
+      for (int t = max(0, k_issued - 2); t < k_issued; ++t)
+        mbar_wait_drain(k_full(t & 1), static_cast<uint32_t>((t >> 1) & 1), err);
+      for (int t = max(0, v_issued - 2); t < v_issued; ++t)
+        mbar_wait_drain(v_full(t & 1), static_cast<uint32_t>((t >> 1) & 1), err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, 128, false, true);
       bool ok = mbar_poll(q_full, 0u, err, kDevErrTimeoutFull, 32);
-      auto issue_s = [&](int t) -> bool {
-        const int s = t & 1;
-        if (!mbar_poll(kv_full(s), static_cast<uint32_t>((t >> 1) & 1), err, kDevErrTimeoutFull, 32)) return false;
-        if (t >= 2 && !mbar_poll(s_empty(s), static_cast<uint32_t>(((t >> 1) - 1) & 1), err, kDevErrTimeoutTmemEmpty, 32))
-          return false;
-        tc_fence_after();
-        const uint32_t sk = base + AttSmem::kKV + static_cast<uint32_t>(s * AttSmem::kStageBytes);
+      // The K and V tiles an MMA pair needs are waited for before the P it waits
+      // on (they have almost always landed by then), so that nothing but the
+      // softmax's arrival stands between one group's P and its two MMAs.
+      int k_ready = -1, v_ready = -1;  // highest key tile whose K / V has been seen landed
+      auto wait_k = [&](int t) -> bool {
+        if (t <= k_ready) return true;
+        k_ready = t;
+        return mbar_poll(k_full(t & 1), static_cast<uint32_t>((t >> 1) & 1), err, kDevErrTimeoutFull, 32);
+      };
+      auto wait_v = [&](int t) -> bool {
+        if (t <= v_ready) return true;
+        v_ready = t;
+        return mbar_poll(v_full(t & 1), static_cast<uint32_t>((t >> 1) & 1), err, kDevErrTimeoutFull, 32);
+      };
+      // S_w = Q_w K_t^T into tile w's score columns (K_t has landed)
+      auto issue_s = [&](int w, int t) {
+        const uint32_t qa = base + AttSmem::kQ + static_cast<uint32_t>(w * kAttTile);
+        const uint32_t kb = base + AttSmem::kK + static_cast<uint32_t>((t & 1) * kAttTile);
 #pragma unroll
         for (int kk = 0; kk < kAttD / kUmmaK; ++kk) {
           const uint32_t atom = static_cast<uint32_t>((kk >> 2) * kAttAtom + (kk & 3) * 32);
-          tc_mma_f16(t_s[s], make_sw128_desc(base + AttSmem::kQ + atom, 16u, 1024u),
-                     make_sw128_desc(sk + atom, 16u, 1024u), idesc_s, kk > 0 ? 1u : 0u);
+          tc_mma_f16(t_s(w), make_sw128_desc(qa + atom, 16u, 1024u), make_sw128_desc(kb + atom, 16u, 1024u),
+                     idesc_s, kk > 0 ? 1u : 0u);
         }
-        tc_commit(s_full(s));
-        return true;
+        tc_commit(s_full(w));
       };
-      if (ok) ok = issue_s(0);
-      for (int t = 0; t < nt && ok; ++t) {
-        if (t + 1 < nt && !(ok = issue_s(t + 1))) break;
-        if (!mbar_poll(p_full, static_cast<uint32_t>(t & 1), err, kDevErrTimeoutFull, 32)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const int s = t & 1;
-        const uint32_t sv = base + AttSmem::kKV + static_cast<uint32_t>(s * AttSmem::kStageBytes + 2 * kAttAtom);
+      // O_w += P_w V_t, P_w read from tensor memory (P_w and V_t ready)
+      auto issue_pv = [&](int w, int t) {
+        const int u = t - t0(w);
+        const uint32_t vb = base + AttSmem::kV + static_cast<uint32_t>((t & 1) * kAttTile);
 #pragma unroll
-        for (int kk = 0; kk < kAttBK / kUmmaK; ++kk) {
-          // A = P [128 q][128 keys] K-major (two 64-key atoms); B = V MN-major
-          const uint32_t pa = base + AttSmem::kP + static_cast<uint32_t>((kk >> 2) * kAttAtom + (kk & 3) * 32);
-          const uint32_t vb = sv + static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 2048);
-          tc_mma_f16(t_o, make_sw128_desc(pa, 16u, 1024u), make_sw128_desc(vb, 8192u, 1024u), idesc_o,
-                     (t > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kAttBK / kUmmaK; ++kk)
+          tc_mma_f16_ts(t_o(w), t_s(w) + static_cast<uint32_t>(kk * 8),
+                        make_sw128_desc(vb + static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 2048), 8192u, 1024u),
+                        idesc_o, (u > 0 || kk > 0) ? 1u : 0u);
+        if (t == t1(w)) tc_commit(o_done(w));
+      };
+      for (int w = 0; w < 2 && ok; ++w)
+        if (covers(w, 0)) {
+          if (!(ok = wait_k(0))) break;
+          tc_fence_after();
+          issue_s(w, 0);
         }
-        tc_commit(kv_empty(s));
-        tc_commit(pv_done);
+      if (ok) tc_commit(k_empty(0));
+      // per key tile: PV_0, S_0 of the next tile, PV_1, S_1 of the next tile, so
+      // that one group's softmax overlaps the other's two MMAs
+      for (int t = 0; t < nkv && ok; ++t) {
+        for (int w = 0; w < 2 && ok; ++w) {
+          const bool pv = covers(w, t), next = covers(w, t + 1);
+          if (pv && !(ok = wait_v(t))) break;
+          if (next && !(ok = wait_k(t + 1))) break;
+          if (pv && !(ok = mbar_poll(p_full(w), static_cast<uint32_t>((t - t0(w)) & 1), err,
+                                                     kDevErrTimeoutFull, 32)))
+            break;
+          if (!pv && !next) continue;
+          tc_fence_after();
+          if (pv) issue_pv(w, t);
+          if (next) issue_s(w, t + 1);
+        }
+        if (!ok) break;
+        if (t + 1 < nkv) tc_commit(k_empty((t + 1) & 1));
+        tc_commit(v_empty(t & 1));
       }
     }
+  }
   } else {
-    // ------------------------------------------------------------ softmax warps
-    const int quad = warp & 3;
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAttSoftmaxRegs));
+    // ------------------------------------------------------------ softmax groups
+    const int w = (warp - 4) >> 2;   // query tile of this group
+    const int quad = warp & 3;       // TMEM lane quarter this warp may access
     const int r = quad * 32 + lane;  // row of the tile
+    const int q0 = (qt0 + w) * kAttBQ;
     const int qpos = q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const float sc = p.scale_log2;
     float m = -INFINITY, l = 0.0f;  // reference max (log2 domain) and row sum
-    bool ok = true;
-    for (int t = 0; t < nt; ++t) {
-      const int s = t & 1;
-      const int key0 = (j0 + t) * kAttBK;
-      if (!warp_poll(s_full(s), static_cast<uint32_t>((t >> 1) & 1), err, kDevErrTimeoutTmemFull, lane)) {
+    bool ok = w == 0 || has1;
+    const int nu = ok ? t1(w) - t0(w) + 1 : 0;
+    for (int u = 0; u < nu; ++u) {
+      const int key0 = (j_first + t0(w) + u) * kAttBK;
+      if (!warp_poll(s_full(w), static_cast<uint32_t>(u & 1), err, kDevErrTimeoutTmemFull, lane)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // the whole score row into registers (four loads, one wait), which frees the
-      // score buffer for S_{t+2}
       const bool full_tile = key0 + kAttBK - 1 <= q0 && q0 + kAttBQ - 1 - key0 < p.window;
       uint32_t x[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_s[s] + lane_off + static_cast<uint32_t>(c * 32), x[c]);
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_s(w) + lane_off + static_cast<uint32_t>(c * 32), x[c]);
       tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty(s));
-      // scaled, masked scores (log2 domain) and their row max (eight independent
-      // partial maxima / sums: the reductions would otherwise be one dependent chain)
+      // row max of the raw scores (masked keys -inf), eight independent partial
+      // maxima / sums: the reductions would otherwise be one dependent chain
       float mxp[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
+      for (int u8 = 0; u8 < 8; ++u8) mxp[u8] = -INFINITY;
       if (full_tile) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float v = __uint_as_float(x[c][i]) * sc;
-            x[c][i] = __float_as_uint(v);
-            mxp[i & 7] = fmaxf(mxp[i & 7], v);
-          }
+          for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(x[c][i]));
       } else {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -291,13 +359,13 @@ __global__ void __launch_bounds__(192, 1)
           for (int i = 0; i < 32; ++i) {
             const int key = key0 + c * 32 + i;
             const bool valid = key <= qpos && qpos - key < p.window;
-            const float v = valid ? __uint_as_float(x[c][i]) * sc : -INFINITY;
+            const float v = valid ? __uint_as_float(x[c][i]) : -INFINITY;
             x[c][i] = __float_as_uint(v);
             mxp[i & 7] = fmaxf(mxp[i & 7], v);
           }
       }
-      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      const float mx = sc * fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                  fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       // The exponent's reference max moves only when this tile exceeds it by more
       // than 8 (so p <= 256): softmax does not depend on the reference, and O and l
       // are rescaled (alpha) only on those moves.  alpha is 0 when the row had no
@@ -307,90 +375,84 @@ __global__ void __launch_bounds__(192, 1)
         alpha = ex2_ftz(m - mx);
         m = mx;
       }
-      const float m_use = m == -INFINITY ? 0.0f : m;
-      // p = exp2(s - m) packed to bf16 for the PV MMA; the row sum (and so the
-      // log-sum-exp the backward recomputes P from) takes the fp32 values
-      uint32_t pk[64];
+      const float neg_m = m == -INFINITY ? 0.0f : -m;
+      // p = exp2(s * scale - m) packed to bf16 pairs for the PV MMA, written over
+      // the first 64 score columns in two halves (S has been read; PV of the
+      // previous tile, which read the previous P there, completed before this S
+      // did); the row sum (and so the log-sum-exp the backward recomputes P from)
+      // takes the fp32 values
       float rsp[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) rsp[u] = 0.0f;
+      for (int u8 = 0; u8 < 8; ++u8) rsp[u8] = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float e0 = ex2_ftz(__uint_as_float(x[c][i]) - m_use);
-          const float e1 = ex2_ftz(__uint_as_float(x[c][i + 1]) - m_use);
-          rsp[(i >> 1) & 7] += e0 + e1;
-          pk[c * 16 + i / 2] = pack_bf16x2(e0, e1);
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * hf + cc;
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float e0 = ex2_ftz(fmaf(__uint_as_float(x[c][i]), sc, neg_m));
+            const float e1 = ex2_ftz(fmaf(__uint_as_float(x[c][i + 1]), sc, neg_m));
+            rsp[(i >> 1) & 7] += e0 + e1;
+            pk[cc * 16 + i / 2] = pack_bf16x2(e0, e1);
+          }
         }
+        tmem_st_32x32b_x32(t_s(w) + lane_off + static_cast<uint32_t>(32 * hf), pk);
       }
       const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       l = alpha * l + rs;
-      // PV_{t-1} done: the P buffer is free and O holds the sum up to t-1
-      if (t > 0) {
-        if (!warp_poll(pv_done, static_cast<uint32_t>((t - 1) & 1), err, kDevErrTimeoutTmemFull, lane)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
-      // P row -> shared memory: key chunk k (8 keys = 16 bytes) of atom k / 8
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const uint32_t addr = base + AttSmem::kP + static_cast<uint32_t>((k >> 3) * kAttAtom + r * 128 +
-                                                                          (((k & 7) ^ (r & 7)) << 4));
-        st_shared_v4(addr, make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]));
-      }
-      // rescale the output row when the reference max moved (O is overwritten at t == 0)
-      if (t > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+      // rescale the output row when the reference max moved (O is overwritten at
+      // u == 0); PV of the previous tile has completed (it precedes this S)
+      if (u > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
         uint32_t o[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_o + lane_off + static_cast<uint32_t>(c * 32), o[c]);
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_o(w) + lane_off + static_cast<uint32_t>(c * 32), o[c]);
         tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * alpha);
-          tmem_st_32x32b_x32(t_o + lane_off + static_cast<uint32_t>(c * 32), o[c]);
+          tmem_st_32x32b_x32(t_o(w) + lane_off + static_cast<uint32_t>(c * 32), o[c]);
         }
-        tmem_st_wait();
       }
-      fence_proxy_async_smem();  // P visible to the MMA (async proxy)
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(p_full(w));
     }
-    if (ok && warp_poll(pv_done, static_cast<uint32_t>((nt - 1) & 1), err, kDevErrTimeoutTmemFull, lane)) {
+    if (ok && warp_poll(o_done(w), 0u, err, kDevErrTimeoutTmemFull, lane)) {
       tc_fence_after();
       const float inv_l = 1.0f / l;
-      // out row -> the Q buffer (free: every S MMA has completed), as two 32 x 64
-      // boxes per warp per 64-column half, then TMA stores
-      const uint32_t stage = base + AttSmem::kQ + static_cast<uint32_t>(quad * 2 * 32 * 128);
+      // out row -> this tile's Q buffer (free: its last S MMA completed before the
+      // last PV did), as two 32 x 64 boxes per warp per 64-column half, then TMA stores
+      const uint32_t stage =
+          base + AttSmem::kQ + static_cast<uint32_t>(w * kAttTile + quad * 2 * 32 * 128);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
-        tmem_ld_32x32b_x32(t_o + lane_off + static_cast<uint32_t>(c * 32), o);
+        tmem_ld_32x32b_x32(t_o(w) + lane_off + static_cast<uint32_t>(c * 32), o);
         tmem_ld_wait();
         const uint32_t box = stage + static_cast<uint32_t>((c >> 1) * 32 * 128);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int ch = (c & 1) * 4 + q;
-          const uint4 w = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l),
-                                     pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l),
-                                     pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l),
-                                     pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l));
-          st_shared_v4(box + static_cast<uint32_t>(lane * 128 + ((ch ^ (lane & 7)) << 4)), w);
+          const uint4 v4 = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l),
+                                      pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l),
+                                      pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l),
+                                      pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l));
+          st_shared_v4(box + static_cast<uint32_t>(lane * 128 + ((ch ^ (lane & 7)) << 4)), v4);
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
+      const int row_q = row_k0 + q0;
       if (lane == 0) {
         tma_store_2d(&tmO, h * kAttD, row_q + quad * 32, stage);
         tma_store_2d(&tmO, h * kAttD + 64, row_q + quad * 32, stage + 32 * 128);
         bulk_commit_group();
       }
-      if (qpos < p.T)
-        p.lse[(static_cast<int64_t>(b) * p.H + h) * p.T + qpos] = (m + __log2f(l)) * 0.6931471805599453f;
+      p.lse[(static_cast<int64_t>(b) * p.H + h) * p.T + qpos] = (m + __log2f(l)) * 0.6931471805599453f;
       if (lane == 0) bulk_wait_group_all();
       __syncwarp();
     }
@@ -431,6 +493,7 @@ extern "C" int hlm_attention_fwd(const void* q, const void* k, const void* v, vo
   p.Hk = static_cast<int>(Hk);
   p.window = window <= 0 || window >= T ? static_cast<int>(T) : static_cast<int>(window);
   p.q_tiles = static_cast<int>(T / kAttBQ);
+  p.q_pairs = (p.q_tiles + 1) / 2;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.lse = lse;
   p.err = device_error_ptr();
@@ -439,11 +502,16 @@ extern "C" int hlm_attention_fwd(const void* q, const void* k, const void* v, vo
   static_assert(AttSmem::kBytes + 1024 <= 232448, "shared memory budget exceeded");
   if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return HLM_ERR_LAUNCH;
+  static const int compiled_regs = [] {
+    cudaFuncAttributes attr{};
+    return cudaFuncGetAttributes(&attr, attn_fwd_kernel) == cudaSuccess ? attr.numRegs : -1;
+  }();
+  if (compiled_regs != kAttLaunchRegs) return HLM_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t grid = B * H * (T / kAttBQ);
+  const int64_t grid = B * H * p.q_pairs;
   {
     LaunchScope scope(HLM_KERNEL_ATTN_FWD, s);
-    attn_fwd_kernel<<<static_cast<unsigned>(grid), 192, smem, s>>>(mq, mk, mv, mo, p);
+    attn_fwd_kernel<<<static_cast<unsigned>(grid), kAttThreads, smem, s>>>(mq, mk, mv, mo, p);
   }
   return launch_status();
 }

@@ -37,7 +37,8 @@ def _inputs(B, T, H, Hk, seed, dev):
 
 
 @pytest.mark.parametrize("B,T,H,Hk,window", [(2, 256, 2, 2, 0), (1, 512, 3, 3, 128), (2, 384, 2, 2, 200),
-                                             (1, 640, 4, 2, 0), (1, 1024, 1, 1, 512)])
+                                             (1, 640, 4, 2, 0), (1, 1024, 1, 1, 512), (1, 128, 1, 1, 0),
+                                             (1, 256, 1, 1, 1)])
 def test_attention_forward_vs_reference(B, T, H, Hk, window, cuda_device):
     from hackable_lm_b200 import _lib, ops
 
