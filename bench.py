@@ -570,8 +570,7 @@ def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
     name starts with it (small, known launch sequences for ncu captures: one
     untimed pass over the copies, then `iters` timed calls)."""
     from hackable_lm_b200 import ops
-
-    import oracle
+    from hackable_lm_b200.model import RotaryEmbedding
 
     peaks, _ = load_peaks()
 
@@ -636,9 +635,9 @@ def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
     B, T, H, D = 8, 2048, 6, 128
     q = torch.randn(B, T, H, D, generator=g).to(torch.bfloat16).to(device)
     k = torch.randn(B, T, H, D, generator=g).to(torch.bfloat16).to(device)
-    cos, sin = oracle.rope_tables(D, T, 10_000.0, 0.25, dtype=torch.bfloat16)
-    cos = cos.transpose(1, 2).to(device)
-    sin = sin.transpose(1, 2).to(device)
+    c1, s1 = RotaryEmbedding(D, 10_000.0, 0.25)(T, device, torch.bfloat16)
+    cos = c1.transpose(1, 2).contiguous()
+    sin = s1.transpose(1, 2).contiguous()
     dq = torch.randn_like(q)
     dk = torch.randn_like(k)
     hbm("qk_norm_rope_fwd [8,2048,6,128]", lambda a, b: ops.qk_norm_rope(a, b, cos, sin, 1e-6), (q, k),
@@ -647,8 +646,6 @@ def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
         lambda a, b, c, d: ops.qk_norm_rope_backward(a, b, c, d, cos, sin, 1e-6), (q, k, dq, dk), 150_994_944)
     xq = torch.randn(8, 2048, 768, generator=g).to(torch.bfloat16).to(device)
     wq = (torch.randn(2304, 768, generator=g) * 0.02).to(torch.bfloat16).to(device)
-    c1, s1 = oracle.rope_tables(D, T, 10_000.0, 0.25, dtype=torch.bfloat16)
-    c1, s1 = c1.to(device), s1.to(device)
     tensor("qkv_rope_fwd X[16384,768] W[2304,768]", lambda a: ops.qkv_rope(a, wq, c1, s1, 6, 6, 1e-6), (xq,),
            57_982_058_496)
     xg = torch.randn(32768, 768, generator=g).to(torch.bfloat16).to(device)
@@ -691,6 +688,20 @@ def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
             lambda a, b: ops.swiglu_down_grad(a, wdn, b, out=outd), (gyd, gud),
             2 * (32768 * 768 + 2 * 32768 * 4096 + 768 * 2048))
         del gyd, gud, wdn, outd
+    # attention forward (tcgen05 kernel) at the d12 shape, full causal, beside torch SDPA (cuDNN) on
+    # the same inputs: tensor-bound, 4*D FLOPs per causal (query, key) pair (Q K^T and P V)
+    key = "attention_fwd [16,2048,6,128] causal"
+    if want(key):
+        qa, ka, va = (torch.randn(16, 2048, 6, 128, generator=g).to(torch.bfloat16).to(device) for _ in range(3))
+        flop = 4 * 128 * (2048 * 2049 // 2) * 16 * 6
+        ms = timed(lambda a, b, c: ops.attention(a, b, c, 0, 128 ** -0.5), (qa, ka, va), nbytes_of((qa, ka, va)))
+        ms_ref = timed(lambda a, b, c: torch.nn.functional.scaled_dot_product_attention(
+            a.transpose(1, 2), b.transpose(1, 2), c.transpose(1, 2), is_causal=True), (qa, ka, va),
+            nbytes_of((qa, ka, va)))
+        tf = flop / (ms / 1e3) / 1e12
+        res[key] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1), "flop": flop,
+                    "frac_of_bf16": round(tf / peaks["bf16_tflops"], 4), "sdpa_us": round(ms_ref * 1e3, 2)}
+        del qa, ka, va
     if not want("qkv_rope_bwd"):
         return res
     qo, ko, vo, rs = ops.qkv_rope(xq, wq, c1, s1, 6, 6, 1e-6)
