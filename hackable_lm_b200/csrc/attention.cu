@@ -137,10 +137,13 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   const int lane = threadIdx.x & 31;
   int* err = p.err;
 
-  // work item: query tiles 2i and 2i + 1 of one (b, h), longest (highest) first
+  // work item: query tiles 2i and 2i + 1 of one (b, h).  Items are ordered by
+  // pair index over the whole grid, highest (longest under the causal mask)
+  // first, so that CTAs start longest-first and the last wave holds short items.
   const int item = static_cast<int>(blockIdx.x);
-  const int bh = item / p.q_pairs;
-  const int pair = p.q_pairs - 1 - (item - bh * p.q_pairs);
+  const int n_bh = p.B * p.H;
+  const int pair = p.q_pairs - 1 - item / n_bh;
+  const int bh = item - (item / n_bh) * n_bh;
   const int b = bh / p.H;
   const int h = bh - b * p.H;
   const int hk = h / (p.H / p.Hk);
