@@ -97,20 +97,20 @@ constexpr int kAttThreads = 384;
 // whole budget of one CTA per SM); the first warpgroup (TMA producer, MMA issuer,
 // two idle warps) gives registers back so that the two softmax warpgroups hold a
 // 128-entry score row and its packed P without spilling.  The shares add up to
-// the launch's total: 128 x 64 + 256 x 216 = 63488 <= 64512.  The host refuses to launch if
+// the launch's total: 128 x 56 + 256 x 224 = 64512.  The host refuses to launch if
 // the compiled kernel's register count differs (a larger share would then wait
 // forever).
 constexpr int kAttLaunchRegs = 168;
-constexpr int kAttIssuerRegs = 64;
-constexpr int kAttSoftmaxRegs = 216;
+constexpr int kAttIssuerRegs = 56;
+constexpr int kAttSoftmaxRegs = 224;
 static_assert(128 * kAttIssuerRegs + 256 * kAttSoftmaxRegs <= kAttThreads * kAttLaunchRegs, "register split");
 struct AttSmem {
   static constexpr int kQ = 0;                   // Q of the two query tiles (K-major atoms d 0-63, 64-127)
   static constexpr int kK = kQ + 2 * kAttTile;   // K ring, two stages (K-major atoms)
   static constexpr int kV = kK + 2 * kAttTile;   // V ring, two stages (MN-major 64 x 64 blocks)
   static constexpr int kBars = kV + 2 * kAttTile;
-  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], o_done[2]
-  static constexpr int kNumBars = 15;
+  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_lo[2], p_hi[2], o_done[2]
+  static constexpr int kNumBars = 17;
   static constexpr int kTmemSlot = kBars + kNumBars * 8;
   static constexpr int kBytes = kTmemSlot + 16;
 };
@@ -166,8 +166,10 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   auto v_full = [&](int s) { return bar0 + 8u * (5 + s); };
   auto v_empty = [&](int s) { return bar0 + 8u * (7 + s); };
   auto s_full = [&](int w) { return bar0 + 8u * (9 + w); };
-  auto p_full = [&](int w) { return bar0 + 8u * (11 + w); };
-  auto o_done = [&](int w) { return bar0 + 8u * (13 + w); };
+  // P of keys 0-63 / 64-127 of tile w's current key tile written
+  auto p_lo = [&](int w) { return bar0 + 8u * (11 + w); };
+  auto p_hi = [&](int w) { return bar0 + 8u * (13 + w); };
+  auto o_done = [&](int w) { return bar0 + 8u * (15 + w); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + AttSmem::kTmemSlot);
 
   if (warp == 0 && lane == 0) {
@@ -178,7 +180,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
       mbar_init(s_full(s), 1);
-      mbar_init(p_full(s), 4);  // the four warps of that tile's softmax group
+      mbar_init(p_lo(s), 4);  // the four warps of that tile's softmax group
+      mbar_init(p_hi(s), 4);
       mbar_init(o_done(s), 1);
     }
     fence_mbar_init();
@@ -281,16 +284,19 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         }
         tc_commit(s_full(w));
       };
-      // O_w += P_w V_t, P_w read from tensor memory (P_w and V_t ready)
-      auto issue_pv = [&](int w, int t) {
+      // O_w += P_w V_t over keys 32 * half .. + 63, P_w read from tensor memory
+      // (that half of P_w and V_t ready)
+      auto issue_pv = [&](int w, int t, int half) {
         const int u = t - t0(w);
         const uint32_t vb = base + AttSmem::kV + static_cast<uint32_t>((t & 1) * kAttTile);
 #pragma unroll
-        for (int kk = 0; kk < kAttBK / kUmmaK; ++kk)
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int kk = 4 * half + k4;
           tc_mma_f16_ts(t_o(w), t_s(w) + static_cast<uint32_t>(kk * 8),
                         make_sw128_desc(vb + static_cast<uint32_t>((kk >> 2) * 16384 + (kk & 3) * 2048), 8192u, 1024u),
                         idesc_o, (u > 0 || kk > 0) ? 1u : 0u);
-        if (t == t1(w)) tc_commit(o_done(w));
+        }
+        if (half == 1 && t == t1(w)) tc_commit(o_done(w));
       };
       for (int w = 0; w < 2 && ok; ++w)
         if (covers(w, 0)) {
@@ -306,12 +312,19 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           const bool pv = covers(w, t), next = covers(w, t + 1);
           if (pv && !(ok = wait_v(t))) break;
           if (next && !(ok = wait_k(t + 1))) break;
-          if (pv && !(ok = mbar_poll(p_full(w), static_cast<uint32_t>((t - t0(w)) & 1), err,
-                                                     kDevErrTimeoutFull, 32)))
-            break;
           if (!pv && !next) continue;
-          tc_fence_after();
-          if (pv) issue_pv(w, t);
+          if (pv) {
+            // the first half of P is ready while the softmax still computes the second
+            const uint32_t par = static_cast<uint32_t>((t - t0(w)) & 1);
+            if (!(ok = mbar_poll(p_lo(w), par, err, kDevErrTimeoutFull, 32))) break;
+            tc_fence_after();
+            issue_pv(w, t, 0);
+            if (!(ok = mbar_poll(p_hi(w), par, err, kDevErrTimeoutFull, 32))) break;
+            tc_fence_after();
+            issue_pv(w, t, 1);
+          } else {
+            tc_fence_after();
+          }
           if (next) issue_s(w, t + 1);
         }
         if (!ok) break;
@@ -341,23 +354,48 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       }
       tc_fence_after();
       const bool full_tile = key0 + kAttBK - 1 <= q0 && q0 + kAttBQ - 1 - key0 < p.window;
+      // the score row in two halves: the second half's load is in flight while
+      // the first half's row max is taken.  Row max of the raw scores (masked keys
+      // -inf), eight independent partial maxima / sums: the reductions would
+      // otherwise be one dependent chain
       uint32_t x[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_s(w) + lane_off + static_cast<uint32_t>(c * 32), x[c]);
-      tmem_ld_wait();
-      // row max of the raw scores (masked keys -inf), eight independent partial
-      // maxima / sums: the reductions would otherwise be one dependent chain
       float mxp[8];
 #pragma unroll
       for (int u8 = 0; u8 < 8; ++u8) mxp[u8] = -INFINITY;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+        for (int c = 2 * hf; c < 2 * hf + 2; ++c)
+          tmem_ld_32x32b_x32(t_s(w) + lane_off + static_cast<uint32_t>(c * 32), x[c]);
+        if (hf == 1) {
+          if (full_tile) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(x[c][i]));
+          } else {
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int key = key0 + c * 32 + i;
+                const bool valid = key <= qpos && qpos - key < p.window;
+                const float v = valid ? __uint_as_float(x[c][i]) : -INFINITY;
+                x[c][i] = __float_as_uint(v);
+                mxp[i & 7] = fmaxf(mxp[i & 7], v);
+              }
+          }
+        }
+        tmem_ld_wait();
+      }
       if (full_tile) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 2; c < 4; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(x[c][i]));
       } else {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 2; c < 4; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int key = key0 + c * 32 + i;
@@ -379,10 +417,25 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         m = mx;
       }
       const float neg_m = m == -INFINITY ? 0.0f : -m;
+      // rescale the output row when the reference max moved (O is overwritten at
+      // u == 0), before either half of P is published; PV of the previous tile has
+      // completed (it precedes this S)
+      if (u > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(t_o(w) + lane_off + static_cast<uint32_t>(c * 32), o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x32(t_o(w) + lane_off + static_cast<uint32_t>(c * 32), o);
+        }
+      }
       // p = exp2(s * scale - m) packed to bf16 pairs for the PV MMA, written over
-      // the first 64 score columns in two halves (S has been read; PV of the
-      // previous tile, which read the previous P there, completed before this S
-      // did); the row sum (and so the log-sum-exp the backward recomputes P from)
+      // the first 64 score columns (S has been read; PV of the previous tile, which
+      // read the previous P there, completed before this S did) and published per
+      // half of the keys, so the PV MMA of the first half overlaps the exp2 of the
+      // second; the row sum (and so the log-sum-exp the backward recomputes P from)
       // takes the fp32 values
       float rsp[8];
 #pragma unroll
@@ -402,27 +455,13 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           }
         }
         tmem_st_32x32b_x32(t_s(w) + lane_off + static_cast<uint32_t>(32 * hf), pk);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(hf == 0 ? p_lo(w) : p_hi(w));
       }
       const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
       l = alpha * l + rs;
-      // rescale the output row when the reference max moved (O is overwritten at
-      // u == 0); PV of the previous tile has completed (it precedes this S)
-      if (u > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-        uint32_t o[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_o(w) + lane_off + static_cast<uint32_t>(c * 32), o[c]);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c][i] = __float_as_uint(__uint_as_float(o[c][i]) * alpha);
-          tmem_st_32x32b_x32(t_o(w) + lane_off + static_cast<uint32_t>(c * 32), o[c]);
-        }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full(w));
     }
     if (ok && warp_poll(o_done(w), 0u, err, kDevErrTimeoutTmemFull, lane)) {
       tc_fence_after();
