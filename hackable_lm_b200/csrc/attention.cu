@@ -87,6 +87,101 @@ HLM_DEVICE void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
       : "memory");
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic, one instruction for two lanes of
+// work; each element rounds exactly as the scalar instruction) and the
+// three-input max: the softmax is bound by its instruction issue, not by the
+// exp2 unit.
+HLM_DEVICE uint64_t f32x2_splat(float v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
+  return r;
+}
+// (d0, d1) = (a0, a1) * b2 + c2
+HLM_DEVICE void fma_f32x2(float& d0, float& d1, float a0, float a1, uint64_t b2, uint64_t c2) {
+  asm("{\n\t.reg .b64 ra, rd;\n\tmov.b64 ra, {%2, %3};\n\t"
+      "fma.rn.f32x2 rd, ra, %4, %5;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "l"(b2), "l"(c2));
+}
+// (s0, s1) += (a0, a1)
+HLM_DEVICE void add_f32x2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n\t.reg .b64 rs, ra;\n\tmov.b64 rs, {%0, %1};\n\tmov.b64 ra, {%2, %3};\n\t"
+      "add.rn.f32x2 rs, rs, ra;\n\tmov.b64 {%0, %1}, rs;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
+}
+HLM_DEVICE float max3_f32(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// Keys of one 32-key chunk outside the causal window [qpos - window + 1, qpos]
+// set to -inf (tiles the mask reaches only).
+HLM_DEVICE void att_chunk_mask(uint32_t (&xc)[32], int key0c, int qpos, int window) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int k = key0c + i;
+    if (!(k <= qpos && qpos - k < window)) xc[i] = __float_as_uint(-INFINITY);
+  }
+}
+// Max of the raw scores of one 32-key chunk into eight partial maxima (the
+// reduction would otherwise be one dependent chain).
+HLM_DEVICE void att_chunk_max(const uint32_t (&xc)[32], float (&mxp)[8]) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 2)
+    mxp[(i >> 1) & 7] = max3_f32(mxp[(i >> 1) & 7], __uint_as_float(xc[i]), __uint_as_float(xc[i + 1]));
+}
+HLM_DEVICE float att_max_of(const float (&mxp)[8]) {
+  return fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])), fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+}
+// Max of the raw scores over `n` 32-key chunks starting at x[c0].
+template <int C0, int N>
+HLM_DEVICE float att_chunks_max(const uint32_t (&x)[4][32]) {
+  float mxp[8];
+#pragma unroll
+  for (int u8 = 0; u8 < 8; ++u8) mxp[u8] = -INFINITY;
+#pragma unroll
+  for (int c = C0; c < C0 + N; ++c) att_chunk_max(x[c], mxp);
+  return att_max_of(mxp);
+}
+// p = 2^(x * sc + nm) over one 32-key chunk: bf16 pairs for the PV MMA into
+// pk[0..15] and the fp32 sums into r0 / r1 (the log-sum-exp the backward
+// recomputes P from takes the fp32 values).
+HLM_DEVICE void att_exp_chunk(const uint32_t (&xc)[32], uint64_t sc2, uint64_t nm2, uint32_t* pk, float (&r0)[4],
+                              float (&r1)[4]) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    float a0, a1;
+    fma_f32x2(a0, a1, __uint_as_float(xc[i]), __uint_as_float(xc[i + 1]), sc2, nm2);
+    const float e0 = ex2_ftz(a0);
+    const float e1 = ex2_ftz(a1);
+    add_f32x2(r0[(i >> 1) & 3], r1[(i >> 1) & 3], e0, e1);
+    pk[i / 2] = pack_bf16x2(e0, e1);
+  }
+}
+// Two chunks (one key half): P pairs into pk[0..31], returns the fp32 sum.
+HLM_DEVICE float att_exp_half(const uint32_t (&xa)[32], const uint32_t (&xb)[32], uint64_t sc2, uint64_t nm2,
+                              uint32_t (&pk)[32]) {
+  float r0[4], r1[4];
+#pragma unroll
+  for (int u4 = 0; u4 < 4; ++u4) r0[u4] = r1[u4] = 0.0f;
+  att_exp_chunk(xa, sc2, nm2, pk, r0, r1);
+  att_exp_chunk(xb, sc2, nm2, pk + 16, r0, r1);
+  return ((r0[0] + r1[0]) + (r0[1] + r1[1])) + ((r0[2] + r1[2]) + (r0[3] + r1[3]));
+}
+// One thread's output row in tensor memory scaled by alpha.
+HLM_DEVICE void att_rescale_o(uint32_t taddr, float alpha) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t o[32];
+    tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), o);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+    tmem_st_32x32b_x32(taddr + static_cast<uint32_t>(c * 32), o);
+  }
+}
+
 constexpr int kAttD = 128;           // head dim
 constexpr int kAttBQ = 128;          // query rows per tile (two tiles per CTA)
 constexpr int kAttBK = 128;          // keys per tile
@@ -109,8 +204,9 @@ struct AttSmem {
   static constexpr int kK = kQ + 2 * kAttTile;   // K ring, two stages (K-major atoms)
   static constexpr int kV = kK + 2 * kAttTile;   // V ring, two stages (MN-major 64 x 64 blocks)
   static constexpr int kBars = kV + 2 * kAttTile;
-  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_lo[2], p_hi[2], o_done[2]
-  static constexpr int kNumBars = 17;
+  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_lo[2], p_hi[2], o_done[2],
+  // pvlo_done[2]
+  static constexpr int kNumBars = 19;
   static constexpr int kTmemSlot = kBars + kNumBars * 8;
   static constexpr int kBytes = kTmemSlot + 16;
 };
@@ -170,6 +266,8 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   auto p_lo = [&](int w) { return bar0 + 8u * (11 + w); };
   auto p_hi = [&](int w) { return bar0 + 8u * (13 + w); };
   auto o_done = [&](int w) { return bar0 + 8u * (15 + w); };
+  // PV of the first key half of tile w's current key tile completed
+  auto pvlo_done = [&](int w) { return bar0 + 8u * (17 + w); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + AttSmem::kTmemSlot);
 
   if (warp == 0 && lane == 0) {
@@ -183,6 +281,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       mbar_init(p_lo(s), 4);  // the four warps of that tile's softmax group
       mbar_init(p_hi(s), 4);
       mbar_init(o_done(s), 1);
+      mbar_init(pvlo_done(s), 1);
     }
     fence_mbar_init();
     prefetch_tensormap(&tmQ);
@@ -319,6 +418,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
             if (!(ok = mbar_poll(p_lo(w), par, err, kDevErrTimeoutFull, 32))) break;
             tc_fence_after();
             issue_pv(w, t, 0);
+            tc_commit(pvlo_done(w));
             if (!(ok = mbar_poll(p_hi(w), par, err, kDevErrTimeoutFull, 32))) break;
             tc_fence_after();
             issue_pv(w, t, 1);
@@ -354,114 +454,77 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       }
       tc_fence_after();
       const bool full_tile = key0 + kAttBK - 1 <= q0 && q0 + kAttBQ - 1 - key0 < p.window;
-      // the score row in two halves: the second half's load is in flight while
-      // the first half's row max is taken.  Row max of the raw scores (masked keys
-      // -inf), eight independent partial maxima / sums: the reductions would
-      // otherwise be one dependent chain
       uint32_t x[4][32];
-      float mxp[8];
 #pragma unroll
-      for (int u8 = 0; u8 < 8; ++u8) mxp[u8] = -INFINITY;
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_s(w) + lane_off + static_cast<uint32_t>(c * 32), x[c]);
+      tmem_ld_wait();
+      if (!full_tile) {
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-#pragma unroll
-        for (int c = 2 * hf; c < 2 * hf + 2; ++c)
-          tmem_ld_32x32b_x32(t_s(w) + lane_off + static_cast<uint32_t>(c * 32), x[c]);
-        if (hf == 1) {
-          if (full_tile) {
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-#pragma unroll
-              for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(x[c][i]));
-          } else {
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int key = key0 + c * 32 + i;
-                const bool valid = key <= qpos && qpos - key < p.window;
-                const float v = valid ? __uint_as_float(x[c][i]) : -INFINITY;
-                x[c][i] = __float_as_uint(v);
-                mxp[i & 7] = fmaxf(mxp[i & 7], v);
-              }
-          }
+        for (int c = 0; c < 4; ++c) att_chunk_mask(x[c], key0 + 32 * c, qpos, p.window);
+      }
+      const uint64_t sc2 = f32x2_splat(sc);
+      // P over the first 64 score columns (S has been read; PV of the previous
+      // tile, which read the previous P there, completed before this S did),
+      // published per key half so that the PV MMA of the first half overlaps the
+      // exp2 of the second.
+      //
+      // Fast path, once every row of the warp has a finite reference m: the
+      // exponents s * scale - m take m as it stands, with no row max (the max is
+      // a large share of the softmax's instructions).  Softmax does not depend on
+      // the reference; it only has to keep the terms in range, so a half whose sum
+      // exceeds 2^64 (or is inf / NaN) in any row of the warp goes the exact way.
+      // Exact path (each row's first key tile, or a first half out of range): the
+      // row max moves the reference when it exceeds it by more than 8, and O and l
+      // are rescaled (alpha) on those moves; alpha is 0 when the row had no valid
+      // key before (its O row and l are 0).
+      float alpha = 1.0f, rs0 = 0.0f;
+      uint32_t pk[32];
+      bool exact = u == 0 || __any_sync(0xffffffffu, m == -INFINITY);
+      if (!exact) {
+        rs0 = att_exp_half(x[0], x[1], sc2, f32x2_splat(-m), pk);
+        exact = __any_sync(0xffffffffu, !(rs0 <= 0x1p64f));
+      }
+      if (exact) {
+        const float mx = sc * att_chunks_max<0, 4>(x);
+        if (mx > m + 8.0f) {
+          alpha = ex2_ftz(m - mx);
+          m = mx;
         }
-        tmem_ld_wait();
+        // O is overwritten at u == 0; PV of the previous tile has completed
+        if (u > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) att_rescale_o(t_o(w) + lane_off, alpha);
+        rs0 = att_exp_half(x[0], x[1], sc2, f32x2_splat(m == -INFINITY ? 0.0f : -m), pk);
       }
-      if (full_tile) {
-#pragma unroll
-        for (int c = 2; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(x[c][i]));
-      } else {
-#pragma unroll
-        for (int c = 2; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int key = key0 + c * 32 + i;
-            const bool valid = key <= qpos && qpos - key < p.window;
-            const float v = valid ? __uint_as_float(x[c][i]) : -INFINITY;
-            x[c][i] = __float_as_uint(v);
-            mxp[i & 7] = fmaxf(mxp[i & 7], v);
-          }
-      }
-      const float mx = sc * fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                                  fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-      // The exponent's reference max moves only when this tile exceeds it by more
-      // than 8 (so p <= 256): softmax does not depend on the reference, and O and l
-      // are rescaled (alpha) only on those moves.  alpha is 0 when the row had no
-      // valid key before (its O row and l are 0).
-      float alpha = 1.0f;
-      if (mx > m + 8.0f) {
-        alpha = ex2_ftz(m - mx);
+      tmem_st_32x32b_x32(t_s(w) + lane_off, pk);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_lo(w));
+      float rs1 = att_exp_half(x[2], x[3], sc2, f32x2_splat(m == -INFINITY ? 0.0f : -m), pk);
+      if (__any_sync(0xffffffffu, !(rs1 <= 0x1p64f))) {
+        // A term of the second half left the range after the first half was
+        // published (only on the fast path: the exact path keeps terms <= 2^8).
+        // Move the reference to the second half's max (the first half's terms, in
+        // range under the old reference, only shrink), wait for the first half's
+        // PV, rescale O and the first half's sum, and recompute the second half.
+        const float mx = fmaxf(m, sc * att_chunks_max<2, 2>(x));
+        const float a2 = ex2_ftz(m - mx);
         m = mx;
-      }
-      const float neg_m = m == -INFINITY ? 0.0f : -m;
-      // rescale the output row when the reference max moved (O is overwritten at
-      // u == 0), before either half of P is published; PV of the previous tile has
-      // completed (it precedes this S)
-      if (u > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(t_o(w) + lane_off + static_cast<uint32_t>(c * 32), o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st_32x32b_x32(t_o(w) + lane_off + static_cast<uint32_t>(c * 32), o);
+        if (!warp_poll(pvlo_done(w), static_cast<uint32_t>(u & 1), err, kDevErrTimeoutTmemFull, lane)) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        att_rescale_o(t_o(w) + lane_off, a2);
+        alpha *= a2;
+        rs0 *= a2;
+        rs1 = att_exp_half(x[2], x[3], sc2, f32x2_splat(-m), pk);
       }
-      // p = exp2(s * scale - m) packed to bf16 pairs for the PV MMA, written over
-      // the first 64 score columns (S has been read; PV of the previous tile, which
-      // read the previous P there, completed before this S did) and published per
-      // half of the keys, so the PV MMA of the first half overlaps the exp2 of the
-      // second; the row sum (and so the log-sum-exp the backward recomputes P from)
-      // takes the fp32 values
-      float rsp[8];
-#pragma unroll
-      for (int u8 = 0; u8 < 8; ++u8) rsp[u8] = 0.0f;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = 2 * hf + cc;
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float e0 = ex2_ftz(fmaf(__uint_as_float(x[c][i]), sc, neg_m));
-            const float e1 = ex2_ftz(fmaf(__uint_as_float(x[c][i + 1]), sc, neg_m));
-            rsp[(i >> 1) & 7] += e0 + e1;
-            pk[cc * 16 + i / 2] = pack_bf16x2(e0, e1);
-          }
-        }
-        tmem_st_32x32b_x32(t_s(w) + lane_off + static_cast<uint32_t>(32 * hf), pk);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(hf == 0 ? p_lo(w) : p_hi(w));
-      }
-      const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-      l = alpha * l + rs;
+      tmem_st_32x32b_x32(t_s(w) + lane_off + 32u, pk);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_hi(w));
+      l = alpha * l + (rs0 + rs1);
     }
     if (ok && warp_poll(o_done(w), 0u, err, kDevErrTimeoutTmemFull, lane)) {
       tc_fence_after();

@@ -52,6 +52,34 @@ def test_attention_forward_vs_reference(B, T, H, Hk, window, cuda_device):
     torch.testing.assert_close(lse, ref_lse, atol=2e-2, rtol=0, msg=lambda m: f"lse: {m}")
 
 
+@pytest.mark.parametrize("slope,window", [(0.9, 0), (1.2, 0), (3.0, 0), (0.9, 300)])
+def test_attention_forward_rising_scores(slope, window, cuda_device):
+    """Scores that rise along the keys by `slope` (log2 units per key): every key tile
+    exceeds the running reference max by far more than the in-range bound, so the
+    kernel leaves its fast path (no row max) for the exact path (first half out of
+    range) or moves the reference after publishing the first half (second half out
+    of range), and must still match the fp32 softmax."""
+    from hackable_lm_b200 import _lib, ops
+
+    _lib.clear_device_error()
+    B, T, H = 1, 512, 2
+    beta = slope * math.sqrt(128) / math.log2(math.e)
+    q = torch.zeros(B, T, H, 128)
+    q[..., 0] = 1.0
+    k = torch.zeros(B, T, H, 128)
+    k[..., 0] = beta * torch.arange(T, dtype=torch.float32)[None, :, None]
+    g = torch.Generator().manual_seed(5)
+    v = torch.randn(B, T, H, 128, generator=g)
+    q, k, v = (t.to(torch.bfloat16).to(cuda_device) for t in (q, k, v))
+    out, lse = ops.attention(q, k, v, window, 1.0 / math.sqrt(128))
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
+    ref, ref_lse = _ref(q, k, v, window)
+    assert_bf16_close(out, ref, what="out")
+    torch.testing.assert_close(lse, ref_lse, atol=2e-2, rtol=1e-5, msg=lambda m: f"lse: {m}")
+
+
 def _sdpa_grads(q, k, v, go, window):
     """Gradients of torch SDPA (cuDNN on B200) on the same bf16 inputs."""
     T = q.shape[1]
