@@ -12,7 +12,7 @@
 // One CTA takes two query tiles of 128 rows of one (b, h) (K and V are read once
 // for both) and walks the key tiles of 128 from the first the window reaches to
 // the last diagonal:
-//   warp 0  TMA producer: Q of both tiles, then K_t / V_t into two-stage rings
+//   warp 0  TMA producer: Q of both tiles, then K_t / V_t through a five-slot ring
 //   warp 1  TMEM owner and MMA issuer: S_w = Q_w K_t^T (M=N=K=128) into tile w's
 //           score columns; O_w += P_w V_t with P_w read from tensor memory; per key
 //           tile PV_0, S_0(next), PV_1, S_1(next), so that one group's softmax
@@ -43,9 +43,10 @@ HLM_DEVICE void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 HLM_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Waits poll the barrier with mbarrier.test_wait (with `backoff_ns` between polls
-// when given, for the single-thread roles).  Measured against suspending in
-// mbarrier.try_wait: no difference here.  Every wait is bounded.
+// Waits poll the barrier with mbarrier.test_wait, back to back: every wait of the
+// MMA issuer is on the critical chain, and a __nanosleep between polls (even of
+// 32 ns) measured about 1000 cycles late.  Suspending in mbarrier.try_wait
+// measured the same as polling.  Every wait is bounded.
 HLM_DEVICE bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -57,11 +58,10 @@ HLM_DEVICE bool mbar_test(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-HLM_DEVICE bool mbar_poll(uint32_t bar, uint32_t parity, int* err, int code, uint32_t backoff_ns = 0) {
+HLM_DEVICE bool mbar_poll(uint32_t bar, uint32_t parity, int* err, int code) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (backoff_ns) __nanosleep(backoff_ns);
     if (mbar_test(bar, parity)) return true;
     if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
       record_error(err, code);
@@ -201,12 +201,14 @@ constexpr int kAttSoftmaxRegs = 224;
 static_assert(128 * kAttIssuerRegs + 256 * kAttSoftmaxRegs <= kAttThreads * kAttLaunchRegs, "register split");
 struct AttSmem {
   static constexpr int kQ = 0;                   // Q of the two query tiles (K-major atoms d 0-63, 64-127)
-  static constexpr int kK = kQ + 2 * kAttTile;   // K ring, two stages (K-major atoms)
-  static constexpr int kV = kK + 2 * kAttTile;   // V ring, two stages (MN-major 64 x 64 blocks)
-  static constexpr int kBars = kV + 2 * kAttTile;
-  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_lo[2], p_hi[2], o_done[2],
-  // pvlo_done[2]
-  static constexpr int kNumBars = 19;
+  // one ring of tile slots for K_0, V_0, K_1, V_1, ... (item n = 2t for K_t,
+  // 2t + 1 for V_t, in slot n % kSlots): K as two K-major atoms, V as MN-major
+  // 64 x 64 blocks
+  static constexpr int kSlots = 5;
+  static constexpr int kKV = kQ + 2 * kAttTile;
+  static constexpr int kBars = kKV + kSlots * kAttTile;
+  // q_full, kv_full[5], kv_empty[5], s_full[2], p_lo[2], p_hi[2], o_done[2], pvlo_done[2]
+  static constexpr int kNumBars = 1 + 2 * kSlots + 10;
   static constexpr int kTmemSlot = kBars + kNumBars * 8;
   static constexpr int kBytes = kTmemSlot + 16;
 };
@@ -257,26 +259,29 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 
   const uint32_t bar0 = base + AttSmem::kBars;
   const uint32_t q_full = bar0;
-  auto k_full = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto k_empty = [&](int s) { return bar0 + 8u * (3 + s); };
-  auto v_full = [&](int s) { return bar0 + 8u * (5 + s); };
-  auto v_empty = [&](int s) { return bar0 + 8u * (7 + s); };
-  auto s_full = [&](int w) { return bar0 + 8u * (9 + w); };
+  // ring item n: its slot, its landing barrier and the barrier that frees it
+  constexpr int kS = AttSmem::kSlots;
+  auto slot_addr = [&](int n) { return base + AttSmem::kKV + static_cast<uint32_t>((n % kS) * kAttTile); };
+  auto kv_full = [&](int n) { return bar0 + 8u * static_cast<uint32_t>(1 + n % kS); };
+  auto kv_empty = [&](int n) { return bar0 + 8u * static_cast<uint32_t>(1 + kS + n % kS); };
+  auto kv_par = [&](int n) { return static_cast<uint32_t>((n / kS) & 1); };  // phase of item n's use
+  constexpr int kB = 1 + 2 * kS;
+  auto s_full = [&](int w) { return bar0 + 8u * (kB + w); };
   // P of keys 0-63 / 64-127 of tile w's current key tile written
-  auto p_lo = [&](int w) { return bar0 + 8u * (11 + w); };
-  auto p_hi = [&](int w) { return bar0 + 8u * (13 + w); };
-  auto o_done = [&](int w) { return bar0 + 8u * (15 + w); };
+  auto p_lo = [&](int w) { return bar0 + 8u * (kB + 2 + w); };
+  auto p_hi = [&](int w) { return bar0 + 8u * (kB + 4 + w); };
+  auto o_done = [&](int w) { return bar0 + 8u * (kB + 6 + w); };
   // PV of the first key half of tile w's current key tile completed
-  auto pvlo_done = [&](int w) { return bar0 + 8u * (17 + w); };
+  auto pvlo_done = [&](int w) { return bar0 + 8u * (kB + 8 + w); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + AttSmem::kTmemSlot);
 
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
+    for (int n = 0; n < kS; ++n) {
+      mbar_init(kv_full(n), 1);
+      mbar_init(kv_empty(n), 1);
+    }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(k_full(s), 1);
-      mbar_init(k_empty(s), 1);
-      mbar_init(v_full(s), 1);
-      mbar_init(v_empty(s), 1);
       mbar_init(s_full(s), 1);
       mbar_init(p_lo(s), 4);  // the four warps of that tile's softmax group
       mbar_init(p_hi(s), 4);
@@ -316,47 +321,39 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         tma_load_2d(dst, &tmQ, h * kAttD, row_q, q_full);
         tma_load_2d(dst + kAttAtom, &tmQ, h * kAttD + 64, row_q, q_full);
       }
-      int k_issued = 0, v_issued = 0;  // key tiles whose K / V loads were issued
-      for (int t = 0; t < nkv && ok; ++t) {
-        const int s = t & 1;
-        const uint32_t par = static_cast<uint32_t>(((t >> 1) - 1) & 1);
-        const int key0 = row_k0 + (j_first + t) * kAttBK;
-        if (t >= 2 && !mbar_poll(k_empty(s), par, err, kDevErrTimeoutEmpty, 64)) {
+      // K_t and V_t into the ring, running up to kSlots items ahead of the MMAs
+      int issued = 0;  // ring items whose loads were issued
+      for (int n = 0; n < 2 * nkv && ok; ++n) {
+        if (n >= kS && !mbar_poll(kv_empty(n), kv_par(n) ^ 1u, err, kDevErrTimeoutEmpty)) {
           ok = false;
           break;
         }
-        const uint32_t kd = base + AttSmem::kK + static_cast<uint32_t>(s * kAttTile);
-        mbar_arrive_expect_tx(k_full(s), kAttTile);
-        tma_load_2d(kd, &tmK, hk * kAttD, key0, k_full(s));
-        tma_load_2d(kd + kAttAtom, &tmK, hk * kAttD + 64, key0, k_full(s));
-        k_issued = t + 1;
-        if (t >= 2 && !mbar_poll(v_empty(s), par, err, kDevErrTimeoutEmpty, 64)) {
-          ok = false;
-          break;
+        const int key0 = row_k0 + (j_first + (n >> 1)) * kAttBK;
+        const uint32_t dst = slot_addr(n);
+        mbar_arrive_expect_tx(kv_full(n), kAttTile);
+        if ((n & 1) == 0) {
+          tma_load_2d(dst, &tmK, hk * kAttD, key0, kv_full(n));
+          tma_load_2d(dst + kAttAtom, &tmK, hk * kAttD + 64, key0, kv_full(n));
+        } else {
+          // V: MN-major blocks [64 keys][64 d]: key block kb at 16 KB, d block i at 8 KB
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+              tma_load_2d(dst + static_cast<uint32_t>(kb * 16384 + i * 8192), &tmVk, hk * kAttD + 64 * i,
+                          key0 + 64 * kb, kv_full(n));
         }
-        // V: MN-major blocks [64 keys][64 d]: key block kb at 16 KB, d block i at 8 KB
-        const uint32_t vd = base + AttSmem::kV + static_cast<uint32_t>(s * kAttTile);
-        mbar_arrive_expect_tx(v_full(s), kAttTile);
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-          for (int i = 0; i < 2; ++i)
-            tma_load_2d(vd + static_cast<uint32_t>(kb * 16384 + i * 8192), &tmVk, hk * kAttD + 64 * i,
-                        key0 + 64 * kb, v_full(s));
-        v_issued = t + 1;
+        issued = n + 1;
       }
       // every load issued has landed before the CTA can exit (after an error too)
       mbar_wait_drain(q_full, 0u, err);
-      for (int t = max(0, k_issued - 2); t < k_issued; ++t)
-        mbar_wait_drain(k_full(t & 1), static_cast<uint32_t>((t >> 1) & 1), err);
-      for (int t = max(0, v_issued - 2); t < v_issued; ++t)
-        mbar_wait_drain(v_full(t & 1), static_cast<uint32_t>((t >> 1) & 1), err);
+      for (int n = max(0, issued - kS); n < issued; ++n) mbar_wait_drain(kv_full(n), kv_par(n), err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, 128, false, true);
-      bool ok = mbar_poll(q_full, 0u, err, kDevErrTimeoutFull, 32);
+      bool ok = mbar_poll(q_full, 0u, err, kDevErrTimeoutFull);
       // The K and V tiles an MMA pair needs are waited for before the P it waits
       // on (they have almost always landed by then), so that nothing but the
       // softmax's arrival stands between one group's P and its two MMAs.
@@ -364,17 +361,17 @@ __global__ void __launch_bounds__(kAttThreads, 1)
       auto wait_k = [&](int t) -> bool {
         if (t <= k_ready) return true;
         k_ready = t;
-        return mbar_poll(k_full(t & 1), static_cast<uint32_t>((t >> 1) & 1), err, kDevErrTimeoutFull, 32);
+        return mbar_poll(kv_full(2 * t), kv_par(2 * t), err, kDevErrTimeoutFull);
       };
       auto wait_v = [&](int t) -> bool {
         if (t <= v_ready) return true;
         v_ready = t;
-        return mbar_poll(v_full(t & 1), static_cast<uint32_t>((t >> 1) & 1), err, kDevErrTimeoutFull, 32);
+        return mbar_poll(kv_full(2 * t + 1), kv_par(2 * t + 1), err, kDevErrTimeoutFull);
       };
       // S_w = Q_w K_t^T into tile w's score columns (K_t has landed)
       auto issue_s = [&](int w, int t) {
         const uint32_t qa = base + AttSmem::kQ + static_cast<uint32_t>(w * kAttTile);
-        const uint32_t kb = base + AttSmem::kK + static_cast<uint32_t>((t & 1) * kAttTile);
+        const uint32_t kb = slot_addr(2 * t);
 #pragma unroll
         for (int kk = 0; kk < kAttD / kUmmaK; ++kk) {
           const uint32_t atom = static_cast<uint32_t>((kk >> 2) * kAttAtom + (kk & 3) * 32);
@@ -383,11 +380,11 @@ __global__ void __launch_bounds__(kAttThreads, 1)
         }
         tc_commit(s_full(w));
       };
-      // O_w += P_w V_t over keys 32 * half .. + 63, P_w read from tensor memory
+      // O_w += P_w V_t over keys 64 * half .. + 63, P_w read from tensor memory
       // (that half of P_w and V_t ready)
       auto issue_pv = [&](int w, int t, int half) {
         const int u = t - t0(w);
-        const uint32_t vb = base + AttSmem::kV + static_cast<uint32_t>((t & 1) * kAttTile);
+        const uint32_t vb = slot_addr(2 * t + 1);
 #pragma unroll
         for (int k4 = 0; k4 < 4; ++k4) {
           const int kk = 4 * half + k4;
@@ -403,7 +400,7 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           tc_fence_after();
           issue_s(w, 0);
         }
-      if (ok) tc_commit(k_empty(0));
+      if (ok) tc_commit(kv_empty(0));
       // per key tile: PV_0, S_0 of the next tile, PV_1, S_1 of the next tile, so
       // that one group's softmax overlaps the other's two MMAs
       for (int t = 0; t < nkv && ok; ++t) {
@@ -415,11 +412,11 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           if (pv) {
             // the first half of P is ready while the softmax still computes the second
             const uint32_t par = static_cast<uint32_t>((t - t0(w)) & 1);
-            if (!(ok = mbar_poll(p_lo(w), par, err, kDevErrTimeoutFull, 32))) break;
+            if (!(ok = mbar_poll(p_lo(w), par, err, kDevErrTimeoutFull))) break;
             tc_fence_after();
             issue_pv(w, t, 0);
             tc_commit(pvlo_done(w));
-            if (!(ok = mbar_poll(p_hi(w), par, err, kDevErrTimeoutFull, 32))) break;
+            if (!(ok = mbar_poll(p_hi(w), par, err, kDevErrTimeoutFull))) break;
             tc_fence_after();
             issue_pv(w, t, 1);
           } else {
@@ -428,8 +425,9 @@ __global__ void __launch_bounds__(kAttThreads, 1)
           if (next) issue_s(w, t + 1);
         }
         if (!ok) break;
-        if (t + 1 < nkv) tc_commit(k_empty((t + 1) & 1));
-        tc_commit(v_empty(t & 1));
+        // K_{t+1} is free once both groups' S MMAs on it complete, V_t once both PVs do
+        if (t + 1 < nkv) tc_commit(kv_empty(2 * t + 2));
+        tc_commit(kv_empty(2 * t + 1));
       }
     }
   }
