@@ -238,6 +238,12 @@ HLM_DEVICE void tma_load_2d_pair(uint32_t dst_smem, const CUtensorMap* map, int 
 }
 
 // TMA store of a 2-D box from shared memory (bulk async group of the issuing thread).
+// Bring one box of a tensor map into L2 (no shared memory, no completion).
+HLM_DEVICE void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
 HLM_DEVICE void tma_store_2d(const CUtensorMap* map, int c0, int c1, uint32_t src_smem) {
   asm volatile(
       "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(

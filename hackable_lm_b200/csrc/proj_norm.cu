@@ -42,11 +42,6 @@ HLM_DEVICE void st_async_f32(uint32_t cluster_addr, float v, uint32_t bar_cluste
                : "memory");
 }
 // Prefetch a 2-D TMA box into L2 (no shared memory, no completion to wait for).
-HLM_DEVICE void tma_prefetch_2d(const CUtensorMap* map, int c0, int c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1)
-               : "memory");
-}
 HLM_DEVICE float ld_shared_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
@@ -293,7 +288,7 @@ struct EpiResidualNormPair {
       const int next_row0 = row0 + 2 * kBM * static_cast<int>(num_clusters_x());
       if (next_row0 < p.M) {
 #pragma unroll
-        for (int i = 0; i < GW; ++i) tma_prefetch_2d(&ep.map_res, col0 + (i * P + part) * 64, next_row0);
+        for (int i = 0; i < GW; ++i) tma_prefetch_l2_2d(&ep.map_res, col0 + (i * P + part) * 64, next_row0);
       }
     }
     warp_wait(res_bar, static_cast<uint32_t>(it & 1), p.err, kDevErrTimeoutEpiLoad, lane);
