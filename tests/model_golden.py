@@ -16,14 +16,18 @@ def fingerprint(t: torch.Tensor) -> torch.Tensor:
     return torch.stack([flat.sum(), flat.abs().sum(), flat[:8].sum(), flat[-8:].sum()])
 
 
-def build(gd: dict, backend: str) -> LanguageModel:
+def build(gd: dict, backend: str, attention_backend: str | None = None) -> LanguageModel:
     """This package's LanguageModel with the fixture's dimensions, initialised from the
     fixture's seed on the CPU in fp32 (the reference's init order, model.py:370-380),
-    checked against the stored init fingerprints, then rounded to bf16 values."""
+    checked against the stored init fingerprints, then rounded to bf16 values.  The
+    attention core defaults to SDPA with the b200 operators and to the explicit
+    softmax with the torch ones."""
     c = gd["config"]
+    if attention_backend is None:
+        attention_backend = "sdpa" if backend == "b200" else "torch"
     cfg = hcfg.model_config_for_depth(c["depth"], vocab_size=c["vocab"], sequence_len=c["seq"],
                                       attention_window=c["window"], backend=backend,
-                                      attention_backend="sdpa" if backend == "b200" else "torch")
+                                      attention_backend=attention_backend)
     assert (cfg.n_embd, cfg.n_head, cfg.mlp_hidden, cfg.attention_full_every, cfg.loss_chunk_size) == (
         c["n_embd"], c["n_head"], c["mlp_hidden"], c["attention_full_every"], c["loss_chunk_size"])
     assert (cfg.rope_theta, cfg.rope_fraction) == (c["rope_theta"], c["rope_fraction"])

@@ -32,10 +32,10 @@ from parity import assert_loss_close, record
 pytestmark = pytest.mark.gpu
 
 
-def _run(gd, backend, device):
+def _run(gd, backend, device, attention_backend=None):
     from hackable_lm_b200 import kernels
 
-    model = mg.build(gd, backend).to(device)
+    model = mg.build(gd, backend, attention_backend).to(device)
     kernels.apply_precision_policy(model, "bf16")
     x, y = mg.batch(gd, device)
     _, loss = model(x, y)
@@ -54,14 +54,21 @@ def _row_rel_l2(model, gd):
     return out
 
 
+@pytest.mark.parametrize("attention", ["sdpa", "b200"])
 @pytest.mark.parametrize("name", ["model_d4_window", "model_d12"])
-def test_b200_model_matches_reference_model(name, golden, cuda_device):
+def test_b200_model_matches_reference_model(name, attention, golden, cuda_device):
+    """With the attention core on SDPA (the default) and on this library's tcgen05
+    forward (attention_backend "b200": sliding windows in three of the d4 model's
+    four layers); the latter also checks that the forward kernel ran in every layer."""
     from hackable_lm_b200 import _lib
 
     gd = golden(name)
     _lib.clear_device_error()
-    mb, loss_b = _run(gd, "b200", cuda_device)
+    depth = gd["config"]["depth"]
+    with _lib.KernelTimer("attn_fwd", 4 * depth) as timer:
+        mb, loss_b = _run(gd, "b200", cuda_device, attention)
     assert _lib.device_error() == 0
+    assert timer.launches == (depth if attention == "b200" else 0), timer.launches
     assert_loss_close(loss_b, gd["loss"].item(), what=f"{name} loss")
     norms = mg.grad_errors(mb, gd)
     rows_b = _row_rel_l2(mb, gd)
