@@ -720,7 +720,8 @@ struct EpiStore {
     int64_t ldd;
     int64_t split_stride;  // elements between split-K slabs (fp32 partials)
     int dtype;             // HLM_BF16 or HLM_F32
-    int accumulate;        // D += acc (read-modify-write)
+    int accumulate;        // 1: D += acc (read-modify-write); 2 (fp32 only): D += acc by
+                           // atomic reductions in L2, for split-K partials of one D
     int vec_ok;            // ldd % 8 == 0 and d 16-byte aligned
     const float* alpha;    // optional device scalar: D = alpha * acc (+ D)
   };
@@ -758,6 +759,12 @@ struct EpiStore {
           for (int j = 0; j < 32; j += 4) {
             float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
                                    __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            if (ep.accumulate == 2) {
+              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(d + j), "f"(v.x), "f"(v.y),
+                           "f"(v.z), "f"(v.w)
+                           : "memory");
+              continue;
+            }
             if (ep.accumulate) {
               const float4 o = *reinterpret_cast<const float4*>(d + j);
               v.x += o.x;
@@ -772,6 +779,10 @@ struct EpiStore {
           for (int j = 0; j < 32; ++j) {
             if (col0 + j < p.N) {
               float v = __uint_as_float(r[j]);
+              if (ep.accumulate == 2) {
+                atomicAdd(d + j, v);
+                continue;
+              }
               if (ep.accumulate) v += d[j];
               d[j] = v;
             }

@@ -15,7 +15,9 @@
 // dq_pre/dk_pre, then two
 // tcgen05 GEMMs read [dq_pre | dk_pre | dv] as one segmented operand:
 //   grad_x = [dq|dk|dv] @ W_qkv          (W read N-major)
-//   grad_w = [dq|dk|dv]^T @ X            (split-K, fp32 slabs, fixed-order sum)
+//   grad_w = [dq|dk|dv]^T @ X            (split-K; the splits add their fp32 partials
+//                                         into one buffer in L2, which one pass rounds to
+//                                         bf16; the fp32 sum order varies run to run)
 #include "gemm_sm100.cuh"
 #include "rope_vec.cuh"
 
@@ -194,9 +196,10 @@ __global__ void __launch_bounds__(256) splitk_reduce_bf16_kernel(const float* __
 }
 
 // Split-K count for the dW GEMM (few output tiles, long K): the smallest split
-// whose work units (256 x kDwBN pair tiles) fill the CTA-pair waves to >= 90%
-// (each split adds an fp32 slab to write and reduce), else the best fill found
-// up to 16 splits; every split keeps at least 8 K blocks.
+// whose work units (256 x kDwBN pair tiles) fill the CTA-pair waves to >= 95%
+// (the splits add their fp32 partials into one L2-resident buffer, so a split
+// costs its reductions, not a slab), else the best fill found up to 16 splits;
+// every split keeps at least 8 K blocks.
 static inline int qkv_dw_splits(int64_t tokens, int64_t nqkv, int64_t C) {
   const int64_t tiles = ((nqkv + 2 * kBM - 1) / (2 * kBM)) * ((C + kDwBN - 1) / kDwBN);
   const int64_t kblocks = (tokens + kBK - 1) / kBK;
@@ -213,7 +216,7 @@ static inline int qkv_dw_splits(int64_t tokens, int64_t nqkv, int64_t C) {
       best_fill = fill;
       best = static_cast<int>(eff);
     }
-    if (fill >= 0.9) break;
+    if (fill >= 0.95) break;
   }
   return best;
 }
@@ -234,8 +237,8 @@ static QkvBwdPlan qkv_bwd_plan(int64_t M, int64_t C, int64_t Hq, int64_t Hk) {
   off = a256(off + static_cast<size_t>(M) * Hq * kQkvD * 2);
   pl.off_dk = off;
   off = a256(off + static_cast<size_t>(M) * Hk * kQkvD * 2);
-  pl.off_slab = off;
-  off = a256(off + static_cast<size_t>(pl.splits) * nqkv * C * 4);
+  pl.off_slab = off;  // fp32 dW accumulated by every split
+  off = a256(off + static_cast<size_t>(nqkv) * C * 4);
   pl.total = off;
   return pl;
 }
@@ -430,18 +433,21 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
     p.a_seg1 = seg1;
     p.a_seg2 = seg2;
     p.err = err;
+    // the splits add into one fp32 dW (zeroed first), then one pass rounds it to bf16
+    const int64_t n = nqkv * C;
+    if (cudaMemsetAsync(slabs, 0, static_cast<size_t>(n) * sizeof(float), s) != cudaSuccess)
+      return HLM_ERR_LAUNCH;
     EpiStore::Params ep;
     ep.d = slabs;
     ep.ldd = C;
-    ep.split_stride = nqkv * C;
+    ep.split_stride = 0;
     ep.dtype = HLM_F32;
-    ep.accumulate = 0;
+    ep.accumulate = 2;
     ep.vec_ok = 1;
     ep.alpha = nullptr;
     const int rc = launch_gemm_pair<kDwBN, kQkvStages, true, true, EpiStore>(a0, a1, a2, mb, p, ep, s,
                                                                             HLM_KERNEL_QKV_DW);
     if (rc != HLM_OK) return rc;
-    const int64_t n = nqkv * C;
     int64_t blocks = (n / 4 + 255) / 256;
     const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
     if (blocks > cap) blocks = cap;
@@ -449,7 +455,7 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
     {
       LaunchScope scope(0, s);
       splitk_reduce_bf16_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
-          slabs, pl.splits, n, static_cast<__nv_bfloat16*>(grad_w));
+          slabs, 1, n, static_cast<__nv_bfloat16*>(grad_w));
     }
     if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
   }
