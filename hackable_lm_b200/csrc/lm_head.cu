@@ -281,34 +281,47 @@ __global__ void __launch_bounds__(256) lm_loss_reduce_kernel(const float* __rest
 // The 1/n_valid scale is applied in fp32 by the dX/dW GEMM epilogues: folded
 // into the bf16 values it would carry one rounding error shared by every
 // element.
+// One block walks whole rows (the row's lse and target read once); each thread
+// keeps kDlogitsU 16-byte loads in flight before it computes, since a single
+// load per thread leaves too few bytes in flight to cover DRAM latency.
+constexpr int kDlogitsU = 4;
 __global__ void __launch_bounds__(256) lm_dlogits_kernel(__nv_bfloat16* __restrict__ logits,
                                                         const int2* __restrict__ info, int rows,
                                                         int64_t V) {
-  const int64_t vpr = V / 8;
-  const int64_t total = static_cast<int64_t>(rows) * vpr;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
-       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = v / vpr;
-    const int col0 = static_cast<int>((v - row * vpr) * 8);
+  const int vpr = static_cast<int>(V / 8);
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
     const int2 ri = info[row];
     const float nl2 = __int_as_float(ri.x);
-    __nv_bfloat16* p = logits + row * V + col0;
-    const uint4 x = ld_global_v4(p);
-    const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
-    float q[8];
+    __nv_bfloat16* base = logits + static_cast<int64_t>(row) * V;
+    for (int c0 = threadIdx.x; c0 < vpr; c0 += 256 * kDlogitsU) {
+      uint4 x[kDlogitsU];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      q[2 * e] = ex2_ftz(fmaf(bf16_lo(xw[e]), kLog2e, -nl2));
-      q[2 * e + 1] = ex2_ftz(fmaf(bf16_hi(xw[e]), kLog2e, -nl2));
-    }
-    const int d = ri.y - col0;
-    if (static_cast<unsigned>(d) < 8u) {
+      for (int u = 0; u < kDlogitsU; ++u) {
+        const int c = c0 + u * 256;
+        if (c < vpr) x[u] = ld_global_v4(base + static_cast<int64_t>(c) * 8);
+      }
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (e == d) q[e] -= 1.0f;
+      for (int u = 0; u < kDlogitsU; ++u) {
+        const int c = c0 + u * 256;
+        if (c >= vpr) break;
+        const uint32_t xw[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+        float q[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          q[2 * e] = ex2_ftz(fmaf(bf16_lo(xw[e]), kLog2e, -nl2));
+          q[2 * e + 1] = ex2_ftz(fmaf(bf16_hi(xw[e]), kLog2e, -nl2));
+        }
+        const int d = ri.y - c * 8;
+        if (static_cast<unsigned>(d) < 8u) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (e == d) q[e] -= 1.0f;
+        }
+        st_global_v4(base + static_cast<int64_t>(c) * 8,
+                     make_uint4(pack_bf16x2(q[0], q[1]), pack_bf16x2(q[2], q[3]), pack_bf16x2(q[4], q[5]),
+                                pack_bf16x2(q[6], q[7])));
+      }
     }
-    st_global_v4(p, make_uint4(pack_bf16x2(q[0], q[1]), pack_bf16x2(q[2], q[3]),
-                               pack_bf16x2(q[4], q[5]), pack_bf16x2(q[6], q[7])));
   }
 }
 
@@ -508,8 +521,7 @@ extern "C" int hlm_lm_head_ce(const void* hidden, const void* weight, const int6
     auto dlogits = [&](int r_lo, int r_hi, cudaStream_t st) -> int {
       const int n = r_hi - r_lo;
       if (n <= 0) return HLM_OK;
-      const int64_t vecs = static_cast<int64_t>(n) * (V / 8);
-      int64_t blocks = (vecs + 255) / 256;
+      int64_t blocks = n;  // whole rows per block
       const int64_t cap = static_cast<int64_t>(num_sms_of_current_device()) * 8;
       if (blocks > cap) blocks = cap;
       LaunchScope scope(HLM_KERNEL_LM_DLOGITS, st);
