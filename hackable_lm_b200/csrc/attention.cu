@@ -18,11 +18,13 @@
 //           tile PV_0, S_0(next), PV_1, S_1(next), so that one group's softmax
 //           runs while the tensor cores do the other group's two MMAs
 //   warps 4-7, 8-11  softmax of tile 0 / 1, one query row per thread: the score row
-//           into registers, row max and exp2 of the scaled, masked scores against
-//           a reference max that moves only when a tile exceeds it by more than 8,
-//           running sum, P as bf16 pairs over the first 64 score columns, and, on
-//           a move, the output row rescaled in TMEM (tcgen05.ld / st); at the end
-//           out = O / l through TMA stores and lse = (m + log2 l) ln 2.
+//           into registers, exp2 of the scaled, masked scores against a running
+//           reference max m (no row max once every row has one; the exact path,
+//           with the row max and m moved only when exceeded by more than 8, takes a
+//           row's first key tile and any half whose sum leaves [0, 2^64]), running
+//           sum, P as bf16 pairs over the first 64 score columns published per key
+//           half, and, when m moves, the output row rescaled in TMEM (tcgen05.ld /
+//           st); at the end out = O / l through TMA stores and lse = (m + log2 l) ln 2.
 // S_w of the next key tile overwrites P_w, so it is issued after PV_w; MMAs of one
 // thread run in order, so the commit that publishes S_w also covers PV_w (its O
 // may be rescaled and its P overwritten).  Every wait is bounded.
