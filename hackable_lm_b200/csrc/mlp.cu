@@ -20,7 +20,7 @@ namespace hlm {
 // (two per quadrant) with four stages at X [32768,768], W [4096,768].
 constexpr int kMlpStages = 5;
 constexpr int kMlpEpiWarps = 4;
-constexpr int kMlpBwdStages = 5;  // 5 x 32 KB stages + 64 KB of epilogue boxes
+constexpr int kMlpBwdStages = 3;  // 3 x 32 KB stages + 128 KB of epilogue boxes (two groups in flight per warp)
 
 // Epilogue: per warp (32 rows) and 64-unit group: gate and up (2 x 64 fp32
 // columns from TMEM) rounded to bf16 and staged as two 32x64 boxes for the
@@ -104,13 +104,15 @@ struct EpiSwiGLU {
 //                                                         swiglu_bwd_vec_kernel)
 // grad_h never goes to memory.  Epilogue: 8 warps, two per TMEM lane quadrant
 // (32 rows each), each taking every other 64-unit group of the 256-column
-// tile.  Per group a warp's gate and up boxes (32 x 64 bf16 each) arrive by
-// TMA into the warp's 8 KB buffer (one mbarrier per warp), dgate / dup are
-// computed row by row and written back in place, and the same buffer goes out
-// with two TMA stores; the next group's load into it waits until those stores
-// have read it.  With two warps per scheduler one computes while the other
-// waits for its load.  The barrier phase continues across tiles through a
-// per-warp use counter kept in shared memory.
+// tile.  A warp's gate and up boxes (32 x 64 bf16 each) of both its groups are
+// loaded by TMA at the start of the tile into two 8 KB buffers (one mbarrier
+// each), so the second group's load runs while the first is computed; dgate /
+// dup are computed row by row and written back in place, and each buffer goes
+// out with two TMA stores; a buffer's next load waits until those stores have
+// read it.  (Two buffers per warp leave room for three mainloop stages; measured
+// 143.7 us vs 151.5 us with one buffer and five stages at the d12 shape.)  The
+// barrier phases continue across tiles through a per-warp tile counter kept in
+// shared memory.
 struct EpiSwiGLUBwd {
   struct Params {
     alignas(64) CUtensorMap map_gu;   // gate_up [M][2H] bf16, box {64, 32}
@@ -119,9 +121,9 @@ struct EpiSwiGLUBwd {
   };
   static constexpr int kBoxBytes = 32 * 128;
   static constexpr int kWarps = 8;
-  static constexpr int kWarpBytes = 2 * kBoxBytes;  // gate box, up box (outputs in place)
+  static constexpr int kWarpBytes = 4 * kBoxBytes;  // per group: gate box, up box (outputs in place)
   static constexpr int kBarOffset = kWarps * kWarpBytes;
-  static constexpr int kCtrOffset = kBarOffset + kWarps * 8;
+  static constexpr int kCtrOffset = kBarOffset + kWarps * 16;
   template <int EPI_WARPS>
   static constexpr int smem_bytes() {
     static_assert(EPI_WARPS == kWarps, "two epilogue warps per lane quadrant");
@@ -129,8 +131,8 @@ struct EpiSwiGLUBwd {
   }
   static HLM_DEVICE void init(uint8_t* smem) {
     const uint32_t b = smem_u32(smem);
+    for (int w = 0; w < 2 * kWarps; ++w) mbar_init(b + kBarOffset + 8 * w, 1);
     for (int w = 0; w < kWarps; ++w) {
-      mbar_init(b + kBarOffset + 8 * w, 1);
       reinterpret_cast<volatile uint32_t*>(smem + kCtrOffset)[w] = 0u;
     }
   }
@@ -143,25 +145,33 @@ struct EpiSwiGLUBwd {
     if (row0 >= p.M) return;  // no rows of this warp in the tile: no loads, barrier phase unchanged
     const int slot = part * 4 + quad;
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t gate_box = sbase + static_cast<uint32_t>(slot * kWarpBytes);
-    const uint32_t up_box = gate_box + kBoxBytes;
-    const uint32_t bar = sbase + static_cast<uint32_t>(kBarOffset + 8 * slot);
+    const uint32_t wbase = sbase + static_cast<uint32_t>(slot * kWarpBytes);
     volatile uint32_t* ctr = reinterpret_cast<volatile uint32_t*>(smem + kCtrOffset) + slot;
     const int h0 = n_tile * BN;  // hidden unit of the tile's first column
     uint32_t n = 0;
     if (lane == 0) n = *ctr;
     n = __shfl_sync(0xffffffffu, n, 0);
-    uint32_t used = 0;
-#pragma unroll 1
-    for (int g = part; g < BN / 64; g += kParts, ++used) {
-      if (lane == 0) {
-        // the stores that last read this buffer must be done with it
-        bulk_wait_group_read<0>();
+    // both groups' boxes in flight at once (buffer k for group part + 2k)
+    if (lane == 0) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int g = part + 2 * k;
+        const uint32_t gb = wbase + static_cast<uint32_t>(k * 2 * kBoxBytes);
+        const uint32_t bar = sbase + static_cast<uint32_t>(kBarOffset + 16 * slot + 8 * k);
+        // the store that last read this buffer (previous tile, group k) must be done with it
+        if (k == 0) bulk_wait_group_read<1>(); else bulk_wait_group_read<0>();
         mbar_arrive_expect_tx(bar, 2 * kBoxBytes);
-        tma_load_2d(gate_box, &ep.map_gu, h0 + g * 64, row0, bar);
-        tma_load_2d(up_box, &ep.map_gu, ep.H + h0 + g * 64, row0, bar);
+        tma_load_2d(gb, &ep.map_gu, h0 + g * 64, row0, bar);
+        tma_load_2d(gb + kBoxBytes, &ep.map_gu, ep.H + h0 + g * 64, row0, bar);
       }
-      if (!warp_wait(bar, (n + used) & 1u, p.err, kDevErrTimeoutEpiLoad, lane)) return;
+    }
+#pragma unroll 1
+    for (int k = 0; k < 2; ++k) {
+      const int g = part + 2 * k;
+      const uint32_t gate_box = wbase + static_cast<uint32_t>(k * 2 * kBoxBytes);
+      const uint32_t up_box = gate_box + kBoxBytes;
+      const uint32_t bar = sbase + static_cast<uint32_t>(kBarOffset + 16 * slot + 8 * k);
+      if (!warp_wait(bar, n & 1u, p.err, kDevErrTimeoutEpiLoad, lane)) return;
 #pragma unroll 1
       for (int hs = 0; hs < 2; ++hs) {
         uint32_t d[32];
@@ -208,7 +218,7 @@ struct EpiSwiGLUBwd {
         bulk_commit_group();
       }
     }
-    if (lane == 0) *ctr = n + used;
+    if (lane == 0) *ctr = n + 1;
   }
 };
 
