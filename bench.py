@@ -345,14 +345,29 @@ D12_KERNELS = {"lm_logits": 1, "lm_dlogits": 1, "lm_dx": 1, "lm_dw": 1, "gate_up
                "proj_norm": 24, "rmsnorm_fwd": 1, "rmsnorm_bwd": 25}
 
 
-def d12_config(world: int, accum: int, max_grad_norm: float = 1.0) -> dict:
+def d12_flops_per_token(window: int) -> int:
+    if not window:
+        return D12_FLOPS_PER_TOKEN
+    from hackable_lm_b200 import config as hcfg
+
+    n_embd, _ = hcfg.depth_dimensions(12)
+    return hcfg.estimate_flops_per_token(12, n_embd, 2048, hcfg.scaling_params_for_depth(12, 32768),
+                                         attention_window=window,
+                                         attention_full_every=hcfg.DEFAULTS["attention_full_every"])
+
+
+def d12_config(world: int, accum: int, max_grad_norm: float = 1.0, window: int = 0) -> dict:
+    attention = ("torch SDPA, full causal" if not window else
+                 f"sliding window {window} (the reference's default pattern: every 4th and the last layer "
+                 "full causal): windowed layers on the tcgen05 forward + flash_attn's windowed backward, "
+                 "full layers on SDPA")
     return {"workload": "d12 DP training step: depth 12, C=768, 6x128 heads, SwiGLU 2048, vocab 32768, "
                         "seq 2048, micro-batch 16/GPU, global batch 2^20 tokens, global grad-norm clip "
                         f"{max_grad_norm}, Muon+AdamW step",
             "model": "hackable-lm d12 (random init)", "global_batch": 2**20, "seq_len": 2048,
             "micro_batch_per_gpu": 16, "grad_accum_per_rank": accum,
             "parallelism": f"dp{world}" + (" (DDP, bf16 25 MB buckets, NCCL)" if world > 1 else ""),
-            "attention": "torch SDPA, full causal",
+            "attention": attention,
             "l2": "working set per micro-step >> 126 MB L2 (activations ~GBs); no flush"}
 
 
@@ -361,7 +376,8 @@ def bench_d12(args, d: Dist, device) -> dict:
     from hackable_lm_b200 import train as tr
 
     peaks, peak_src = load_peaks()
-    s = tr.build(device, world=d.world)
+    window = int(args.attention_window or 0)
+    s = tr.build(device, world=d.world, attention_window=window or None)
     # fresh data: one distinct micro-batch for every micro-step of the run (warm-up, timed
     # steps and the end-to-end pass), cycling only beyond 1024 micro-batches (268 MB)
     n_micro = min(1024, s.accum * (args.warmup + 2 * args.steps + 1))
@@ -517,14 +533,16 @@ def bench_d12(args, d: Dist, device) -> dict:
     bytes_in = s.accum * (host[0][0].numel() + host[0][1].numel()) * 8
     e2e = {"value": tokens_per_step / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": bytes_in,
            "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 3)}
-    mfu = D12_FLOPS_PER_TOKEN * value / (peaks["bf16_tflops"] * 1e12 * d.world)
+    flops_per_token = d12_flops_per_token(window)
+    mfu = flops_per_token * value / (peaks["bf16_tflops"] * 1e12 * d.world)
     return {
         "metric": "d12 step tok/s", "value": value, "unit": "tokens/s", "n_gpus": d.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: uniform token ids (seeded per rank), targets = ids shifted by one",
-        "config": d12_config(d.world, s.accum, args.max_grad_norm), "roofline": roofline, "kernel_breakdown": breakdown,
-        "mfu": round(mfu, 4), "mfu_basis": f"{D12_FLOPS_PER_TOKEN} FLOP/token / measured bf16 burst peak",
+        "config": d12_config(d.world, s.accum, args.max_grad_norm, window), "roofline": roofline,
+        "kernel_breakdown": breakdown,
+        "mfu": round(mfu, 4), "mfu_basis": f"{flops_per_token} FLOP/token / measured bf16 burst peak",
         "loss_first_step": first_loss, "loss": float(loss.float().item()),
         "loss_note": f"mean micro-batch loss of the first warm-up step and of the last timed step; "
                      f"{n_micro} distinct micro-batches over the run; random-init loss is ln(32768) = 10.40",
@@ -783,6 +801,9 @@ def main() -> None:
                          "its default 0 skips the clip, this bench includes it so the step does all of "
                          "the reference's per-step work)")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-operator section")
+    ap.add_argument("--attention-window", type=int, default=0,
+                    help="d12 variant: sliding window on every layer but each 4th and the last "
+                         "(the reference's default pattern); 0 (default, BASELINE config 5) = full causal")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-tokens", type=int, default=1024, help="tokens per reference-arm step")
     ap.add_argument("--tokens", type=int, default=None,

@@ -150,18 +150,21 @@ class AttentionCore(nn.Module):
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         seq_len = q.shape[1]
-        if (self.config.attention_backend == "b200" and (q.is_cuda or q.is_meta)
-                and self.config.dropout == 0.0 and ops.attention_supported(q, k, v)):
-            # tcgen05 forward on the [B, T, H, D] layout the QKV kernel wrote
-            window = self.window if self.window is not None and self.window < seq_len else None
+        window = self.window if self.window is not None and self.window < seq_len else None
+        backend = self.config.attention_backend
+        if backend != "torch" and self.config.dropout == 0.0 and (
+                (backend == "b200" and (q.is_cuda or q.is_meta) and ops.attention_supported(q, k, v))
+                or kernels.sliding_window_b200(q, k, v, window, 0.0)):
+            # tcgen05 forward on the [B, T, H, D] layout the QKV kernel wrote: every
+            # layer with "b200", and the sliding-window layers with every other name
+            # (SDPA has no sliding-window kernel)
             return kernels.attention_b200(q, k, v, window)
         q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         if self.n_kv_head != self.n_head:
             rep = self.n_head // self.n_kv_head
             k = k.repeat_interleave(rep, dim=1)
             v = v.repeat_interleave(rep, dim=1)
-        window = self.window if self.window is not None and self.window < seq_len else None
-        backend = "torch" if q.device.type == "cpu" else self.config.attention_backend
+        backend = "torch" if q.device.type == "cpu" else backend
         y = kernels.scaled_dot_product_attention(q, k, v, 0.0, is_causal=True, window_size=window,
                                                  backend=backend)
         return y.transpose(1, 2)

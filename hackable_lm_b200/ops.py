@@ -768,6 +768,22 @@ def _attention_fake(q, k, v, window, scale):
     return torch.empty_like(q, memory_format=torch.contiguous_format), q.new_empty((B, H, T), dtype=torch.float32)
 
 
+_FLASH_BWD = []
+
+
+def _flash_attn_backward_op():
+    """flash_attn's backward (library code, like cuBLAS for the plain GEMMs), which
+    has a sliding-window kernel and takes the forward's output and natural-log lse
+    in this layout; None when the package is not installed."""
+    if not _FLASH_BWD:
+        try:
+            from flash_attn.flash_attn_interface import _flash_attn_backward
+        except Exception:  # noqa: BLE001 - any import failure means "not available"
+            _flash_attn_backward = None
+        _FLASH_BWD.append(_flash_attn_backward)
+    return _FLASH_BWD[0]
+
+
 def _window_bias(T: int, window: int, device) -> torch.Tensor:
     pos = torch.arange(T, device=device)
     dist = pos[:, None] - pos[None, :]
@@ -779,17 +795,29 @@ def _window_bias(T: int, window: int, device) -> torch.Tensor:
 def attention_backward(grad_out: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                        out: torch.Tensor, lse: torch.Tensor, window: int,
                        scale: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Gradients of attention() through cuDNN's SDPA backward kernel (library code, as
-    cuBLAS is for the plain GEMMs), fed with this forward's output and log-sum-exp."""
+    """Gradients of attention() through a library backward kernel (library code, as
+    cuBLAS is for the plain GEMMs), fed with this forward's output and log-sum-exp:
+    cuDNN's SDPA backward for full causal attention, flash_attn's windowed backward
+    for a sliding window (cuDNN would take the window as a dense T x T bias and run
+    every key: measured 1.3 ms vs 0.6 ms at [16, 2048, 6, 128], window 512), cuDNN
+    with that bias when flash_attn is not installed."""
     _require_cuda(grad_out, q, k, v, out, lse)
     B, T, H, D = q.shape
+    full = window <= 0 or window >= T
+    fa_bwd = None if full else _flash_attn_backward_op()
+    if fa_bwd is not None:
+        q, k, v, out = q.contiguous(), k.contiguous(), v.contiguous(), out.contiguous()
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        # keys with 0 <= t - k < window: causal, left window window - 1, no dropout
+        fa_bwd(grad_out.contiguous(), q, k, v, out, lse.contiguous(), dq, dk, dv, 0.0, float(scale), True,
+               int(window) - 1, 0, 0.0, None, False, None)
+        return dq, dk, dv
     # [B, H, T, D] views of the [B, T, H, D] tensors: q, k, v, out and grad_out share
     # one stride pattern, as cuDNN's backward expects of tensors from its own forward;
     # no dropout (seed / offset zero), dense (no cumulative sequence lengths), the
     # log-sum-exp as its [B, H, T, 1] statistics
     tr = lambda t: t.transpose(1, 2)  # noqa: E731
     zero = torch.zeros((), dtype=torch.int64, device=q.device)
-    full = window <= 0 or window >= T
     bias = None if full else _window_bias(T, window, q.device)[None, None].expand(B, H, T, T)
     dq, dk, dv = torch.ops.aten._scaled_dot_product_cudnn_attention_backward(
         tr(grad_out.contiguous()), tr(q), tr(k), tr(v), tr(out), lse.unsqueeze(-1), zero, zero, bias, None, None,

@@ -144,3 +144,37 @@ def test_attention_d12_shape_vs_sdpa(cuda_device):
     for name, a, e in zip("qkv", (qd.grad, kd.grad, vd.grad), (qs.grad, ks.grad, vs.grad)):
         # both bf16; the backward kernel is the same, fed with either forward's statistics
         assert _rel_l2(a, e.transpose(1, 2)) <= 1e-2, (name, _rel_l2(a, e.transpose(1, 2)))
+
+
+@pytest.mark.parametrize("backend", ["flash_attn_2", "sdpa"])
+def test_sliding_window_takes_the_b200_path(backend, cuda_device):
+    """The reference entry point with a sliding window (its default pattern) runs the
+    tcgen05 forward under every backend name but "torch", and its gradients (flash_attn's
+    windowed backward when installed, else cuDNN with the window as a bias) match the
+    fp32 reference within the bar SDPA's own bf16 gradients set."""
+    from hackable_lm_b200 import _lib, kernels
+
+    _lib.clear_device_error()
+    B, T, H, W = 2, 512, 2, 160
+    q, k, v = _inputs(B, T, H, H, 6, cuda_device)
+    g = torch.Generator().manual_seed(7)
+    go = torch.randn(B, T, H, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    qd, kd, vd = (t.clone().requires_grad_(True) for t in (q, k, v))
+    flash = backend.startswith("flash")
+    args = (qd, kd, vd) if flash else tuple(t.transpose(1, 2) for t in (qd, kd, vd))
+    with _lib.KernelTimer("attn_fwd", 4) as timer:
+        out = kernels.scaled_dot_product_attention(*args, 0.0, is_causal=True, window_size=W, backend=backend)
+    out = out if flash else out.transpose(1, 2)
+    out.backward(go)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert timer.launches == 1
+    ref, _ = _ref(q, k, v, W)
+    assert_bf16_close(out, ref, what="out")
+    qr, kr, vr = (t.float().clone().requires_grad_(True) for t in (q, k, v))
+    ref_out, _ = _ref(qr, kr, vr, W)
+    ref_out.backward(go.float())
+    for name, a, e, s in zip("qkv", (qd.grad, kd.grad, vd.grad), (qr.grad, kr.grad, vr.grad),
+                             _sdpa_grads(q, k, v, go, W)):
+        sdpa_err = _rel_l2(s, e)
+        assert _rel_l2(a, e) <= 2 * sdpa_err + 1e-3, (name, _rel_l2(a, e), sdpa_err)

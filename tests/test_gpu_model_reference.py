@@ -62,13 +62,21 @@ def test_b200_model_matches_reference_model(name, attention, golden, cuda_device
     four layers); the latter also checks that the forward kernel ran in every layer."""
     from hackable_lm_b200 import _lib
 
+    from hackable_lm_b200.config import layer_attention_window
+
     gd = golden(name)
     _lib.clear_device_error()
-    depth = gd["config"]["depth"]
+    c = gd["config"]
+    depth = c["depth"]
+    # with "sdpa" the sliding-window layers still run the tcgen05 forward (SDPA has no
+    # sliding-window kernel); the full-attention layers run SDPA
+    windowed = sum(1 for i in range(depth)
+                   if (w := layer_attention_window(i, depth, c["window"], c["attention_full_every"])) is not None
+                   and w < c["seq"])
     with _lib.KernelTimer("attn_fwd", 4 * depth) as timer:
         mb, loss_b = _run(gd, "b200", cuda_device, attention)
     assert _lib.device_error() == 0
-    assert timer.launches == (depth if attention == "b200" else 0), timer.launches
+    assert timer.launches == (depth if attention == "b200" else windowed), timer.launches
     assert_loss_close(loss_b, gd["loss"].item(), what=f"{name} loss")
     norms = mg.grad_errors(mb, gd)
     rows_b = _row_rel_l2(mb, gd)
