@@ -359,7 +359,7 @@ def d12_flops_per_token(window: int) -> int:
 def d12_config(world: int, accum: int, max_grad_norm: float = 1.0, window: int = 0) -> dict:
     attention = ("torch SDPA, full causal" if not window else
                  f"sliding window {window} (the reference's default pattern: every 4th and the last layer "
-                 "full causal): windowed layers on the tcgen05 forward + flash_attn's windowed backward, "
+                 "full causal): windowed layers on the tcgen05 forward and backward, "
                  "full layers on SDPA")
     return {"workload": "d12 DP training step: depth 12, C=768, 6x128 heads, SwiGLU 2048, vocab 32768, "
                         "seq 2048, micro-batch 16/GPU, global batch 2^20 tokens, global grad-norm clip "

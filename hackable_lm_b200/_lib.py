@@ -60,6 +60,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "hlm_swiglu_down_bwd": ([_P, _P, _P, _P, _I64, _I64, _I64, _P], c_int),
     "hlm_proj_residual_rms_norm_fwd": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, c_float, _P], c_int),
     "hlm_attention_fwd": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, c_float, _P], c_int),
+    "hlm_attention_bwd_workspace_bytes": ([_I64, _I64, _I64, _I64], c_size_t),
+    "hlm_attention_bwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _I64, _I64, _I64, _I64, _I64, _I64,
+                           c_float, _P], c_int),
     "hlm_gemm_bf16": (
         [_P, _P, _P, _I64, _I64, _I64, c_int, c_int, _I64, _I64, _I64, c_int, c_int, _P], c_int),
 }
@@ -139,7 +142,7 @@ KERNEL_IDS = {
     "lm_logits": 1, "lm_dlogits": 2, "lm_dx": 3, "lm_dw": 4, "qkv_fwd": 5, "qkv_bwd_norm": 6,
     "qkv_dx": 7, "qkv_dw": 8, "swiglu_fwd": 9, "swiglu_bwd": 10, "rmsnorm_fwd": 11,
     "rmsnorm_bwd": 12, "qk_rope_fwd": 13, "qk_rope_bwd": 14, "gemm": 15, "gate_up": 16,
-    "swiglu_down_bwd": 17, "proj_norm": 18, "attn_fwd": 19,
+    "swiglu_down_bwd": 17, "proj_norm": 18, "attn_fwd": 19, "attn_bwd": 20,
 }
 
 

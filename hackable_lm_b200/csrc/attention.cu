@@ -571,6 +571,366 @@ __global__ void __launch_bounds__(kAttThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Attention backward (the same masks, head_dim 128, H == Hk):
+//   D[b,h,t]  = sum_d dO . O                                  (attn_bwd_prep_kernel)
+//   P^T       = 2^(S^T scale log2 e - lse log2 e), S^T = K Q^T, masked
+//   dP^T      = V dO^T,   dS^T = P^T (dP^T - D)
+//   dV += P^T dO,   dK += scale dS^T Q,   dQ += scale dS K    (attn_bwd_kernel)
+// One CTA per (b, h, key tile j) walks the query tiles i >= j that the window
+// reaches.  S^T, dP^T, dV and dK live in the 512 TMEM columns; P^T and dS^T are
+// written as bf16 pairs over columns 0-31 and 64-95 of S^T and dP^T (each warp of
+// a lane quarter over the half it read; the A operands of the dV and dK MMAs), dS also into shared memory in the MN-major layout of the
+// dQ MMA's A operand, and each tile's dQ (in S^T's columns, after the dV MMA read
+// P^T there) is added into an fp32 accumulator in global memory by the
+// eight compute warps (two per TMEM lane quarter, each taking half the columns),
+// which a last pass scales and rounds (attn_dq_convert_kernel).
+//   warp 0  TMA: K_j, V_j once, then Q_i, dO_i into a two-stage ring
+//   warp 1  TMEM owner and MMA issuer
+//   warps 4-11  P, dS, the dQ reduction and the dK / dV epilogue
+// Every wait is bounded.
+// ---------------------------------------------------------------------------
+constexpr int kAbThreads = 384;
+struct AbSmem {
+  static constexpr int kK = 0;                      // K_j (K-major atoms, d 0-63 / 64-127)
+  static constexpr int kV = kK + kAttTile;          // V_j
+  static constexpr int kQ = kV + kAttTile;          // Q_i, two stages
+  static constexpr int kDO = kQ + 2 * kAttTile;     // dO_i, two stages
+  static constexpr int kDS = kDO + 2 * kAttTile;    // dS: query blocks [128 keys][64 queries] (MN-major A)
+  static constexpr int kBars = kDS + kAttTile;
+  // kv_full, qd_full[2], qd_empty[2], s_full, p_ready, ds_ready, dq_full, dq_free, dkv_done
+  static constexpr int kNumBars = 11;
+  static constexpr int kTmemSlot = kBars + kNumBars * 8;
+  static constexpr int kBytes = kTmemSlot + 16;
+};
+
+struct AbParams {
+  int B, T, H;
+  int window;        // keys with t - k < window (window >= T: full causal)
+  int k_tiles;       // T / 128
+  float scale;       // softmax scale
+  float scale_log2;  // softmax scale * log2(e)
+  const float* lse;  // [B, H, T] natural log
+  const float* Dv;   // [B, H, T] rowsum(dO . O)
+  float* dq_acc;     // [B, T, H, 128] fp32, zeroed
+  __nv_bfloat16* dk; // [B, T, H, 128]
+  __nv_bfloat16* dv;
+  int* err;
+};
+
+// D[b, h, t] = sum_d dO[b,t,h,d] O[b,t,h,d]: one warp per (b, t, h) row.
+__global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ dout,
+                                                            const __nv_bfloat16* __restrict__ out,
+                                                            float* __restrict__ Dv, int B, int T, int H) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(B) * T * H;
+  for (int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; row < rows;
+       row += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
+    const uint2 a = *reinterpret_cast<const uint2*>(dout + row * kAttD + 4 * lane);
+    const uint2 o = *reinterpret_cast<const uint2*>(out + row * kAttD + 4 * lane);
+    float acc = bf16_lo(a.x) * bf16_lo(o.x) + bf16_hi(a.x) * bf16_hi(o.x) + bf16_lo(a.y) * bf16_lo(o.y) +
+                bf16_hi(a.y) * bf16_hi(o.y);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      const int64_t bt = row / H;
+      const int h = static_cast<int>(row - bt * H);
+      const int64_t b = bt / T;
+      const int64_t t = bt - b * T;
+      Dv[(b * H + h) * T + t] = acc;
+    }
+  }
+}
+
+// dq = bf16(scale * dq_acc)
+__global__ void __launch_bounds__(256) attn_dq_convert_kernel(const float* __restrict__ acc, float scale,
+                                                              __nv_bfloat16* __restrict__ dq, int64_t n4) {
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < n4;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 x = reinterpret_cast<const float4*>(acc)[v];
+    uint2 o;
+    o.x = pack_bf16x2(x.x * scale, x.y * scale);
+    o.y = pack_bf16x2(x.z * scale, x.w * scale);
+    reinterpret_cast<uint2*>(dq)[v] = o;
+  }
+}
+
+__global__ void __launch_bounds__(kAbThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const AbParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int* err = p.err;
+
+  // work item: key tile j of one (b, h), key tiles in increasing order over the
+  // grid (the lowest see the most query tiles under the causal mask)
+  const int BH = p.B * p.H;
+  const int j = static_cast<int>(blockIdx.x) / BH;
+  const int bh = static_cast<int>(blockIdx.x) - j * BH;
+  const int b = bh / p.H;
+  const int h = bh - b * p.H;
+  // query tiles j .. i_last: the window reaches query tile i from key tile j while
+  // 128 (i - j) - 127 < window
+  const int i_last = min(p.k_tiles - 1, j + (p.window + 126) / kAttBQ);
+  const int n_i = i_last - j + 1;
+
+  const uint32_t bar0 = base + AbSmem::kBars;
+  const uint32_t kv_full = bar0;
+  auto qd_full = [&](int s) { return bar0 + 8u * static_cast<uint32_t>(1 + s); };
+  auto qd_empty = [&](int s) { return bar0 + 8u * static_cast<uint32_t>(3 + s); };
+  const uint32_t s_full = bar0 + 40, p_ready = bar0 + 48, ds_ready = bar0 + 56, dq_full = bar0 + 64,
+                 dq_free = bar0 + 72, dkv_done = bar0 + 80;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + AbSmem::kTmemSlot);
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(qd_full(s), 1);
+      mbar_init(qd_empty(s), 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_ready, 8);
+    mbar_init(ds_ready, 8);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 8);
+    mbar_init(dkv_done, 1);
+    fence_mbar_init();
+    prefetch_tensormap(&tmQ);
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+    prefetch_tensormap(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  // TMEM columns: S^T 0-127 (P^T over 0-31 and 64-95; then this tile's dQ over
+  // 0-127), dP^T 128-255 (dS^T over 128-159 and 192-223), dV 256-383, dK 384-511
+  const uint32_t t_s = tmem_base, t_dp = tmem_base + 128u, t_dv = tmem_base + 256u, t_dk = tmem_base + 384u;
+  const int row_k = b * p.T + j * kAttBK;
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttIssuerRegs));
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(kv_full, 2 * kAttTile);
+      for (int a = 0; a < 2; ++a) {
+        tma_load_2d(base + AbSmem::kK + static_cast<uint32_t>(a * kAttAtom), &tmK, h * kAttD + 64 * a, row_k, kv_full);
+        tma_load_2d(base + AbSmem::kV + static_cast<uint32_t>(a * kAttAtom), &tmV, h * kAttD + 64 * a, row_k, kv_full);
+      }
+      int issued = 0;
+      for (int ii = 0; ii < n_i && ok; ++ii) {
+        const int s = ii & 1;
+        if (ii >= 2 && !mbar_poll(qd_empty(s), static_cast<uint32_t>(((ii >> 1) - 1) & 1), err, kDevErrTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        const int row_q = b * p.T + (j + ii) * kAttBQ;
+        mbar_arrive_expect_tx(qd_full(s), 2 * kAttTile);
+        for (int a = 0; a < 2; ++a) {
+          tma_load_2d(base + AbSmem::kQ + static_cast<uint32_t>(s * kAttTile + a * kAttAtom), &tmQ, h * kAttD + 64 * a,
+                      row_q, qd_full(s));
+          tma_load_2d(base + AbSmem::kDO + static_cast<uint32_t>(s * kAttTile + a * kAttAtom), &tmDO,
+                      h * kAttD + 64 * a, row_q, qd_full(s));
+        }
+        issued = ii + 1;
+      }
+      mbar_wait_drain(kv_full, 0u, err);
+      for (int ii = max(0, issued - 2); ii < issued; ++ii)
+        mbar_wait_drain(qd_full(ii & 1), static_cast<uint32_t>((ii >> 1) & 1), err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_kk = make_idesc_bf16_f32(128, 128, false, false);  // S^T, dP^T
+      constexpr uint32_t idesc_km = make_idesc_bf16_f32(128, 128, false, true);   // dV, dK (A in TMEM)
+      constexpr uint32_t idesc_mm = make_idesc_bf16_f32(128, 128, true, true);    // dQ
+      bool ok = mbar_poll(kv_full, 0u, err, kDevErrTimeoutFull);
+      const uint32_t kbase = base + AbSmem::kK, vbase = base + AbSmem::kV, dsbase = base + AbSmem::kDS;
+      for (int ii = 0; ii < n_i && ok; ++ii) {
+        const int s = ii & 1;
+        const uint32_t par = static_cast<uint32_t>(ii & 1);
+        if (!(ok = mbar_poll(qd_full(s), static_cast<uint32_t>((ii >> 1) & 1), err, kDevErrTimeoutFull))) break;
+        // the previous tile's dQ (in S^T's columns) has been read out
+        if (ii > 0 && !(ok = mbar_poll(dq_free, par ^ 1u, err, kDevErrTimeoutTmemEmpty))) break;
+        tc_fence_after();
+        const uint32_t qbase = base + AbSmem::kQ + static_cast<uint32_t>(s * kAttTile);
+        const uint32_t dobase = base + AbSmem::kDO + static_cast<uint32_t>(s * kAttTile);
+#pragma unroll
+        for (int kk = 0; kk < kAttD / kUmmaK; ++kk) {
+          const uint32_t atom = static_cast<uint32_t>((kk >> 2) * kAttAtom + (kk & 3) * 32);
+          tc_mma_f16(t_s, make_sw128_desc(kbase + atom, 16u, 1024u), make_sw128_desc(qbase + atom, 16u, 1024u),
+                     idesc_kk, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < kAttD / kUmmaK; ++kk) {
+          const uint32_t atom = static_cast<uint32_t>((kk >> 2) * kAttAtom + (kk & 3) * 32);
+          tc_mma_f16(t_dp, make_sw128_desc(vbase + atom, 16u, 1024u), make_sw128_desc(dobase + atom, 16u, 1024u),
+                     idesc_kk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full);
+        // dV += P^T dO: A = P^T from TMEM (16 queries per step), B = dO as MN-major
+        // (d contiguous, 64-wide d blocks 16 KB apart, 16 query rows per step)
+        if (!(ok = mbar_poll(p_ready, par, err, kDevErrTimeoutFull))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kAttBQ / kUmmaK; ++kk)
+          tc_mma_f16_ts(t_dv, t_s + static_cast<uint32_t>((kk >> 2) * 64 + (kk & 3) * 8),
+                        make_sw128_desc(dobase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u), idesc_km,
+                        (ii > 0 || kk > 0) ? 1u : 0u);
+        // dK += dS^T Q, and this tile's dQ = dS K into S^T's columns (after the dV
+        // MMA read P^T there: one thread's MMAs run in order)
+        if (!(ok = mbar_poll(ds_ready, par, err, kDevErrTimeoutFull))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kAttBQ / kUmmaK; ++kk)
+          tc_mma_f16_ts(t_dk, t_dp + static_cast<uint32_t>((kk >> 2) * 64 + (kk & 3) * 8),
+                        make_sw128_desc(qbase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u), idesc_km,
+                        (ii > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kAttBK / kUmmaK; ++kk)
+          tc_mma_f16(t_s, make_sw128_desc(dsbase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u),
+                     make_sw128_desc(kbase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u), idesc_mm,
+                     kk > 0 ? 1u : 0u);
+        tc_commit(dq_full);
+        tc_commit(qd_empty(s));
+      }
+      if (ok) tc_commit(dkv_done);
+    }
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAttSoftmaxRegs));
+    const int quad = warp & 3;          // TMEM lane quarter
+    const int hh = (warp - 4) >> 2;     // column half: queries (and d) 64 hh .. 64 hh + 63
+    const int kr = quad * 32 + lane;    // key row of the tile
+    const int key = j * kAttBK + kr;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const float sc = p.scale_log2;
+    const float* lse_bh = p.lse + static_cast<int64_t>(bh) * p.T;
+    const float* d_bh = p.Dv + static_cast<int64_t>(bh) * p.T;
+    const uint32_t ds_row = base + AbSmem::kDS + static_cast<uint32_t>(hh * kAttAtom + kr * 128);
+    bool ok = true;
+    for (int ii = 0; ii < n_i; ++ii) {
+      const uint32_t par = static_cast<uint32_t>(ii & 1);
+      const int q0 = (j + ii) * kAttBQ + 64 * hh;  // first query of this warp's columns
+      if (!warp_poll(s_full, par, err, kDevErrTimeoutTmemFull, lane)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sx[2][32], dpx[2][32];
+      tmem_ld_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh), sx[0]);
+      tmem_ld_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh + 32), sx[1]);
+      tmem_ld_32x32b_x32(t_dp + lane_off + static_cast<uint32_t>(64 * hh), dpx[0]);
+      tmem_ld_32x32b_x32(t_dp + lane_off + static_cast<uint32_t>(64 * hh + 32), dpx[1]);
+      tmem_ld_wait();
+      // P^T and dS^T for queries q0 .. q0 + 63 (masked pairs give 0)
+      uint32_t pk[32], dk2[32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int q = q0 + 32 * c + i + e;
+            const bool valid = key <= q && q - key < p.window;
+            const float lq = __ldg(lse_bh + q) * 1.4426950408889634f;
+            const float pq = valid ? ex2_ftz(fmaf(__uint_as_float(sx[c][i + e]), sc, -lq)) : 0.0f;
+            pv[e] = pq;
+            dsv[e] = pq * (__uint_as_float(dpx[c][i + e]) - __ldg(d_bh + q));
+          }
+          pk[16 * c + i / 2] = pack_bf16x2(pv[0], pv[1]);
+          dk2[16 * c + i / 2] = pack_bf16x2(dsv[0], dsv[1]);
+        }
+      }
+      // P^T (query pairs) over the first 32 of the 64 S^T columns this warp read (the
+      // other warp of the lane quarter reads the other 64): the dV MMA may start
+      tmem_st_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh), pk);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      // dS^T over dP^T's columns, and dS into shared memory (the dQ MMA's A operand,
+      // queries contiguous: this row of 64 queries, 128-byte swizzled); the previous
+      // tile's dQ MMA, which read it, completed before this tile's S did
+      tmem_st_32x32b_x32(t_dp + lane_off + static_cast<uint32_t>(64 * hh), dk2);
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        st_shared_v4(ds_row + static_cast<uint32_t>((c ^ (kr & 7)) << 4),
+                     make_uint4(dk2[4 * c], dk2[4 * c + 1], dk2[4 * c + 2], dk2[4 * c + 3]));
+      fence_proxy_async_smem();
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_ready);
+      // this tile's dQ (TMEM lanes = queries 32 quad .., columns = d 64 hh ..) into
+      // the fp32 accumulator
+      if (!warp_poll(dq_full, par, err, kDevErrTimeoutTmemFull, lane)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t dq[2][32];
+      tmem_ld_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh), dq[0]);
+      tmem_ld_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh + 32), dq[1]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      float* dst = p.dq_acc + (static_cast<int64_t>(b * p.T + (j + ii) * kAttBQ + quad * 32 + lane) * p.H + h) * kAttD +
+                   64 * hh;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 32 * c + i),
+                       "f"(__uint_as_float(dq[c][i])), "f"(__uint_as_float(dq[c][i + 1])),
+                       "f"(__uint_as_float(dq[c][i + 2])), "f"(__uint_as_float(dq[c][i + 3]))
+                       : "memory");
+    }
+    // dK (scaled) and dV of this key tile: TMEM lanes = keys, columns = d 64 hh ..
+    if (ok && warp_poll(dkv_done, 0u, err, kDevErrTimeoutTmemFull, lane)) {
+      tc_fence_after();
+      const int64_t o = (static_cast<int64_t>(b * p.T + key) * p.H + h) * kAttD + 64 * hh;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        uint32_t x[2][32];
+        const uint32_t t = (which == 0 ? t_dk : t_dv) + lane_off + static_cast<uint32_t>(64 * hh);
+        tmem_ld_32x32b_x32(t, x[0]);
+        tmem_ld_32x32b_x32(t + 32u, x[1]);
+        tmem_ld_wait();
+        const float f = which == 0 ? p.scale : 1.0f;
+        __nv_bfloat16* d = (which == 0 ? p.dk : p.dv) + o;
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; i += 8)
+            st_global_v4(d + 32 * c + i,
+                         make_uint4(pack_bf16x2(__uint_as_float(x[c][i]) * f, __uint_as_float(x[c][i + 1]) * f),
+                                    pack_bf16x2(__uint_as_float(x[c][i + 2]) * f, __uint_as_float(x[c][i + 3]) * f),
+                                    pack_bf16x2(__uint_as_float(x[c][i + 4]) * f, __uint_as_float(x[c][i + 5]) * f),
+                                    pack_bf16x2(__uint_as_float(x[c][i + 6]) * f, __uint_as_float(x[c][i + 7]) * f)));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
 }  // namespace hlm
 
 using namespace hlm;
@@ -617,6 +977,84 @@ extern "C" int hlm_attention_fwd(const void* q, const void* k, const void* v, vo
   {
     LaunchScope scope(HLM_KERNEL_ATTN_FWD, s);
     attn_fwd_kernel<<<static_cast<unsigned>(grid), kAttThreads, smem, s>>>(mq, mk, mv, mo, p);
+  }
+  return launch_status();
+}
+
+extern "C" size_t hlm_attention_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t D) {
+  if (B <= 0 || T <= 0 || H <= 0 || D <= 0) return 0;
+  return static_cast<size_t>(B * T * H * D) * 4 + static_cast<size_t>(B * H * T) * 4 + 256;
+}
+
+extern "C" int hlm_attention_bwd(const void* grad_out, const void* q, const void* k, const void* v, const void* out,
+                                 const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                                 size_t workspace_bytes, int64_t B, int64_t T, int64_t H, int64_t Hk, int64_t D,
+                                 int64_t window, float scale, void* stream) {
+  if (B < 0 || T < 0 || H <= 0 || Hk <= 0 || D <= 0) return HLM_ERR_INVALID_ARG;
+  if (B == 0 || T == 0) return HLM_OK;
+  const void* ptrs[] = {grad_out, q, k, v, out, lse, dq, dk, dv, workspace};
+  for (const void* ptr : ptrs)
+    if (ptr == nullptr) return HLM_ERR_INVALID_ARG;
+  if (D != kAttD || T % kAttBQ != 0 || Hk != H) return HLM_ERR_UNSUPPORTED;
+  if (B * T * H > (1ll << 30)) return HLM_ERR_UNSUPPORTED;
+  for (const void* ptr : ptrs)
+    if (!host_aligned16(ptr)) return HLM_ERR_UNSUPPORTED;
+  if (workspace_bytes < hlm_attention_bwd_workspace_bytes(B, T, H, D)) return HLM_ERR_INVALID_ARG;
+  float* dq_acc = static_cast<float*>(workspace);
+  float* Dv = dq_acc + B * T * H * D;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int sms = num_sms_of_current_device();
+  if (cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(B * T * H * D) * 4, s) != cudaSuccess) return HLM_ERR_LAUNCH;
+  {
+    const int64_t rows = B * T * H;
+    int64_t blocks = (rows * 32 + 255) / 256;
+    if (blocks > static_cast<int64_t>(sms) * 8) blocks = static_cast<int64_t>(sms) * 8;
+    LaunchScope scope(HLM_KERNEL_ATTN_BWD, s);
+    attn_bwd_prep_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(grad_out), static_cast<const __nv_bfloat16*>(out), Dv, static_cast<int>(B),
+        static_cast<int>(T), static_cast<int>(H));
+  }
+  if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
+  CUtensorMap mq, mk, mv, mdo;
+  const int64_t rows = B * T;
+  if (!encode_bf16_map(&mq, q, H * D, rows, H * D, 128) || !encode_bf16_map(&mk, k, H * D, rows, H * D, 128) ||
+      !encode_bf16_map(&mv, v, H * D, rows, H * D, 128) || !encode_bf16_map(&mdo, grad_out, H * D, rows, H * D, 128))
+    return HLM_ERR_DRIVER;
+  AbParams p;
+  p.B = static_cast<int>(B);
+  p.T = static_cast<int>(T);
+  p.H = static_cast<int>(H);
+  p.window = window <= 0 || window >= T ? static_cast<int>(T) : static_cast<int>(window);
+  p.k_tiles = static_cast<int>(T / kAttBK);
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.lse = lse;
+  p.Dv = Dv;
+  p.dq_acc = dq_acc;
+  p.dk = static_cast<__nv_bfloat16*>(dk);
+  p.dv = static_cast<__nv_bfloat16*>(dv);
+  p.err = device_error_ptr();
+  if (p.err == nullptr) return HLM_ERR_LAUNCH;
+  const int smem = AbSmem::kBytes + 1024;
+  static_assert(AbSmem::kBytes + 1024 <= 232448, "shared memory budget exceeded");
+  if (cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return HLM_ERR_LAUNCH;
+  static const int compiled_regs = [] {
+    cudaFuncAttributes attr{};
+    return cudaFuncGetAttributes(&attr, attn_bwd_kernel) == cudaSuccess ? attr.numRegs : -1;
+  }();
+  if (compiled_regs != kAttLaunchRegs) return HLM_ERR_UNSUPPORTED;
+  {
+    LaunchScope scope(HLM_KERNEL_ATTN_BWD, s);
+    attn_bwd_kernel<<<static_cast<unsigned>(B * H * (T / kAttBK)), kAbThreads, smem, s>>>(mq, mk, mv, mdo, p);
+  }
+  if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
+  {
+    const int64_t n4 = B * T * H * D / 4;
+    int64_t blocks = (n4 + 255) / 256;
+    if (blocks > static_cast<int64_t>(sms) * 8) blocks = static_cast<int64_t>(sms) * 8;
+    LaunchScope scope(HLM_KERNEL_ATTN_BWD, s);
+    attn_dq_convert_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(dq_acc, scale, static_cast<__nv_bfloat16*>(dq), n4);
   }
   return launch_status();
 }

@@ -103,7 +103,8 @@ uint64_t hlm_launch_count(void);
 #define HLM_KERNEL_SWIGLU_DOWN_BWD 17 /* down grad_h GEMM + SwiGLU backward epilogue */
 #define HLM_KERNEL_PROJ_NORM 18    /* o_proj / down GEMM + residual add + RMSNorm epilogue */
 #define HLM_KERNEL_ATTN_FWD 19     /* attention forward (causal / sliding window) */
-#define HLM_KERNEL_MAX 20
+#define HLM_KERNEL_ATTN_BWD 20     /* attention backward (its three launches) */
+#define HLM_KERNEL_MAX 21
 
 /* Start timing every launch of kernel `kernel_id`: launch i records
  * start_events[i] immediately before and stop_events[i] immediately after
@@ -340,6 +341,20 @@ int hlm_proj_residual_rms_norm_fwd(const void* y, const void* w, const void* res
 int hlm_attention_fwd(const void* q, const void* k, const void* v, void* out, float* lse, int64_t B,
                       int64_t T, int64_t H, int64_t Hk, int64_t D, int64_t window, float scale,
                       void* stream);
+
+/* Gradients of hlm_attention_fwd: dq, dk, dv [B, T, H, 128] bf16 from grad_out
+ * and the forward's q, k, v, out and lse (natural log, [B, H, T] fp32), the same
+ * mask (window <= 0 or >= T: full causal), H == Hk.  workspace: at least
+ * hlm_attention_bwd_workspace_bytes(B, T, H, D) bytes (an fp32 dq accumulator and
+ * the per-row dot(dO, O)), 16-byte aligned.  Replaces the backward of the
+ * FlashAttention / SDPA call of kernels.scaled_dot_product_attention
+ * (kernels.py:774-847) with the window convention (window - 1, 0) of
+ * kernels.py:839.  Other shapes return HLM_ERR_UNSUPPORTED. */
+size_t hlm_attention_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t D);
+int hlm_attention_bwd(const void* grad_out, const void* q, const void* k, const void* v, const void* out,
+                      const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                      size_t workspace_bytes, int64_t B, int64_t T, int64_t H, int64_t Hk, int64_t D,
+                      int64_t window, float scale, void* stream);
 
 /* ------------------------------------------------------------------------
  * Plain tcgen05 GEMM (building block; also used by tests)

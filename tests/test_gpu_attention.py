@@ -146,13 +146,14 @@ def test_attention_d12_shape_vs_sdpa(cuda_device):
         assert _rel_l2(a, e.transpose(1, 2)) <= 1e-2, (name, _rel_l2(a, e.transpose(1, 2)))
 
 
-@pytest.mark.parametrize("backend", ["flash_attn_2", "sdpa"])
-def test_sliding_window_takes_the_b200_path(backend, cuda_device):
+@pytest.mark.parametrize("backend,bwd", [("flash_attn_2", "auto"), ("sdpa", "auto"), ("sdpa", "library")])
+def test_sliding_window_takes_the_b200_path(backend, bwd, cuda_device):
     """The reference entry point with a sliding window (its default pattern) runs the
-    tcgen05 forward under every backend name but "torch", and its gradients (flash_attn's
-    windowed backward when installed, else cuDNN with the window as a bias) match the
-    fp32 reference within the bar SDPA's own bf16 gradients set."""
-    from hackable_lm_b200 import _lib, kernels
+    tcgen05 forward under every backend name but "torch", and its gradients (the tcgen05
+    backward by default; flash_attn's windowed backward, or cuDNN with the window as a
+    bias, in "library" mode) match the fp32 reference within the bar SDPA's own bf16
+    gradients set."""
+    from hackable_lm_b200 import _lib, kernels, ops
 
     _lib.clear_device_error()
     B, T, H, W = 2, 512, 2, 160
@@ -165,10 +166,17 @@ def test_sliding_window_takes_the_b200_path(backend, cuda_device):
     with _lib.KernelTimer("attn_fwd", 4) as timer:
         out = kernels.scaled_dot_product_attention(*args, 0.0, is_causal=True, window_size=W, backend=backend)
     out = out if flash else out.transpose(1, 2)
-    out.backward(go)
+    old = ops.ATTENTION_BWD["mode"]
+    ops.ATTENTION_BWD["mode"] = bwd
+    try:
+        with _lib.KernelTimer("attn_bwd", 8) as btimer:
+            out.backward(go)
+    finally:
+        ops.ATTENTION_BWD["mode"] = old
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
     assert timer.launches == 1
+    assert btimer.launches == (3 if bwd == "auto" else 0)
     ref, _ = _ref(q, k, v, W)
     assert_bf16_close(out, ref, what="out")
     qr, kr, vr = (t.float().clone().requires_grad_(True) for t in (q, k, v))
@@ -176,5 +184,36 @@ def test_sliding_window_takes_the_b200_path(backend, cuda_device):
     ref_out.backward(go.float())
     for name, a, e, s in zip("qkv", (qd.grad, kd.grad, vd.grad), (qr.grad, kr.grad, vr.grad),
                              _sdpa_grads(q, k, v, go, W)):
+        sdpa_err = _rel_l2(s, e)
+        assert _rel_l2(a, e) <= 2 * sdpa_err + 1e-3, (name, _rel_l2(a, e), sdpa_err)
+
+
+@pytest.mark.parametrize("B,T,H,window", [(2, 256, 2, 0), (2, 512, 2, 160), (1, 384, 2, 200), (1, 1024, 1, 512),
+                                          (1, 128, 1, 0), (2, 512, 2, 1)])
+def test_attention_native_backward_vs_reference(B, T, H, window, cuda_device):
+    """hlm_attention_bwd (the tcgen05 backward) against fp32 gradients, within twice
+    the error SDPA's own bf16 gradients have on the same inputs."""
+    from hackable_lm_b200 import _lib, ops
+
+    _lib.clear_device_error()
+    q, k, v = _inputs(B, T, H, H, 8, cuda_device)
+    g = torch.Generator().manual_seed(9)
+    go = torch.randn(B, T, H, 128, generator=g).to(torch.bfloat16).to(cuda_device)
+    scale = 1.0 / math.sqrt(128)
+    out, lse = ops.attention(q, k, v, window, scale)
+    old = ops.ATTENTION_BWD["mode"]
+    ops.ATTENTION_BWD["mode"] = "native"
+    try:
+        with _lib.KernelTimer("attn_bwd", 8) as timer:
+            dq, dk, dv = ops.attention_backward(go, q, k, v, out, lse, window, scale)
+    finally:
+        ops.ATTENTION_BWD["mode"] = old
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert timer.launches == 3
+    qr, kr, vr = (t.float().clone().requires_grad_(True) for t in (q, k, v))
+    ref_out, _ = _ref(qr, kr, vr, window)
+    ref_out.backward(go.float())
+    for name, a, e, s in zip("qkv", (dq, dk, dv), (qr.grad, kr.grad, vr.grad), _sdpa_grads(q, k, v, go, window)):
         sdpa_err = _rel_l2(s, e)
         assert _rel_l2(a, e) <= 2 * sdpa_err + 1e-3, (name, _rel_l2(a, e), sdpa_err)
