@@ -574,24 +574,30 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 
 // ---------------------------------------------------------------------------
 // Attention backward (the same masks, head_dim 128, H == Hk):
-//   D[b,h,t]  = sum_d dO . O                                  (attn_bwd_prep_kernel)
-//   P^T       = 2^(S^T scale log2 e - lse log2 e), S^T = K Q^T, masked
+//   D[b,h,t]  = sum_d dO . O,  L[b,h,t] = lse log2 e           (attn_bwd_prep_kernel)
+//   P^T       = 2^(S^T scale log2 e - L), S^T = K Q^T, masked
 //   dP^T      = V dO^T,   dS^T = P^T (dP^T - D)
 //   dV += P^T dO,   dK += scale dS^T Q,   dQ += scale dS K    (attn_bwd_kernel)
 // One CTA per (b, h, key tile j) walks the query tiles i >= j that the window
 // reaches.  S^T, dP^T, dV and dK live in the 512 TMEM columns; P^T and dS^T are
 // written as bf16 pairs over columns 0-31 and 64-95 of S^T and dP^T (each warp of
-// a lane quarter over the half it read; the A operands of the dV and dK MMAs), dS also into shared memory in the MN-major layout of the
-// dQ MMA's A operand, and each tile's dQ (in S^T's columns, after the dV MMA read
-// P^T there) is added into an fp32 accumulator in global memory by the
-// eight compute warps (two per TMEM lane quarter, each taking half the columns),
-// which a last pass scales and rounds (attn_dq_convert_kernel).
+// a lane quarter over the half it read; the A operands of the dV and dK MMAs), dS
+// also into shared memory in the MN-major layout of the dQ^T MMA's B operand; each
+// tile's dQ^T = K^T dS^T (in S^T's columns, after the dV MMA read P^T there) is
+// added into an fp32 accumulator in global memory by the eight compute warps (two
+// per TMEM lane quarter, each taking half the queries), which a last pass scales
+// and rounds (attn_dq_convert_kernel).
 //   warp 0  TMA: K_j, V_j once, then Q_i, dO_i into a two-stage ring
 //   warp 1  TMEM owner and MMA issuer
 //   warps 4-11  P, dS, the dQ reduction and the dK / dV epilogue
 // Every wait is bounded.
 // ---------------------------------------------------------------------------
 constexpr int kAbThreads = 384;
+// register split after setmaxnreg (the launch holds 384 x 168): the MMA issuer's
+// descriptor loops want more than the forward's 56
+constexpr int kAbIssuerRegs = 72;
+constexpr int kAbComputeRegs = 216;
+static_assert(128 * kAbIssuerRegs + 256 * kAbComputeRegs <= kAbThreads * kAttLaunchRegs, "register split");
 struct AbSmem {
   static constexpr int kK = 0;                      // K_j (K-major atoms, d 0-63 / 64-127)
   static constexpr int kV = kK + kAttTile;          // V_j
@@ -611,7 +617,7 @@ struct AbParams {
   int k_tiles;       // T / 128
   float scale;       // softmax scale
   float scale_log2;  // softmax scale * log2(e)
-  const float* lse;  // [B, H, T] natural log
+  const float* lse2; // [B, H, T] log-sum-exp in base 2 (lse log2 e)
   const float* Dv;   // [B, H, T] rowsum(dO . O)
   float* dq_acc;     // [B, T, H, 128] fp32, zeroed
   __nv_bfloat16* dk; // [B, T, H, 128]
@@ -619,10 +625,12 @@ struct AbParams {
   int* err;
 };
 
-// D[b, h, t] = sum_d dO[b,t,h,d] O[b,t,h,d]: one warp per (b, t, h) row.
+// D[b, h, t] = sum_d dO[b,t,h,d] O[b,t,h,d] and L[b, h, t] = lse[b, h, t] log2 e:
+// one warp per (b, t, h) row.
 __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ dout,
                                                             const __nv_bfloat16* __restrict__ out,
-                                                            float* __restrict__ Dv, int B, int T, int H) {
+                                                            const float* __restrict__ lse, float* __restrict__ Dv,
+                                                            float* __restrict__ lse2, int B, int T, int H) {
   const int lane = threadIdx.x & 31;
   const int64_t rows = static_cast<int64_t>(B) * T * H;
   for (int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; row < rows;
@@ -637,7 +645,9 @@ __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const __nv_bfloat16*
       const int h = static_cast<int>(row - bt * H);
       const int64_t b = bt / T;
       const int64_t t = bt - b * T;
-      Dv[(b * H + h) * T + t] = acc;
+      const int64_t o = (b * H + h) * T + t;
+      Dv[o] = acc;
+      lse2[o] = lse[o] * 1.4426950408889634f;
     }
   }
 }
@@ -652,6 +662,41 @@ __global__ void __launch_bounds__(256) attn_dq_convert_kernel(const float* __res
     o.x = pack_bf16x2(x.x * scale, x.y * scale);
     o.y = pack_bf16x2(x.z * scale, x.w * scale);
     reinterpret_cast<uint2*>(dq)[v] = o;
+  }
+}
+
+// P^T = 2^(S^T sc - L) and dS^T = P^T (dP^T - D) of one key row over 64 queries,
+// packed as bf16 query pairs; L and D point at the first query's entries (16-byte
+// aligned; every lane reads the same, one transaction), dq0 = first query - key
+// (the pair is kept when 0 <= q - key < window).
+template <bool kMask>
+__device__ __forceinline__ void ab_p_ds(const uint32_t (&sx)[2][32], const uint32_t (&dpx)[2][32],
+                                        uint32_t (&pk)[32], uint32_t (&dk2)[32], const float* __restrict__ L,
+                                        const float* __restrict__ D, int dq0, int window, float sc) {
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 l4 = __ldg(reinterpret_cast<const float4*>(L + 32 * c + i));
+      const float4 d4 = __ldg(reinterpret_cast<const float4*>(D + 32 * c + i));
+      const float lq[4] = {l4.x, l4.y, l4.z, l4.w};
+      const float dq[4] = {d4.x, d4.y, d4.z, d4.w};
+      float pv[4], dsv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float pq = ex2_ftz(fmaf(__uint_as_float(sx[c][i + e]), sc, -lq[e]));
+        if (kMask) {
+          const int d = dq0 + 32 * c + i + e;
+          pq = (d >= 0 && d < window) ? pq : 0.0f;
+        }
+        pv[e] = pq;
+        dsv[e] = pq * (__uint_as_float(dpx[c][i + e]) - dq[e]);
+      }
+      pk[16 * c + i / 2] = pack_bf16x2(pv[0], pv[1]);
+      pk[16 * c + i / 2 + 1] = pack_bf16x2(pv[2], pv[3]);
+      dk2[16 * c + i / 2] = pack_bf16x2(dsv[0], dsv[1]);
+      dk2[16 * c + i / 2 + 1] = pack_bf16x2(dsv[2], dsv[3]);
+    }
   }
 }
 
@@ -719,7 +764,7 @@ __global__ void __launch_bounds__(kAbThreads, 1)
   const int row_k = b * p.T + j * kAttBK;
 
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttIssuerRegs));
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAbIssuerRegs));
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
@@ -753,7 +798,7 @@ __global__ void __launch_bounds__(kAbThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_kk = make_idesc_bf16_f32(128, 128, false, false);  // S^T, dP^T
       constexpr uint32_t idesc_km = make_idesc_bf16_f32(128, 128, false, true);   // dV, dK (A in TMEM)
-      constexpr uint32_t idesc_mm = make_idesc_bf16_f32(128, 128, true, true);    // dQ
+      constexpr uint32_t idesc_mm = make_idesc_bf16_f32(128, 128, true, true);    // dQ^T
       bool ok = mbar_poll(kv_full, 0u, err, kDevErrTimeoutFull);
       const uint32_t kbase = base + AbSmem::kK, vbase = base + AbSmem::kV, dsbase = base + AbSmem::kDS;
       for (int ii = 0; ii < n_i && ok; ++ii) {
@@ -787,8 +832,9 @@ __global__ void __launch_bounds__(kAbThreads, 1)
           tc_mma_f16_ts(t_dv, t_s + static_cast<uint32_t>((kk >> 2) * 64 + (kk & 3) * 8),
                         make_sw128_desc(dobase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u), idesc_km,
                         (ii > 0 || kk > 0) ? 1u : 0u);
-        // dK += dS^T Q, and this tile's dQ = dS K into S^T's columns (after the dV
-        // MMA read P^T there: one thread's MMAs run in order)
+        // dK += dS^T Q, and this tile's dQ^T = K^T dS^T into S^T's columns (after
+        // the dV MMA read P^T there: one thread's MMAs run in order); A = K as
+        // MN-major (d contiguous), B = dS as MN-major (queries contiguous)
         if (!(ok = mbar_poll(ds_ready, par, err, kDevErrTimeoutFull))) break;
         tc_fence_after();
 #pragma unroll
@@ -798,8 +844,8 @@ __global__ void __launch_bounds__(kAbThreads, 1)
                         (ii > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kAttBK / kUmmaK; ++kk)
-          tc_mma_f16(t_s, make_sw128_desc(dsbase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u),
-                     make_sw128_desc(kbase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u), idesc_mm,
+          tc_mma_f16(t_s, make_sw128_desc(kbase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u),
+                     make_sw128_desc(dsbase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u), idesc_mm,
                      kk > 0 ? 1u : 0u);
         tc_commit(dq_full);
         tc_commit(qd_empty(s));
@@ -808,15 +854,13 @@ __global__ void __launch_bounds__(kAbThreads, 1)
     }
   }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAttSoftmaxRegs));
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAbComputeRegs));
     const int quad = warp & 3;          // TMEM lane quarter
     const int hh = (warp - 4) >> 2;     // column half: queries (and d) 64 hh .. 64 hh + 63
     const int kr = quad * 32 + lane;    // key row of the tile
     const int key = j * kAttBK + kr;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const float sc = p.scale_log2;
-    const float* lse_bh = p.lse + static_cast<int64_t>(bh) * p.T;
-    const float* d_bh = p.Dv + static_cast<int64_t>(bh) * p.T;
     const uint32_t ds_row = base + AbSmem::kDS + static_cast<uint32_t>(hh * kAttAtom + kr * 128);
     bool ok = true;
     for (int ii = 0; ii < n_i; ++ii) {
@@ -833,26 +877,14 @@ __global__ void __launch_bounds__(kAbThreads, 1)
       tmem_ld_32x32b_x32(t_dp + lane_off + static_cast<uint32_t>(64 * hh), dpx[0]);
       tmem_ld_32x32b_x32(t_dp + lane_off + static_cast<uint32_t>(64 * hh + 32), dpx[1]);
       tmem_ld_wait();
-      // P^T and dS^T for queries q0 .. q0 + 63 (masked pairs give 0)
+      // P^T and dS^T for queries q0 .. q0 + 63 (masked pairs give 0; only the
+      // diagonal tile and the tiles the window edge crosses hold any)
       uint32_t pk[32], dk2[32];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float pv[2], dsv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int q = q0 + 32 * c + i + e;
-            const bool valid = key <= q && q - key < p.window;
-            const float lq = __ldg(lse_bh + q) * 1.4426950408889634f;
-            const float pq = valid ? ex2_ftz(fmaf(__uint_as_float(sx[c][i + e]), sc, -lq)) : 0.0f;
-            pv[e] = pq;
-            dsv[e] = pq * (__uint_as_float(dpx[c][i + e]) - __ldg(d_bh + q));
-          }
-          pk[16 * c + i / 2] = pack_bf16x2(pv[0], pv[1]);
-          dk2[16 * c + i / 2] = pack_bf16x2(dsv[0], dsv[1]);
-        }
-      }
+      const int64_t stat = static_cast<int64_t>(bh) * p.T + q0;
+      if (ii == 0 || kAttBQ * ii + kAttBQ - 1 >= p.window)
+        ab_p_ds<true>(sx, dpx, pk, dk2, p.lse2 + stat, p.Dv + stat, q0 - key, p.window, sc);
+      else
+        ab_p_ds<false>(sx, dpx, pk, dk2, p.lse2 + stat, p.Dv + stat, q0 - key, p.window, sc);
       // P^T (query pairs) over the first 32 of the 64 S^T columns this warp read (the
       // other warp of the lane quarter reads the other 64): the dV MMA may start
       tmem_st_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh), pk);
@@ -873,8 +905,9 @@ __global__ void __launch_bounds__(kAbThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_ready);
-      // this tile's dQ (TMEM lanes = queries 32 quad .., columns = d 64 hh ..) into
-      // the fp32 accumulator
+      // this tile's dQ^T (TMEM lanes = d 32 quad .., columns = queries 64 hh ..) into
+      // the fp32 accumulator: each warp instruction adds one query's 32 d, a
+      // contiguous 128-byte line
       if (!warp_poll(dq_full, par, err, kDevErrTimeoutTmemFull, lane)) {
         ok = false;
         break;
@@ -887,15 +920,13 @@ __global__ void __launch_bounds__(kAbThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
-      float* dst = p.dq_acc + (static_cast<int64_t>(b * p.T + (j + ii) * kAttBQ + quad * 32 + lane) * p.H + h) * kAttD +
-                   64 * hh;
+      float* dst = p.dq_acc + (static_cast<int64_t>(b * p.T + q0) * p.H + h) * kAttD + quad * 32 + lane;
+      const int64_t qstride = static_cast<int64_t>(p.H) * kAttD;
 #pragma unroll
       for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + 32 * c + i),
-                       "f"(__uint_as_float(dq[c][i])), "f"(__uint_as_float(dq[c][i + 1])),
-                       "f"(__uint_as_float(dq[c][i + 2])), "f"(__uint_as_float(dq[c][i + 3]))
+        for (int i = 0; i < 32; ++i)
+          asm volatile("red.global.add.f32 [%0], %1;" ::"l"(dst + (32 * c + i) * qstride), "f"(__uint_as_float(dq[c][i]))
                        : "memory");
     }
     // dK (scaled) and dV of this key tile: TMEM lanes = keys, columns = d 64 hh ..
@@ -983,7 +1014,7 @@ extern "C" int hlm_attention_fwd(const void* q, const void* k, const void* v, vo
 
 extern "C" size_t hlm_attention_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t D) {
   if (B <= 0 || T <= 0 || H <= 0 || D <= 0) return 0;
-  return static_cast<size_t>(B * T * H * D) * 4 + static_cast<size_t>(B * H * T) * 4 + 256;
+  return static_cast<size_t>(B * T * H * D) * 4 + static_cast<size_t>(B * H * T) * 8 + 256;
 }
 
 extern "C" int hlm_attention_bwd(const void* grad_out, const void* q, const void* k, const void* v, const void* out,
@@ -1002,6 +1033,7 @@ extern "C" int hlm_attention_bwd(const void* grad_out, const void* q, const void
   if (workspace_bytes < hlm_attention_bwd_workspace_bytes(B, T, H, D)) return HLM_ERR_INVALID_ARG;
   float* dq_acc = static_cast<float*>(workspace);
   float* Dv = dq_acc + B * T * H * D;
+  float* lse2 = Dv + B * H * T;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int sms = num_sms_of_current_device();
   if (cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(B * T * H * D) * 4, s) != cudaSuccess) return HLM_ERR_LAUNCH;
@@ -1011,7 +1043,7 @@ extern "C" int hlm_attention_bwd(const void* grad_out, const void* q, const void
     if (blocks > static_cast<int64_t>(sms) * 8) blocks = static_cast<int64_t>(sms) * 8;
     LaunchScope scope(HLM_KERNEL_ATTN_BWD, s);
     attn_bwd_prep_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(grad_out), static_cast<const __nv_bfloat16*>(out), Dv, static_cast<int>(B),
+        static_cast<const __nv_bfloat16*>(grad_out), static_cast<const __nv_bfloat16*>(out), lse, Dv, lse2, static_cast<int>(B),
         static_cast<int>(T), static_cast<int>(H));
   }
   if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
@@ -1028,7 +1060,7 @@ extern "C" int hlm_attention_bwd(const void* grad_out, const void* q, const void
   p.k_tiles = static_cast<int>(T / kAttBK);
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.lse = lse;
+  p.lse2 = lse2;
   p.Dv = Dv;
   p.dq_acc = dq_acc;
   p.dk = static_cast<__nv_bfloat16*>(dk);

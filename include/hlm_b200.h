@@ -345,8 +345,8 @@ int hlm_attention_fwd(const void* q, const void* k, const void* v, void* out, fl
 /* Gradients of hlm_attention_fwd: dq, dk, dv [B, T, H, 128] bf16 from grad_out
  * and the forward's q, k, v, out and lse (natural log, [B, H, T] fp32), the same
  * mask (window <= 0 or >= T: full causal), H == Hk.  workspace: at least
- * hlm_attention_bwd_workspace_bytes(B, T, H, D) bytes (an fp32 dq accumulator and
- * the per-row dot(dO, O)), 16-byte aligned.  Replaces the backward of the
+ * hlm_attention_bwd_workspace_bytes(B, T, H, D) bytes (an fp32 dq accumulator,
+ * the per-row dot(dO, O) and the log-sum-exp in base 2), 16-byte aligned.  Replaces the backward of the
  * FlashAttention / SDPA call of kernels.scaled_dot_product_attention
  * (kernels.py:774-847) with the window convention (window - 1, 0) of
  * kernels.py:839.  Other shapes return HLM_ERR_UNSUPPORTED. */
