@@ -577,36 +577,54 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 //   D[b,h,t]  = sum_d dO . O,  L[b,h,t] = lse log2 e           (attn_bwd_prep_kernel)
 //   P^T       = 2^(S^T scale log2 e - L), S^T = K Q^T, masked
 //   dP^T      = V dO^T,   dS^T = P^T (dP^T - D)
-//   dV += P^T dO,   dK += scale dS^T Q,   dQ += scale dS K    (attn_bwd_kernel)
-// One CTA per (b, h, key tile j) walks the query tiles i >= j that the window
-// reaches.  S^T, dP^T, dV and dK live in the 512 TMEM columns; P^T and dS^T are
-// written as bf16 pairs over columns 0-31 and 64-95 of S^T and dP^T (each warp of
-// a lane quarter over the half it read; the A operands of the dV and dK MMAs), dS
-// also into shared memory in the MN-major layout of the dQ^T MMA's B operand; each
-// tile's dQ^T = K^T dS^T (in S^T's columns, after the dV MMA read P^T there) is
-// added into an fp32 accumulator in global memory by the eight compute warps (two
-// per TMEM lane quarter, each taking half the queries), which a last pass scales
-// and rounds (attn_dq_convert_kernel).
-//   warp 0  TMA: K_j, V_j once, then Q_i, dO_i into a two-stage ring
+//   dV += P^T dO,   dK += scale dS^T Q,   dQ^T += scale K^T dS^T  (attn_bwd_kernel)
+// One CTA per (b, h, key tile j of 128 keys) walks the 64-query blocks the window
+// reaches from tile j.  Tensor memory: two stages of [S^T | dP^T] (64 + 64
+// columns each), dV (256-383) and dK (384-511).  Per block:
+//   MMA   S^T, dP^T into the block's stage (issued two blocks ahead: S^T right
+//         after the dV MMA of the block before in that stage, dP^T once that
+//         block's dQ^T has been read out);
+//   warps 4-11 (lane quarter = 32 keys, half = 32 queries) read S^T, dP^T, write
+//         P^T as bf16 pairs over the first 16 of their S^T columns (the A operand
+//         of the dV MMA) and dS into shared memory (K-major A of the dK MMA and
+//         MN-major B of the dQ^T MMA);
+//   MMA   dV += P^T dO, dK += dS^T Q, dQ^T = K^T dS^T over the stage's dP^T
+//         columns (read into registers before the compute warps signalled);
+//   warps 12-15 (one per lane quarter = 32 d) read dQ^T and add it into an fp32
+//         accumulator in global memory, one 128-byte line per warp instruction
+//         (reductions the L2 takes at its own rate, off the compute warps' path);
+//         a last pass scales and rounds it (attn_dq_convert_kernel).
+//   warp 0  TMA: K_j, V_j once, then Q, dO blocks (and L, D of their queries)
+//           into a three-stage ring
 //   warp 1  TMEM owner and MMA issuer
-//   warps 4-11  P, dS, the dQ reduction and the dK / dV epilogue
-// Every wait is bounded.
+// The producer and the other warps wait suspended in mbarrier.try_wait (they
+// share their schedulers with the MMA issuer, whose issue rate a spinning poll
+// would take slots from); the issuer polls.  Every wait is bounded.
 // ---------------------------------------------------------------------------
-constexpr int kAbThreads = 384;
-// register split after setmaxnreg (the launch holds 384 x 168): the MMA issuer's
-// descriptor loops want more than the forward's 56
+constexpr int kAbThreads = 512;
+constexpr int kAbLaunchRegs = 128;  // 65536 / 512
+// register split after setmaxnreg: producer / MMA warpgroup, two compute
+// warpgroups, the dQ warpgroup (128 x 72 + 256 x 168 + 128 x 104 = 65536)
 constexpr int kAbIssuerRegs = 72;
-constexpr int kAbComputeRegs = 216;
-static_assert(128 * kAbIssuerRegs + 256 * kAbComputeRegs <= kAbThreads * kAttLaunchRegs, "register split");
+constexpr int kAbComputeRegs = 168;
+constexpr int kAbReduceRegs = 104;
+static_assert(128 * kAbIssuerRegs + 256 * kAbComputeRegs + 128 * kAbReduceRegs <= kAbThreads * kAbLaunchRegs,
+              "register split");
+constexpr int kAbBQ = 64;                   // queries per block
+constexpr int kAbAtom = kAbBQ * 128;        // one 64-row x 64-column bf16 swizzle atom (8 KB)
+constexpr int kAbBlock = 2 * kAbAtom;       // one 64 x 128 bf16 block (16 KB)
+constexpr int kAbStages = 3;                // Q / dO ring
 struct AbSmem {
-  static constexpr int kK = 0;                      // K_j (K-major atoms, d 0-63 / 64-127)
-  static constexpr int kV = kK + kAttTile;          // V_j
-  static constexpr int kQ = kV + kAttTile;          // Q_i, two stages
-  static constexpr int kDO = kQ + 2 * kAttTile;     // dO_i, two stages
-  static constexpr int kDS = kDO + 2 * kAttTile;    // dS: query blocks [128 keys][64 queries] (MN-major A)
-  static constexpr int kBars = kDS + kAttTile;
-  // kv_full, qd_full[2], qd_empty[2], s_full, p_ready, ds_ready, dq_full, dq_free, dkv_done
-  static constexpr int kNumBars = 11;
+  static constexpr int kK = 0;                          // K_j (K-major atoms, d 0-63 / 64-127)
+  static constexpr int kV = kK + kAttTile;              // V_j
+  static constexpr int kQ = kV + kAttTile;              // Q blocks, kAbStages stages
+  static constexpr int kDO = kQ + kAbStages * kAbBlock; // dO blocks
+  static constexpr int kDS = kDO + kAbStages * kAbBlock;  // dS per TMEM stage: [128 keys][64 queries], 128-byte swizzle
+  static constexpr int kStats = kDS + 2 * kAbBlock;   // per Q / dO stage: L[64], D[64] fp32
+  static constexpr int kStatBytes = 2 * kAbBQ * 4;
+  static constexpr int kBars = kStats + kAbStages * kStatBytes;
+  // kv_full, qd_full[3], qd_empty[3], s_full[2], pds_ready[2], dq_full[2], dq_free[2], dkv_done
+  static constexpr int kNumBars = 16;
   static constexpr int kTmemSlot = kBars + kNumBars * 8;
   static constexpr int kBytes = kTmemSlot + 16;
 };
@@ -614,7 +632,6 @@ struct AbSmem {
 struct AbParams {
   int B, T, H;
   int window;        // keys with t - k < window (window >= T: full causal)
-  int k_tiles;       // T / 128
   float scale;       // softmax scale
   float scale_log2;  // softmax scale * log2(e)
   const float* lse2; // [B, H, T] log-sum-exp in base 2 (lse log2 e)
@@ -665,39 +682,52 @@ __global__ void __launch_bounds__(256) attn_dq_convert_kernel(const float* __res
   }
 }
 
-// P^T = 2^(S^T sc - L) and dS^T = P^T (dP^T - D) of one key row over 64 queries,
-// packed as bf16 query pairs; L and D point at the first query's entries (16-byte
-// aligned; every lane reads the same, one transaction), dq0 = first query - key
+HLM_DEVICE void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0],"
+      " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// P^T = 2^(S^T sc - L) and dS^T = P^T (dP^T - D) of one key row over 32 queries,
+// packed as bf16 query pairs; L and D are the shared-memory addresses of the first
+// query's entries (every lane reads the same 16 bytes), dq0 = first query - key
 // (the pair is kept when 0 <= q - key < window).
 template <bool kMask>
-__device__ __forceinline__ void ab_p_ds(const uint32_t (&sx)[2][32], const uint32_t (&dpx)[2][32],
-                                        uint32_t (&pk)[32], uint32_t (&dk2)[32], const float* __restrict__ L,
-                                        const float* __restrict__ D, int dq0, int window, float sc) {
+__device__ __forceinline__ void ab_p_ds(const uint32_t (&sx)[32], const uint32_t (&dpx)[32], uint32_t (&pk)[16],
+                                        uint32_t (&dk2)[16], uint32_t L, uint32_t D, int dq0, int window, float sc) {
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
+  for (int i = 0; i < 32; i += 4) {
+    const uint4 l4 = ld_shared_v4(L + static_cast<uint32_t>(i * 4));
+    const uint4 d4 = ld_shared_v4(D + static_cast<uint32_t>(i * 4));
+    const float lq[4] = {__uint_as_float(l4.x), __uint_as_float(l4.y), __uint_as_float(l4.z), __uint_as_float(l4.w)};
+    const float dq[4] = {__uint_as_float(d4.x), __uint_as_float(d4.y), __uint_as_float(d4.z), __uint_as_float(d4.w)};
+    float pv[4], dsv[4];
 #pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      const float4 l4 = __ldg(reinterpret_cast<const float4*>(L + 32 * c + i));
-      const float4 d4 = __ldg(reinterpret_cast<const float4*>(D + 32 * c + i));
-      const float lq[4] = {l4.x, l4.y, l4.z, l4.w};
-      const float dq[4] = {d4.x, d4.y, d4.z, d4.w};
-      float pv[4], dsv[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float pq = ex2_ftz(fmaf(__uint_as_float(sx[c][i + e]), sc, -lq[e]));
-        if (kMask) {
-          const int d = dq0 + 32 * c + i + e;
-          pq = (d >= 0 && d < window) ? pq : 0.0f;
-        }
-        pv[e] = pq;
-        dsv[e] = pq * (__uint_as_float(dpx[c][i + e]) - dq[e]);
+    for (int e = 0; e < 4; ++e) {
+      float pq = ex2_ftz(fmaf(__uint_as_float(sx[i + e]), sc, -lq[e]));
+      if (kMask) {
+        const int d = dq0 + i + e;
+        pq = (d >= 0 && d < window) ? pq : 0.0f;
       }
-      pk[16 * c + i / 2] = pack_bf16x2(pv[0], pv[1]);
-      pk[16 * c + i / 2 + 1] = pack_bf16x2(pv[2], pv[3]);
-      dk2[16 * c + i / 2] = pack_bf16x2(dsv[0], dsv[1]);
-      dk2[16 * c + i / 2 + 1] = pack_bf16x2(dsv[2], dsv[3]);
+      pv[e] = pq;
+      dsv[e] = pq * (__uint_as_float(dpx[i + e]) - dq[e]);
     }
+    pk[i / 2] = pack_bf16x2(pv[0], pv[1]);
+    pk[i / 2 + 1] = pack_bf16x2(pv[2], pv[3]);
+    dk2[i / 2] = pack_bf16x2(dsv[0], dsv[1]);
+    dk2[i / 2 + 1] = pack_bf16x2(dsv[2], dsv[3]);
   }
+}
+
+// One block's dQ^T column slice (this thread's d, 32 queries qstride apart) added
+// into the fp32 accumulator.
+HLM_DEVICE void ab_dq_reduce(float* dst, int64_t qstride, const uint32_t (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(dst + i * qstride), "f"(__uint_as_float(v[i])) : "memory");
 }
 
 __global__ void __launch_bounds__(kAbThreads, 1)
@@ -713,36 +743,41 @@ __global__ void __launch_bounds__(kAbThreads, 1)
   int* err = p.err;
 
   // work item: key tile j of one (b, h), key tiles in increasing order over the
-  // grid (the lowest see the most query tiles under the causal mask)
+  // grid (the lowest see the most query blocks under the causal mask)
   const int BH = p.B * p.H;
   const int j = static_cast<int>(blockIdx.x) / BH;
   const int bh = static_cast<int>(blockIdx.x) - j * BH;
   const int b = bh / p.H;
   const int h = bh - b * p.H;
-  // query tiles j .. i_last: the window reaches query tile i from key tile j while
-  // 128 (i - j) - 127 < window
-  const int i_last = min(p.k_tiles - 1, j + (p.window + 126) / kAttBQ);
-  const int n_i = i_last - j + 1;
+  // query blocks qb0 .. qb_last: query q sees a key of tile j while
+  // 0 <= q - k < window for some k in [128 j, 128 j + 127]
+  const int qb0 = j * (kAttBK / kAbBQ);
+  const int qb_last = min(p.T / kAbBQ - 1, (j * kAttBK + kAttBK - 2 + p.window) / kAbBQ);
+  const int n_i = qb_last - qb0 + 1;
 
   const uint32_t bar0 = base + AbSmem::kBars;
   const uint32_t kv_full = bar0;
   auto qd_full = [&](int s) { return bar0 + 8u * static_cast<uint32_t>(1 + s); };
-  auto qd_empty = [&](int s) { return bar0 + 8u * static_cast<uint32_t>(3 + s); };
-  const uint32_t s_full = bar0 + 40, p_ready = bar0 + 48, ds_ready = bar0 + 56, dq_full = bar0 + 64,
-                 dq_free = bar0 + 72, dkv_done = bar0 + 80;
+  auto qd_empty = [&](int s) { return bar0 + 8u * static_cast<uint32_t>(4 + s); };
+  auto s_full = [&](int st) { return bar0 + 8u * static_cast<uint32_t>(7 + st); };
+  auto pds_ready = [&](int st) { return bar0 + 8u * static_cast<uint32_t>(9 + st); };
+  auto dq_full = [&](int st) { return bar0 + 8u * static_cast<uint32_t>(11 + st); };
+  auto dq_free = [&](int st) { return bar0 + 8u * static_cast<uint32_t>(13 + st); };
+  const uint32_t dkv_done = bar0 + 8u * 15u;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base_ptr + AbSmem::kTmemSlot);
 
   if (warp == 0 && lane == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kAbStages; ++s) {
       mbar_init(qd_full(s), 1);
       mbar_init(qd_empty(s), 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_ready, 8);
-    mbar_init(ds_ready, 8);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_free, 8);
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(s_full(st), 1);
+      mbar_init(pds_ready(st), 8);
+      mbar_init(dq_full(st), 1);
+      mbar_init(dq_free(st), 4);
+    }
     mbar_init(dkv_done, 1);
     fence_mbar_init();
     prefetch_tensormap(&tmQ);
@@ -758,179 +793,179 @@ __global__ void __launch_bounds__(kAbThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
-  // TMEM columns: S^T 0-127 (P^T over 0-31 and 64-95; then this tile's dQ over
-  // 0-127), dP^T 128-255 (dS^T over 128-159 and 192-223), dV 256-383, dK 384-511
-  const uint32_t t_s = tmem_base, t_dp = tmem_base + 128u, t_dv = tmem_base + 256u, t_dk = tmem_base + 384u;
+  // stage st: S^T (then P^T over its first columns) at 128 st, dP^T (then the
+  // block's dQ^T) at 128 st + 64
+  auto t_stage = [&](int st) { return tmem_base + 128u * static_cast<uint32_t>(st); };
+  const uint32_t t_dv = tmem_base + 256u, t_dk = tmem_base + 384u;
   const int row_k = b * p.T + j * kAttBK;
 
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAbIssuerRegs));
   if (warp == 0) {
     if (lane == 0) {
-      bool ok = true;
       mbar_arrive_expect_tx(kv_full, 2 * kAttTile);
       for (int a = 0; a < 2; ++a) {
         tma_load_2d(base + AbSmem::kK + static_cast<uint32_t>(a * kAttAtom), &tmK, h * kAttD + 64 * a, row_k, kv_full);
         tma_load_2d(base + AbSmem::kV + static_cast<uint32_t>(a * kAttAtom), &tmV, h * kAttD + 64 * a, row_k, kv_full);
       }
       int issued = 0;
-      for (int ii = 0; ii < n_i && ok; ++ii) {
-        const int s = ii & 1;
-        if (ii >= 2 && !mbar_poll(qd_empty(s), static_cast<uint32_t>(((ii >> 1) - 1) & 1), err, kDevErrTimeoutEmpty)) {
-          ok = false;
+      for (int ii = 0; ii < n_i; ++ii) {
+        const int s = ii % kAbStages;
+        if (ii >= kAbStages &&
+            !mbar_wait(qd_empty(s), static_cast<uint32_t>((ii / kAbStages - 1) & 1), err, kDevErrTimeoutEmpty))
           break;
-        }
-        const int row_q = b * p.T + (j + ii) * kAttBQ;
-        mbar_arrive_expect_tx(qd_full(s), 2 * kAttTile);
+        const int row_q = b * p.T + (qb0 + ii) * kAbBQ;
+        const int64_t stat = static_cast<int64_t>(bh) * p.T + (qb0 + ii) * kAbBQ;
+        const uint32_t stats = base + AbSmem::kStats + static_cast<uint32_t>(s * AbSmem::kStatBytes);
+        mbar_arrive_expect_tx(qd_full(s), 2 * kAbBlock + AbSmem::kStatBytes);
+        bulk_load_1d(stats, p.lse2 + stat, kAbBQ * 4, qd_full(s));
+        bulk_load_1d(stats + kAbBQ * 4, p.Dv + stat, kAbBQ * 4, qd_full(s));
         for (int a = 0; a < 2; ++a) {
-          tma_load_2d(base + AbSmem::kQ + static_cast<uint32_t>(s * kAttTile + a * kAttAtom), &tmQ, h * kAttD + 64 * a,
+          tma_load_2d(base + AbSmem::kQ + static_cast<uint32_t>(s * kAbBlock + a * kAbAtom), &tmQ, h * kAttD + 64 * a,
                       row_q, qd_full(s));
-          tma_load_2d(base + AbSmem::kDO + static_cast<uint32_t>(s * kAttTile + a * kAttAtom), &tmDO,
+          tma_load_2d(base + AbSmem::kDO + static_cast<uint32_t>(s * kAbBlock + a * kAbAtom), &tmDO,
                       h * kAttD + 64 * a, row_q, qd_full(s));
         }
         issued = ii + 1;
       }
       mbar_wait_drain(kv_full, 0u, err);
-      for (int ii = max(0, issued - 2); ii < issued; ++ii)
-        mbar_wait_drain(qd_full(ii & 1), static_cast<uint32_t>((ii >> 1) & 1), err);
+      for (int ii = max(0, issued - kAbStages); ii < issued; ++ii)
+        mbar_wait_drain(qd_full(ii % kAbStages), static_cast<uint32_t>((ii / kAbStages) & 1), err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc_kk = make_idesc_bf16_f32(128, 128, false, false);  // S^T, dP^T
-      constexpr uint32_t idesc_km = make_idesc_bf16_f32(128, 128, false, true);   // dV, dK (A in TMEM)
-      constexpr uint32_t idesc_mm = make_idesc_bf16_f32(128, 128, true, true);    // dQ^T
+      constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, kAbBQ, false, false);  // S^T, dP^T
+      constexpr uint32_t idesc_kv = make_idesc_bf16_f32(128, 128, false, true);    // dV (A in TMEM), dK
+      constexpr uint32_t idesc_q = make_idesc_bf16_f32(128, kAbBQ, true, true);    // dQ^T
+      const uint64_t dk_kmaj = make_sw128_desc(base + AbSmem::kK, 16u, 1024u);
+      const uint64_t dv_kmaj = make_sw128_desc(base + AbSmem::kV, 16u, 1024u);
+      const uint64_t dk_mn = make_sw128_desc(base + AbSmem::kK, kAttAtom, 1024u);
+      // S^T = K Q^T and dP^T = V dO^T of block ii into its stage, once the block
+      // two before it (same stage) has had its dQ^T read out
+      // S^T = K Q^T of block ii into its stage's S^T columns (descriptors advance by
+      // the operand offset / 16: the address field, no carry out of it inside
+      // shared memory); the block's Q / dO stage must have landed
+      auto issue_s = [&](int ii) -> bool {
+        const int s = ii % kAbStages;
+        if (!mbar_poll(qd_full(s), static_cast<uint32_t>((ii / kAbStages) & 1), err, kDevErrTimeoutFull)) return false;
+        tc_fence_after();
+        const uint64_t dq_ = make_sw128_desc(base + AbSmem::kQ + static_cast<uint32_t>(s * kAbBlock), 16u, 1024u);
+#pragma unroll
+        for (int kk = 0; kk < kAttD / kUmmaK; ++kk)
+          tc_mma_f16(t_stage(ii & 1), dk_kmaj + ((kk >> 2) * kAttAtom + (kk & 3) * 32) / 16,
+                     dq_ + ((kk >> 2) * kAbAtom + (kk & 3) * 32) / 16, idesc_s, kk > 0 ? 1u : 0u);
+        return true;
+      };
+      // dP^T = V dO^T of block ii into its stage's dP^T columns, then publish the stage
+      auto issue_dp = [&](int ii) {
+        const int s = ii % kAbStages;
+        const uint64_t ddo = make_sw128_desc(base + AbSmem::kDO + static_cast<uint32_t>(s * kAbBlock), 16u, 1024u);
+#pragma unroll
+        for (int kk = 0; kk < kAttD / kUmmaK; ++kk)
+          tc_mma_f16(t_stage(ii & 1) + 64u, dv_kmaj + ((kk >> 2) * kAttAtom + (kk & 3) * 32) / 16,
+                     ddo + ((kk >> 2) * kAbAtom + (kk & 3) * 32) / 16, idesc_s, kk > 0 ? 1u : 0u);
+        tc_commit(s_full(ii & 1));
+      };
       bool ok = mbar_poll(kv_full, 0u, err, kDevErrTimeoutFull);
-      const uint32_t kbase = base + AbSmem::kK, vbase = base + AbSmem::kV, dsbase = base + AbSmem::kDS;
+      for (int ii = 0; ii < 2 && ii < n_i && ok; ++ii)
+        if ((ok = issue_s(ii))) issue_dp(ii);
       for (int ii = 0; ii < n_i && ok; ++ii) {
-        const int s = ii & 1;
-        const uint32_t par = static_cast<uint32_t>(ii & 1);
-        if (!(ok = mbar_poll(qd_full(s), static_cast<uint32_t>((ii >> 1) & 1), err, kDevErrTimeoutFull))) break;
-        // the previous tile's dQ (in S^T's columns) has been read out
-        if (ii > 0 && !(ok = mbar_poll(dq_free, par ^ 1u, err, kDevErrTimeoutTmemEmpty))) break;
+        const int s = ii % kAbStages, st = ii & 1;
+        if (!(ok = mbar_poll(pds_ready(st), static_cast<uint32_t>((ii >> 1) & 1), err, kDevErrTimeoutFull))) break;
         tc_fence_after();
-        const uint32_t qbase = base + AbSmem::kQ + static_cast<uint32_t>(s * kAttTile);
-        const uint32_t dobase = base + AbSmem::kDO + static_cast<uint32_t>(s * kAttTile);
+        const uint32_t qbase = base + AbSmem::kQ + static_cast<uint32_t>(s * kAbBlock);
+        const uint32_t dobase = base + AbSmem::kDO + static_cast<uint32_t>(s * kAbBlock);
+        const uint32_t dsbase = base + AbSmem::kDS + static_cast<uint32_t>(st * kAbBlock);
+        const uint64_t ddo_mn = make_sw128_desc(dobase, kAbAtom, 1024u);
+        const uint64_t dq_mn = make_sw128_desc(qbase, kAbAtom, 1024u);
+        const uint64_t dds_k = make_sw128_desc(dsbase, 16u, 1024u);
+        const uint64_t dds_mn = make_sw128_desc(dsbase, kAbBlock, 1024u);
+        // dV += P^T dO: A = P^T from TMEM (16 queries per step: half kk >> 1 of the
+        // block, 8 packed columns in), B = dO as MN-major (d contiguous, the two
+        // 64-wide d atoms 8 KB apart, 16 query rows per step)
 #pragma unroll
-        for (int kk = 0; kk < kAttD / kUmmaK; ++kk) {
-          const uint32_t atom = static_cast<uint32_t>((kk >> 2) * kAttAtom + (kk & 3) * 32);
-          tc_mma_f16(t_s, make_sw128_desc(kbase + atom, 16u, 1024u), make_sw128_desc(qbase + atom, 16u, 1024u),
-                     idesc_kk, kk > 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kAbBQ / kUmmaK; ++kk)
+          tc_mma_f16_ts(t_dv, t_stage(st) + static_cast<uint32_t>((kk >> 1) * 32 + (kk & 1) * 8), ddo_mn + kk * 2048 / 16,
+                        idesc_kv, (ii > 0 || kk > 0) ? 1u : 0u);
+        // dK += dS^T Q: A = dS as K-major (keys are rows, queries contiguous), B = Q as MN-major
 #pragma unroll
-        for (int kk = 0; kk < kAttD / kUmmaK; ++kk) {
-          const uint32_t atom = static_cast<uint32_t>((kk >> 2) * kAttAtom + (kk & 3) * 32);
-          tc_mma_f16(t_dp, make_sw128_desc(vbase + atom, 16u, 1024u), make_sw128_desc(dobase + atom, 16u, 1024u),
-                     idesc_kk, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(s_full);
-        // dV += P^T dO: A = P^T from TMEM (16 queries per step), B = dO as MN-major
-        // (d contiguous, 64-wide d blocks 16 KB apart, 16 query rows per step)
-        if (!(ok = mbar_poll(p_ready, par, err, kDevErrTimeoutFull))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kAttBQ / kUmmaK; ++kk)
-          tc_mma_f16_ts(t_dv, t_s + static_cast<uint32_t>((kk >> 2) * 64 + (kk & 3) * 8),
-                        make_sw128_desc(dobase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u), idesc_km,
-                        (ii > 0 || kk > 0) ? 1u : 0u);
-        // dK += dS^T Q, and this tile's dQ^T = K^T dS^T into S^T's columns (after
-        // the dV MMA read P^T there: one thread's MMAs run in order); A = K as
-        // MN-major (d contiguous), B = dS as MN-major (queries contiguous)
-        if (!(ok = mbar_poll(ds_ready, par, err, kDevErrTimeoutFull))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kAttBQ / kUmmaK; ++kk)
-          tc_mma_f16_ts(t_dk, t_dp + static_cast<uint32_t>((kk >> 2) * 64 + (kk & 3) * 8),
-                        make_sw128_desc(qbase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u), idesc_km,
-                        (ii > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kAbBQ / kUmmaK; ++kk)
+          tc_mma_f16(t_dk, dds_k + kk * 32 / 16, dq_mn + kk * 2048 / 16, idesc_kv, (ii > 0 || kk > 0) ? 1u : 0u);
+        // dQ^T = K^T dS^T over the stage's dP^T columns (read into registers before
+        // pds_ready): A = K as MN-major (d contiguous, the two d atoms 16 KB apart),
+        // B = dS as MN-major (queries contiguous), 16 keys per step
 #pragma unroll
         for (int kk = 0; kk < kAttBK / kUmmaK; ++kk)
-          tc_mma_f16(t_s, make_sw128_desc(kbase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u),
-                     make_sw128_desc(dsbase + static_cast<uint32_t>(kk * 2048), 16384u, 1024u), idesc_mm,
-                     kk > 0 ? 1u : 0u);
-        tc_commit(dq_full);
+          tc_mma_f16(t_stage(st) + 64u, dk_mn + kk * 2048 / 16, dds_mn + kk * 2048 / 16, idesc_q, kk > 0 ? 1u : 0u);
+        tc_commit(dq_full(st));
         tc_commit(qd_empty(s));
+        // block ii + 2 into this stage: S^T right behind the dV MMA that read P^T
+        // from those columns (one thread's MMAs run in order), dP^T once this
+        // block's dQ^T has been read out
+        if (ii + 2 < n_i) {
+          if (!(ok = issue_s(ii + 2))) break;
+          if (!(ok = mbar_poll(dq_free(st), static_cast<uint32_t>((ii >> 1) & 1), err, kDevErrTimeoutTmemEmpty))) break;
+          tc_fence_after();
+          issue_dp(ii + 2);
+        }
       }
       if (ok) tc_commit(dkv_done);
     }
   }
-  } else {
+  } else if (warp < 12) {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAbComputeRegs));
     const int quad = warp & 3;          // TMEM lane quarter
-    const int hh = (warp - 4) >> 2;     // column half: queries (and d) 64 hh .. 64 hh + 63
-    const int kr = quad * 32 + lane;    // key row of the tile
+    const int hh = (warp - 4) >> 2;     // half of the block's queries: 32 hh .. 32 hh + 31
+    const int kr = quad * 32 + lane;    // key row of the tile (and d of the dQ^T lanes)
     const int key = j * kAttBK + kr;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const float sc = p.scale_log2;
-    const uint32_t ds_row = base + AbSmem::kDS + static_cast<uint32_t>(hh * kAttAtom + kr * 128);
     bool ok = true;
     for (int ii = 0; ii < n_i; ++ii) {
-      const uint32_t par = static_cast<uint32_t>(ii & 1);
-      const int q0 = (j + ii) * kAttBQ + 64 * hh;  // first query of this warp's columns
-      if (!warp_poll(s_full, par, err, kDevErrTimeoutTmemFull, lane)) {
+      const int st = ii & 1;
+      const uint32_t par = static_cast<uint32_t>((ii >> 1) & 1);
+      const int q0 = (qb0 + ii) * kAbBQ + 32 * hh;  // first query of this warp's columns
+      // S^T, dP^T in TMEM; L, D of the block in its Q / dO stage (that TMA phase
+      // completed before the MMA thread issued S^T)
+      if (!warp_wait(s_full(st), par, err, kDevErrTimeoutTmemFull, lane) ||
+          !warp_wait(qd_full(ii % kAbStages), static_cast<uint32_t>((ii / kAbStages) & 1), err, kDevErrTimeoutFull,
+                     lane)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sx[2][32], dpx[2][32];
-      tmem_ld_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh), sx[0]);
-      tmem_ld_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh + 32), sx[1]);
-      tmem_ld_32x32b_x32(t_dp + lane_off + static_cast<uint32_t>(64 * hh), dpx[0]);
-      tmem_ld_32x32b_x32(t_dp + lane_off + static_cast<uint32_t>(64 * hh + 32), dpx[1]);
+      uint32_t sx[32], dpx[32];
+      tmem_ld_32x32b_x32(t_stage(st) + lane_off + static_cast<uint32_t>(32 * hh), sx);
+      tmem_ld_32x32b_x32(t_stage(st) + lane_off + static_cast<uint32_t>(64 + 32 * hh), dpx);
       tmem_ld_wait();
-      // P^T and dS^T for queries q0 .. q0 + 63 (masked pairs give 0; only the
-      // diagonal tile and the tiles the window edge crosses hold any)
-      uint32_t pk[32], dk2[32];
-      const int64_t stat = static_cast<int64_t>(bh) * p.T + q0;
-      if (ii == 0 || kAttBQ * ii + kAttBQ - 1 >= p.window)
-        ab_p_ds<true>(sx, dpx, pk, dk2, p.lse2 + stat, p.Dv + stat, q0 - key, p.window, sc);
+      // P^T and dS^T for queries q0 .. q0 + 31 (masked pairs give 0; only the two
+      // diagonal blocks and the blocks the window edge crosses hold any)
+      uint32_t pk[16], dk2[16];
+      const uint32_t stats =
+          base + AbSmem::kStats + static_cast<uint32_t>((ii % kAbStages) * AbSmem::kStatBytes + 32 * hh * 4);
+      if (ii < kAttBK / kAbBQ || (qb0 + ii) * kAbBQ + kAbBQ - 1 - j * kAttBK >= p.window)
+        ab_p_ds<true>(sx, dpx, pk, dk2, stats, stats + kAbBQ * 4, q0 - key, p.window, sc);
       else
-        ab_p_ds<false>(sx, dpx, pk, dk2, p.lse2 + stat, p.Dv + stat, q0 - key, p.window, sc);
-      // P^T (query pairs) over the first 32 of the 64 S^T columns this warp read (the
-      // other warp of the lane quarter reads the other 64): the dV MMA may start
-      tmem_st_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh), pk);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready);
-      // dS^T over dP^T's columns, and dS into shared memory (the dQ MMA's A operand,
-      // queries contiguous: this row of 64 queries, 128-byte swizzled); the previous
-      // tile's dQ MMA, which read it, completed before this tile's S did
-      tmem_st_32x32b_x32(t_dp + lane_off + static_cast<uint32_t>(64 * hh), dk2);
+        ab_p_ds<false>(sx, dpx, pk, dk2, stats, stats + kAbBQ * 4, q0 - key, p.window, sc);
+      // P^T pairs over the first 16 of the 32 S^T columns this warp read (the other
+      // warp of the lane quarter reads the other 32); dS into this stage's shared
+      // buffer (row = key, 64 queries, 128-byte swizzle; this warp's 32 queries are
+      // 16-byte chunks 4 hh .. 4 hh + 3), which the block two before released (its
+      // dK and dQ^T MMAs completed before this block's dP^T was issued)
+      tmem_st_32x32b_x16(t_stage(st) + lane_off + static_cast<uint32_t>(32 * hh), pk);
+      const uint32_t ds_row = base + AbSmem::kDS + static_cast<uint32_t>(st * kAbBlock + kr * 128);
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        st_shared_v4(ds_row + static_cast<uint32_t>((c ^ (kr & 7)) << 4),
+      for (int c = 0; c < 4; ++c)
+        st_shared_v4(ds_row + static_cast<uint32_t>(((4 * hh + c) ^ (kr & 7)) << 4),
                      make_uint4(dk2[4 * c], dk2[4 * c + 1], dk2[4 * c + 2], dk2[4 * c + 3]));
       fence_proxy_async_smem();
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(ds_ready);
-      // this tile's dQ^T (TMEM lanes = d 32 quad .., columns = queries 64 hh ..) into
-      // the fp32 accumulator: each warp instruction adds one query's 32 d, a
-      // contiguous 128-byte line
-      if (!warp_poll(dq_full, par, err, kDevErrTimeoutTmemFull, lane)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t dq[2][32];
-      tmem_ld_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh), dq[0]);
-      tmem_ld_32x32b_x32(t_s + lane_off + static_cast<uint32_t>(64 * hh + 32), dq[1]);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
-      float* dst = p.dq_acc + (static_cast<int64_t>(b * p.T + q0) * p.H + h) * kAttD + quad * 32 + lane;
-      const int64_t qstride = static_cast<int64_t>(p.H) * kAttD;
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          asm volatile("red.global.add.f32 [%0], %1;" ::"l"(dst + (32 * c + i) * qstride), "f"(__uint_as_float(dq[c][i]))
-                       : "memory");
+      if (lane == 0) mbar_arrive(pds_ready(st));
     }
     // dK (scaled) and dV of this key tile: TMEM lanes = keys, columns = d 64 hh ..
-    if (ok && warp_poll(dkv_done, 0u, err, kDevErrTimeoutTmemFull, lane)) {
+    if (ok && warp_wait(dkv_done, 0u, err, kDevErrTimeoutTmemFull, lane)) {
       tc_fence_after();
       const int64_t o = (static_cast<int64_t>(b * p.T + key) * p.H + h) * kAttD + 64 * hh;
 #pragma unroll
@@ -952,6 +987,27 @@ __global__ void __launch_bounds__(kAbThreads, 1)
                                     pack_bf16x2(__uint_as_float(x[c][i + 4]) * f, __uint_as_float(x[c][i + 5]) * f),
                                     pack_bf16x2(__uint_as_float(x[c][i + 6]) * f, __uint_as_float(x[c][i + 7]) * f)));
       }
+    }
+  } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAbReduceRegs));
+    // each block's dQ^T: TMEM lanes = d 32 quad .., dP^T columns = its 64 queries
+    const int quad = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const int64_t qstride = static_cast<int64_t>(p.H) * kAttD;
+    for (int ii = 0; ii < n_i; ++ii) {
+      const int st = ii & 1;
+      if (!warp_wait(dq_full(st), static_cast<uint32_t>((ii >> 1) & 1), err, kDevErrTimeoutTmemFull, lane)) break;
+      tc_fence_after();
+      uint32_t dq[2][32];
+      tmem_ld_32x32b_x32(t_stage(st) + lane_off + 64u, dq[0]);
+      tmem_ld_32x32b_x32(t_stage(st) + lane_off + 96u, dq[1]);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free(st));
+      float* dst = p.dq_acc + (static_cast<int64_t>(b * p.T + (qb0 + ii) * kAbBQ) * p.H + h) * kAttD + quad * 32 + lane;
+      ab_dq_reduce(dst, qstride, dq[0]);
+      ab_dq_reduce(dst + 32 * qstride, qstride, dq[1]);
     }
   }
 
@@ -1049,15 +1105,14 @@ extern "C" int hlm_attention_bwd(const void* grad_out, const void* q, const void
   if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
   CUtensorMap mq, mk, mv, mdo;
   const int64_t rows = B * T;
-  if (!encode_bf16_map(&mq, q, H * D, rows, H * D, 128) || !encode_bf16_map(&mk, k, H * D, rows, H * D, 128) ||
-      !encode_bf16_map(&mv, v, H * D, rows, H * D, 128) || !encode_bf16_map(&mdo, grad_out, H * D, rows, H * D, 128))
+  if (!encode_bf16_map(&mq, q, H * D, rows, H * D, kAbBQ) || !encode_bf16_map(&mk, k, H * D, rows, H * D, 128) ||
+      !encode_bf16_map(&mv, v, H * D, rows, H * D, 128) || !encode_bf16_map(&mdo, grad_out, H * D, rows, H * D, kAbBQ))
     return HLM_ERR_DRIVER;
   AbParams p;
   p.B = static_cast<int>(B);
   p.T = static_cast<int>(T);
   p.H = static_cast<int>(H);
   p.window = window <= 0 || window >= T ? static_cast<int>(T) : static_cast<int>(window);
-  p.k_tiles = static_cast<int>(T / kAttBK);
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.lse2 = lse2;
@@ -1075,7 +1130,7 @@ extern "C" int hlm_attention_bwd(const void* grad_out, const void* q, const void
     cudaFuncAttributes attr{};
     return cudaFuncGetAttributes(&attr, attn_bwd_kernel) == cudaSuccess ? attr.numRegs : -1;
   }();
-  if (compiled_regs != kAttLaunchRegs) return HLM_ERR_UNSUPPORTED;
+  if (compiled_regs != kAbLaunchRegs) return HLM_ERR_UNSUPPORTED;
   {
     LaunchScope scope(HLM_KERNEL_ATTN_BWD, s);
     attn_bwd_kernel<<<static_cast<unsigned>(B * H * (T / kAttBK)), kAbThreads, smem, s>>>(mq, mk, mv, mdo, p);

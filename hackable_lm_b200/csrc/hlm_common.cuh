@@ -275,6 +275,14 @@ HLM_DEVICE void bulk_wait_group_read() {
 // Wait until every committed bulk group has fully completed.
 HLM_DEVICE void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Plain (untiled) bulk copy global -> this CTA's shared memory, completing on
+// mbarrier bar; addresses 16-byte aligned, bytes a multiple of 16.
+HLM_DEVICE void bulk_load_1d(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 HLM_DEVICE uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
