@@ -720,6 +720,34 @@ def bench_ops(device, iters: int = 20, only: str | None = None) -> dict:
         res[key] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1), "flop": flop,
                     "frac_of_bf16": round(tf / peaks["bf16_tflops"], 4), "sdpa_us": round(ms_ref * 1e3, 2)}
         del qa, ka, va
+    # attention backward (tcgen05 kernel) at the d12 shape with the reference's 512-key window
+    # (where it runs) and full causal, beside the library backward on the same inputs
+    # (flash_attn's windowed backward; cuDNN's SDPA backward): 10*D FLOPs per unmasked
+    # (query, key) pair (S, dP, dV, dK, dQ)
+    key = "attention_bwd [16,2048,6,128] window 512"
+    if want(key):
+        qa, ka, va, ga = (torch.randn(16, 2048, 6, 128, generator=g).to(torch.bfloat16).to(device) for _ in range(4))
+        sc = 128 ** -0.5
+        entry = {}
+        old = ops.ATTENTION_BWD["mode"]
+        try:
+            for w, tag in ((512, ""), (0, "causal_")):
+                oa, la = ops.attention(qa, ka, va, w, sc)
+                for mode, name in (("native", "us"), ("library", "library_us")):
+                    ops.ATTENTION_BWD["mode"] = mode
+                    ms = timed(lambda a, b, c, d_, o=oa, l=la, w=w: ops.attention_backward(d_, a, b, c, o, l, w, sc),
+                               (qa, ka, va, ga), nbytes_of((qa, ka, va, ga)))
+                    entry[tag + name] = round(ms * 1e3, 2)
+                del oa, la
+        finally:
+            ops.ATTENTION_BWD["mode"] = old
+        pairs = 512 * 513 // 2 + (2048 - 512) * 512
+        flop = 10 * 128 * pairs * 16 * 6
+        tf = flop / (entry["us"] / 1e6) / 1e12
+        res[key] = {"us": entry["us"], "TFLOP/s": round(tf, 1), "flop": flop,
+                    "frac_of_bf16": round(tf / peaks["bf16_tflops"], 4), "flash_attn_us": entry["library_us"],
+                    "causal_us": entry["causal_us"], "causal_cudnn_us": entry["causal_library_us"]}
+        del qa, ka, va, ga
     if not want("qkv_rope_bwd"):
         return res
     qo, ko, vo, rs = ops.qkv_rope(xq, wq, c1, s1, 6, 6, 1e-6)

@@ -642,18 +642,20 @@ struct AbParams {
   int* err;
 };
 
-// D[b, h, t] = sum_d dO[b,t,h,d] O[b,t,h,d] and L[b, h, t] = lse[b, h, t] log2 e:
-// one warp per (b, t, h) row.
+// D[b, h, t] = sum_d dO[b,t,h,d] O[b,t,h,d] and L[b, h, t] = lse[b, h, t] log2 e,
+// and the row of the fp32 dq accumulator zeroed: one warp per (b, t, h) row.
 __global__ void __launch_bounds__(256) attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ dout,
                                                             const __nv_bfloat16* __restrict__ out,
                                                             const float* __restrict__ lse, float* __restrict__ Dv,
-                                                            float* __restrict__ lse2, int B, int T, int H) {
+                                                            float* __restrict__ lse2, float* __restrict__ dq_acc, int B,
+                                                            int T, int H) {
   const int lane = threadIdx.x & 31;
   const int64_t rows = static_cast<int64_t>(B) * T * H;
   for (int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; row < rows;
        row += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
     const uint2 a = *reinterpret_cast<const uint2*>(dout + row * kAttD + 4 * lane);
     const uint2 o = *reinterpret_cast<const uint2*>(out + row * kAttD + 4 * lane);
+    reinterpret_cast<float4*>(dq_acc + row * kAttD)[lane] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float acc = bf16_lo(a.x) * bf16_lo(o.x) + bf16_hi(a.x) * bf16_hi(o.x) + bf16_lo(a.y) * bf16_lo(o.y) +
                 bf16_hi(a.y) * bf16_hi(o.y);
     acc = warp_sum(acc);
@@ -1092,14 +1094,14 @@ extern "C" int hlm_attention_bwd(const void* grad_out, const void* q, const void
   float* lse2 = Dv + B * H * T;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int sms = num_sms_of_current_device();
-  if (cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(B * T * H * D) * 4, s) != cudaSuccess) return HLM_ERR_LAUNCH;
   {
     const int64_t rows = B * T * H;
     int64_t blocks = (rows * 32 + 255) / 256;
     if (blocks > static_cast<int64_t>(sms) * 8) blocks = static_cast<int64_t>(sms) * 8;
     LaunchScope scope(HLM_KERNEL_ATTN_BWD, s);
     attn_bwd_prep_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(grad_out), static_cast<const __nv_bfloat16*>(out), lse, Dv, lse2, static_cast<int>(B),
+        static_cast<const __nv_bfloat16*>(grad_out), static_cast<const __nv_bfloat16*>(out), lse, Dv, lse2, dq_acc,
+        static_cast<int>(B),
         static_cast<int>(T), static_cast<int>(H));
   }
   if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
