@@ -772,8 +772,8 @@ _FLASH_BWD = []
 
 # Which backward attention_backward runs: "native" (hlm_attention_bwd, this
 # library's tcgen05 kernel), "library" (cuDNN / flash_attn), or "auto": native for
-# a sliding window (measured at [16, 2048, 6, 128], window 512: 447 us vs 539 us for
-# flash_attn's windowed backward), cuDNN for full causal attention (335 us vs 745 us).
+# a sliding window (measured at [16, 2048, 6, 128], window 512: 311 us vs 540 us for
+# flash_attn's windowed backward), cuDNN for full causal attention (335 us vs 455 us).
 ATTENTION_BWD = {"mode": "auto"}
 
 
@@ -818,7 +818,7 @@ def attention_backward(grad_out: torch.Tensor, q: torch.Tensor, k: torch.Tensor,
     and faster there today); ATTENTION_BWD selects.  Without the native kernel (grouped
     heads, or mode "library") a window goes to flash_attn's windowed backward, or to
     cuDNN with the window as a dense T x T bias when flash_attn is not installed
-    (measured at [16, 2048, 6, 128], window 512: native 0.45 ms, flash_attn 0.54 ms,
+    (measured at [16, 2048, 6, 128], window 512: native 0.31 ms, flash_attn 0.54 ms,
     cuDNN with the bias 1.3 ms)."""
     _require_cuda(grad_out, q, k, v, out, lse)
     B, T, H, D = q.shape
