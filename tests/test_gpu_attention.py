@@ -217,3 +217,35 @@ def test_attention_native_backward_vs_reference(B, T, H, window, cuda_device):
     for name, a, e, s in zip("qkv", (dq, dk, dv), (qr.grad, kr.grad, vr.grad), _sdpa_grads(q, k, v, go, window)):
         sdpa_err = _rel_l2(s, e)
         assert _rel_l2(a, e) <= 2 * sdpa_err + 1e-3, (name, _rel_l2(a, e), sdpa_err)
+
+
+def test_attention_native_backward_argument_checks(cuda_device):
+    """hlm_attention_bwd refuses what it does not handle before any launch: grouped
+    heads, head_dim other than 128, T not a multiple of 128 (HLM_ERR_UNSUPPORTED), a
+    workspace below hlm_attention_bwd_workspace_bytes or a null pointer
+    (HLM_ERR_INVALID_ARG); B == 0 is a no-op."""
+    from hackable_lm_b200 import _lib
+
+    lib = _lib.load()
+    B, T, H = 1, 256, 2
+    t = torch.zeros(B, T, H, 128, dtype=torch.bfloat16, device=cuda_device)
+    lse = torch.zeros(B, H, T, dtype=torch.float32, device=cuda_device)
+    need = int(lib.hlm_attention_bwd_workspace_bytes(B, T, H, 128))
+    assert need == B * T * H * 128 * 4 + B * H * T * 8 + 256
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda_device)
+    outs = [torch.empty_like(t) for _ in range(3)]
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+
+    def call(nbytes=need, B_=B, T_=T, Hk=H, D=128, ws_ptr=ws.data_ptr()):
+        return lib.hlm_attention_bwd(t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(),
+                                     lse.data_ptr(), *(o.data_ptr() for o in outs), ws_ptr, nbytes, B_, T_, H, Hk, D,
+                                     0, 0.088, stream)
+
+    assert call(Hk=1) == -2
+    assert call(D=64) == -2
+    assert call(T_=200) == -2
+    assert call(nbytes=need - 16) == -1
+    assert call(ws_ptr=0) == -1
+    assert call(B_=0) == 0
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
