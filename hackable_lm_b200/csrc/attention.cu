@@ -580,7 +580,11 @@ __global__ void __launch_bounds__(kAttThreads, 1)
 //   dV += P^T dO,   dK += scale dS^T Q,   dQ^T += scale K^T dS^T  (attn_bwd_kernel)
 // One CTA per (b, h, key tile j of 128 keys) walks the 64-query blocks the window
 // reaches from tile j.  Tensor memory: two stages of [S^T | dP^T] (64 + 64
-// columns each), dV (256-383) and dK (384-511).  Per block:
+// columns each), dV (256-383) and dK (384-511); the 64-query blocks are what lets
+// two stages fit (an M = 128 tcgen05.mma costs about the same at N = 64 as at
+// N = 128, but a single stage of 128-query tiles serialises the MMAs with the
+// softmax-like P / dS work and measured slower).  The prep kernel also zeroes the
+// dq accumulator.  Per block:
 //   MMA   S^T, dP^T into the block's stage (issued two blocks ahead: S^T right
 //         after the dV MMA of the block before in that stage, dP^T once that
 //         block's dQ^T has been read out);
