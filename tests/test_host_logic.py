@@ -78,3 +78,23 @@ def test_fake_implementations_shapes():
         assert loss.shape == () and gx.shape == h.shape and gw.shape == W.shape
         out, norm = ops.residual_rms_norm(x, x, None, 1e-6)
         assert out.shape == norm.shape == x.shape
+
+
+def test_attention_backward_selection():
+    """The backward attention_backward runs: the tcgen05 kernel for a sliding window
+    shorter than the sequence with equal q / kv heads, the library backward for full
+    causal attention and grouped heads; ATTENTION_BWD overrides (never to the native
+    kernel for grouped heads, which it does not handle)."""
+    sel = ops._native_attention_bwd
+    old = ops.ATTENTION_BWD["mode"]
+    try:
+        ops.ATTENTION_BWD["mode"] = "auto"
+        assert sel(512, 2048, 6, 6) and sel(1, 128, 2, 2)
+        assert not sel(0, 2048, 6, 6) and not sel(2048, 2048, 6, 6) and not sel(4096, 2048, 6, 6)
+        assert not sel(512, 2048, 6, 2)
+        ops.ATTENTION_BWD["mode"] = "native"
+        assert sel(0, 2048, 6, 6) and not sel(512, 2048, 6, 3)
+        ops.ATTENTION_BWD["mode"] = "library"
+        assert not sel(512, 2048, 6, 6)
+    finally:
+        ops.ATTENTION_BWD["mode"] = old
