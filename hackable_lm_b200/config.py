@@ -16,9 +16,10 @@ from typing import Any
 # B200 kernels unchanged; it resolves to "b200".
 MODULE_BACKENDS = {"torch", "triton", "b200"}
 # "sdpa" is this path's attention core (torch SDPA); "b200" the tcgen05 forward
-# (hlm_attention_fwd) with cuDNN's backward; the reference's names (config.py:11)
-# are accepted too and run on SDPA, so reference configs and their default
-# "flash_attn_2" select it unchanged.
+# (hlm_attention_fwd) with the tcgen05 backward for sliding windows and cuDNN's
+# for full causal attention; the reference's names (config.py:11) are accepted too
+# and run on SDPA (sliding-window layers on the tcgen05 kernels), so reference
+# configs and their default "flash_attn_2" select it unchanged.
 ATTENTION_BACKENDS = {"torch", "sdpa", "b200", "flex_attention", "flash_attn_2", "flash_attn_3", "flash_attn_4"}
 MODULE_BACKEND_FIELDS = (
     "qkv_backend",

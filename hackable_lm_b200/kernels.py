@@ -301,8 +301,9 @@ def sliding_window_b200(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, windo
 
 def attention_b200(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, window_size: int | None) -> torch.Tensor:
     """Causal attention on [B, T, H, 128] bf16 q, k, v (the QKV kernel's layout, no
-    transposes): the tcgen05 forward of hlm_attention_fwd, gradients through a library
-    backward (cuDNN's SDPA backward; flash_attn's for a sliding window).
+    transposes): the tcgen05 forward of hlm_attention_fwd; gradients through the tcgen05
+    backward (hlm_attention_bwd) for a sliding window and cuDNN's SDPA backward for full
+    causal attention (ops.attention_backward).
     ``window_size`` keys per query (the FlashAttention window ``(window_size - 1, 0)``,
     kernels.py:839) or None for full causal."""
     _cuda_only(q, "attention_b200")
