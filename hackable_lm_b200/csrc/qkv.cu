@@ -393,6 +393,21 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
   }
   const int seg1 = static_cast<int>(Hq * kQkvD);
   const int seg2 = static_cast<int>((Hq + Hk) * kQkvD);
+  // grad_w (step 3) runs on the library's side stream, forked here and joined at the
+  // end, so that its CTAs take the SMs grad_x's last wave leaves idle (the two GEMMs
+  // are independent; each holds one CTA per SM)
+  SideStream* side = nullptr;
+  std::unique_lock<std::mutex> side_lock;
+  cudaStream_t sw = s;
+  if (grad_x != nullptr && grad_w != nullptr) {
+    side = side_stream_of_current_device();
+    if (side == nullptr) return HLM_ERR_LAUNCH;
+    side_lock = std::unique_lock<std::mutex>(side->mu);
+    if (cudaEventRecord(side->ev_start, s) != cudaSuccess ||
+        cudaStreamWaitEvent(side->stream, side->ev_start, 0) != cudaSuccess)
+      return HLM_ERR_LAUNCH;
+    sw = side->stream;
+  }
   // 2. grad_x = [dq|dk|dv] @ W_qkv
   if (grad_x != nullptr) {
     CUtensorMap a0, a1, a2, mb;
@@ -435,7 +450,7 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
     p.err = err;
     // the splits add into one fp32 dW (zeroed first), then one pass rounds it to bf16
     const int64_t n = nqkv * C;
-    if (cudaMemsetAsync(slabs, 0, static_cast<size_t>(n) * sizeof(float), s) != cudaSuccess)
+    if (cudaMemsetAsync(slabs, 0, static_cast<size_t>(n) * sizeof(float), sw) != cudaSuccess)
       return HLM_ERR_LAUNCH;
     EpiStore::Params ep;
     ep.d = slabs;
@@ -445,7 +460,7 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
     ep.accumulate = 2;
     ep.vec_ok = 1;
     ep.alpha = nullptr;
-    const int rc = launch_gemm_pair<kDwBN, kQkvStages, true, true, EpiStore>(a0, a1, a2, mb, p, ep, s,
+    const int rc = launch_gemm_pair<kDwBN, kQkvStages, true, true, EpiStore>(a0, a1, a2, mb, p, ep, sw,
                                                                             HLM_KERNEL_QKV_DW);
     if (rc != HLM_OK) return rc;
     int64_t blocks = (n / 4 + 255) / 256;
@@ -453,11 +468,14 @@ extern "C" int hlm_qkv_rope_bwd(const void* x, const void* w_qkv, const void* q_
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     {
-      LaunchScope scope(0, s);
-      splitk_reduce_bf16_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
+      LaunchScope scope(0, sw);
+      splitk_reduce_bf16_kernel<<<static_cast<int>(blocks), 256, 0, sw>>>(
           slabs, 1, n, static_cast<__nv_bfloat16*>(grad_w));
     }
     if (launch_status() != HLM_OK) return HLM_ERR_LAUNCH;
   }
+  if (side != nullptr && (cudaEventRecord(side->ev_done[0], side->stream) != cudaSuccess ||
+                          cudaStreamWaitEvent(s, side->ev_done[0], 0) != cudaSuccess))
+    return HLM_ERR_LAUNCH;
   return HLM_OK;
 }
