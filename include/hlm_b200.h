@@ -240,7 +240,9 @@ int hlm_qkv_rope_fwd(const void* x, const void* w_qkv, const void* cos, const vo
  * grad_q/grad_k (contiguous [B,T,H,D] bf16), then computes on the tensor
  * cores grad_x = [dq|dk|dv] @ w_qkv and grad_w = [dq|dk|dv]^T @ x.
  * grad_x or grad_w may be NULL (not needed).  Workspace bytes from
- * hlm_qkv_rope_bwd_workspace_bytes.
+ * hlm_qkv_rope_bwd_workspace_bytes.  With both requested, grad_w runs on the
+ * library's per-device side stream beside grad_x, forked from `stream` and
+ * joined back into it before the call returns (stream-ordered, capturable).
  * Replaces the autograd backward of QKVProjection.fwd_triton: view/split
  * backward + _qk_norm_rope_backward (kernels.py:711-735) + the qkv_proj
  * nn.Linear dgrad/wgrad. */
